@@ -1,0 +1,118 @@
+/*
+ * tila_b200.h - C ABI of the B200 (sm_100a) execution backend for Tila's typed TIR.
+ *
+ * The reference executes a checked kernel through Triton: runtime.py builds
+ * Triton source (lowering.py:136-182), compiles it in backend.preflight
+ * (backend.py:61-88) and launches it with `kern[grid](*args, num_warps=...)`
+ * (runtime.py:1107).  This library is the native replacement for those three
+ * steps.  Python reaches it through ctypes; nothing here takes torch types:
+ * device buffers are plain device addresses, streams are CUstream handles cast
+ * to uint64_t.
+ *
+ * Every function returns 0 (TILA_OK) or a negative status code.  The Python
+ * host maps the codes onto Tila's diagnostics (TILA-TARGET-010 compile/load,
+ * TILA-TARGET-011 resources; backend.py:30-58).  No function aborts the process.
+ */
+#ifndef TILA_B200_H
+#define TILA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TILA_OK = 0,
+  TILA_ERR_DRIVER_MISSING = -1,  /* libcuda.so.1 could not be opened (no GPU driver) */
+  TILA_ERR_DRIVER = -2,          /* a CUDA driver call failed; message in the log buffer */
+  TILA_ERR_COMPILE = -3,         /* NVRTC rejected the generated source */
+  TILA_ERR_LOAD = -4,            /* the cubin could not be loaded */
+  TILA_ERR_RESOURCES = -5,       /* launch exceeds a device limit (smem, threads) */
+  TILA_ERR_ARGUMENT = -6,        /* invalid argument to this ABI */
+  TILA_ERR_NO_CONTEXT = -7       /* no current CUDA context on the calling thread */
+};
+
+/* Launch geometry.  grid/block/cluster as in cuLaunchKernelEx; cluster all
+ * ones (or zeros) means no cluster.  stream is a CUstream (0 = legacy). */
+typedef struct tila_launch_config {
+  uint32_t grid[3];
+  uint32_t block[3];
+  uint32_t cluster[3];
+  uint32_t smem_bytes;
+  uint64_t stream;
+} tila_launch_config;
+
+/* Compiled resource usage of one kernel (backend.py:77-86 reports the same
+ * quantities for Triton kernels). */
+typedef struct tila_kernel_attrs {
+  int32_t registers_per_thread;
+  int32_t static_smem_bytes;
+  int32_t local_bytes_per_thread; /* > 0 means register spills */
+  int32_t max_threads_per_block;
+  int32_t max_dynamic_smem_bytes; /* device opt-in limit */
+  int32_t binary_version;
+} tila_kernel_attrs;
+
+/* Replaces: Triton compile inside backend.preflight (backend.py:65-66).
+ * Compiles CUDA C++ source with NVRTC for sm_100a.  On success *cubin_out
+ * receives a malloc'ed buffer (release with tila_free_buffer).  The compiler
+ * log (warnings or errors) is copied into log (NUL-terminated, truncated to
+ * log_cap).  Works without a GPU. */
+int tila_nvrtc_compile(const char *source, const char *program_name,
+                       const char *const *options, int num_options,
+                       void **cubin_out, size_t *cubin_size,
+                       char *log, size_t log_cap);
+
+/* NVRTC version, e.g. 12090 for 12.9 (part of the compile cache key). */
+int tila_nvrtc_version(int *version_out);
+
+void tila_free_buffer(void *buffer);
+
+/* Loads libcuda.so.1 and calls cuInit.  Idempotent.  Fails with
+ * TILA_ERR_DRIVER_MISSING on a machine without the NVIDIA driver. */
+int tila_init(char *log, size_t log_cap);
+
+/* Replaces: compiled._init_handles() (backend.py:78).  Loads a cubin as a
+ * context-independent CUlibrary, usable on every device of the process. */
+int tila_library_load(const void *cubin, size_t size, void **library_out,
+                      char *log, size_t log_cap);
+int tila_library_unload(void *library);
+
+/* Looks up an extern "C" __global__ function of a loaded library. */
+int tila_kernel_get(void *library, const char *name, void **kernel_out,
+                    char *log, size_t log_cap);
+
+/* Replaces: the shared-memory / thread checks of backend.preflight
+ * (backend.py:71-82).  Reports usage on the current device. */
+int tila_kernel_attrs_get(void *kernel, tila_kernel_attrs *out, char *log,
+                          size_t log_cap);
+
+/* Replaces: kern[grid](*args, num_warps=...) (runtime.py:1107).  args is the
+ * usual cuLaunchKernel parameter array: args[i] points at the value of
+ * kernel parameter i.  Raises the kernel's dynamic shared memory limit when
+ * cfg->smem_bytes needs it.  Asynchronous on cfg->stream. */
+int tila_launch(void *kernel, const tila_launch_config *cfg, void **args,
+                char *log, size_t log_cap);
+
+/* Builds a CUtensorMap (128 bytes, 64-byte aligned) for a TMA tile copy.
+ * dtype uses CUtensorMapDataType numbering; dims/strides are innermost first,
+ * strides in bytes for dims 1..rank-1; box in elements; swizzle uses
+ * CUtensorMapSwizzle numbering.  Out-of-bounds elements read as zero. */
+int tila_encode_tensor_map(void *tensor_map_out, int dtype, int rank,
+                           uint64_t global_address, const uint64_t *dims,
+                           const uint64_t *strides_bytes, const uint32_t *box,
+                           int swizzle, char *log, size_t log_cap);
+
+/* Number of SMs and opt-in shared memory per block of the current device. */
+int tila_device_info(int *sm_count, int *max_smem_optin, int *cc_major,
+                     int *cc_minor, char *log, size_t log_cap);
+
+const char *tila_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILA_B200_H */

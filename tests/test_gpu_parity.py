@@ -1,0 +1,154 @@
+"""GPU parity of the five workloads against Tila's interpreter (the oracle).
+
+Mirrors the reference's differential tests (tests/gpu_examples.py:19-97):
+fixed seeds, the CPU interpreter and the B200 backend run the same program on
+the same inputs.  Bars: bit-exact for add; rtol 1e-6 against the interpreter
+for softmax; relative Frobenius error <= 2e-3 for the f16-dot kernels (plus
+the K * eps_f32 elementwise bound of the reference for matmul).
+"""
+
+import numpy as np
+import pytest
+
+import tila_b200
+from tila_b200 import workloads as W
+from oracle import restate
+
+ti = tila_b200.tila
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a) if a.flags.c_contiguous else a).cuda() \
+        if a.flags.c_contiguous else torch.from_numpy(np.ascontiguousarray(a.T)).cuda().T
+
+
+def _no_device_errors():
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+
+
+def execute(kernel, grid, inputs, out_shape, *scalars, warps=4, **consts):
+    """Run on the interpreter (NumPy) and on the B200 backend (CUDA)."""
+    cpu = np.zeros(out_shape, np.float32)
+    gpu = torch.zeros(out_shape, dtype=torch.float32, device="cuda")
+    launch = kernel[grid].with_options(num_warps=warps)
+    launch(*inputs, cpu, *scalars, **consts)
+    launch(*(_cuda(x) for x in inputs), gpu, *scalars, **consts)
+    _no_device_errors()
+    return cpu, gpu.cpu().numpy()
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("n", [127, 128, 129])
+def test_add_bit_exact(n, warps):
+    rng = np.random.default_rng(301)
+    x, y = [rng.normal(size=n).astype(np.float32) for _ in range(2)]
+    cpu, gpu = execute(W.vector_add, (ti.cdiv(n, 128),), [x, y], (n,), warps=warps, BLOCK=128)
+    np.testing.assert_array_equal(cpu, x + y)
+    np.testing.assert_array_equal(gpu, cpu)
+
+
+def test_add_full_size_bit_exact():
+    x, y = W.add_inputs()
+    out = torch.zeros(x.shape, dtype=torch.float32, device="cuda")
+    W.vector_add[(ti.cdiv(x.size, 1024),)](_cuda(x), _cuda(y), out, BLOCK=1024)
+    _no_device_errors()
+    np.testing.assert_array_equal(out.cpu().numpy(), restate.vector_add(x, y))
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("n", [31, 32, 33])
+def test_softmax(n, warps):
+    x = np.random.default_rng(302).normal(size=(3, n)).astype(np.float32)
+    cpu, gpu = execute(W.row_softmax, (3,), [x], x.shape, warps=warps, BN=64)
+    ref = restate.row_softmax_f64(x)
+    np.testing.assert_allclose(gpu, ref, rtol=2e-6, atol=2e-7)
+    np.testing.assert_allclose(gpu, cpu, rtol=1e-6, atol=0)
+
+
+def test_softmax_full_size():
+    x = W.softmax_inputs()
+    out = torch.zeros(x.shape, dtype=torch.float32, device="cuda")
+    W.row_softmax[(x.shape[0],)](_cuda(x), out, BN=1024)
+    _no_device_errors()
+    got = out.cpu().numpy()
+    # the interpreter's arithmetic restated (bit-for-bit the same NumPy calls)
+    ref = restate.row_softmax_f32(x[:512], 1024)
+    np.testing.assert_allclose(got[:512], ref, rtol=1e-6, atol=0)
+    # every row sums to one (size-independent property over all rows)
+    np.testing.assert_allclose(got.astype(np.float64).sum(axis=1), 1.0, rtol=1e-5)
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("shape", [(16, 16, 16), (19, 23, 35)])
+@pytest.mark.parametrize("strided", [False, True])
+def test_matmul_small(shape, strided, warps):
+    m, n, k = shape
+    rng = np.random.default_rng(303)
+    a = rng.normal(size=(m, k)).astype(np.float16)
+    b = rng.normal(size=(k, n)).astype(np.float16)
+    if strided:
+        a = np.ascontiguousarray(a.T).T
+        b = np.ascontiguousarray(b.T).T
+    cpu, gpu = execute(W.tiled_matmul, (ti.cdiv(m, 16), ti.cdiv(n, 16)), [a, b], (m, n),
+                       warps=warps, BM=16, BN=16, BK=32)
+    ref = restate.matmul_f64(a, b)
+    bound = restate.matmul_bound(a, b)
+    assert np.all(np.abs(gpu - ref) <= bound)
+    assert restate.rel_frobenius(gpu, cpu) <= 2e-3
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 256), (300, 200, 136)])
+def test_matmul_128_tiles(shape):
+    m, n, k = shape
+    a, b = W.matmul_inputs(m, n, k, seed=7)
+    c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    W.tiled_matmul[(ti.cdiv(m, 128), ti.cdiv(n, 128))](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)
+    _no_device_errors()
+    got = c.cpu().numpy()
+    assert np.all(np.abs(got - restate.matmul_f64(a, b)) <= restate.matmul_bound(a, b))
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("n", [32, 65])
+def test_fused_attention_small(n, warps):
+    rng = np.random.default_rng(305)
+    q, k, v = [rng.normal(size=(2, n, 32)).astype(np.float16) for _ in range(3)]
+    cpu, gpu = execute(W.flash_attention, (ti.cdiv(n, 32), 2), [q, k, v], (2, n, 32),
+                       1 / np.sqrt(32), warps=warps, BM=32, BN=32, BD=32)
+    ref = restate.attention_f64(q, k, v)
+    np.testing.assert_allclose(gpu, ref, rtol=2e-3, atol=2e-3)
+    assert restate.rel_frobenius(gpu, cpu) <= 2e-3
+
+
+def test_fused_attention_128_tiles():
+    q, k, v = W.attention_inputs(2, 384, 128, seed=11)
+    o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    W.flash_attention[(ti.cdiv(384, 128), 2)](_cuda(q), _cuda(k), _cuda(v), o, 128 ** -0.5,
+                                              BM=128, BN=128, BD=128)
+    _no_device_errors()
+    assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
+
+
+@pytest.mark.parametrize("l,d,blk", [(65, 32, 32), (256, 64, 128)])
+def test_unfused_attention(l, d, blk):
+    bh = 2
+    q, k, v = W.attention_inputs(bh, l, d, seed=12)
+    scale = d ** -0.5
+    qg, kg, vg = (_cuda(t) for t in (q, k, v))
+    s = torch.zeros((bh, l, l), dtype=torch.float32, device="cuda")
+    p = torch.zeros_like(s)
+    o = torch.zeros((bh, l, d), dtype=torch.float32, device="cuda")
+    W.attention_scores[(ti.cdiv(l, blk), ti.cdiv(l, blk), bh)](qg, kg, s, scale, BM=blk, BN=blk, BD=d)
+    bn = 1 << (l - 1).bit_length()
+    W.row_softmax[(bh * l,)](s.view(bh * l, l), p.view(bh * l, l), BN=max(bn, 16))
+    W.attention_pv[(ti.cdiv(l, blk), bh)](p, vg, o, BM=blk, BN=blk, BD=d)
+    _no_device_errors()
+    ref = restate.attention_f64(q, k, v, scale)
+    assert restate.rel_frobenius(o.cpu().numpy(), ref) <= 2e-3
+    # scores against the f64 product (f16 inputs are exact in f32 products)
+    s_ref = np.asarray(q, np.float64) @ np.asarray(k, np.float64).swapaxes(-1, -2) * scale
+    assert restate.rel_frobenius(s.cpu().numpy(), s_ref) <= 1e-5

@@ -1,0 +1,309 @@
+"""Execution of checked Tila kernels on B200 (the replacement of the Triton
+branch of ``_Launcher._execute``, runtime.py:1062-1108).
+
+Per launch: derive the binding facts that specialise code generation
+(dtypes, unit last-dim strides, stride and base-address divisibility), look
+up or build the kernel (TIR -> CUDA C++ -> NVRTC cubin -> CUlibrary), check
+its resources against the device (backend.preflight, backend.py:61-88), and
+launch it on the current PyTorch stream through the C ABI.  Compile and load
+failures raise ``TILA-TARGET-010`` with a replayable artifact, resource
+overflows ``TILA-TARGET-011``, unsupported TIR ``TILA-TARGET-009``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from contextlib import contextmanager
+from dataclasses import dataclass, asdict
+
+from ._reference import tila
+from . import native
+from .codegen.emitter import BufferInfo, CodegenError, KernelEmitter
+
+TilaError = tila.errors.TilaError
+Loc = tila.errors.Loc
+_runtime = tila.runtime
+
+SCALAR_CTYPES = {
+    "bool": ctypes.c_uint8, "i8": ctypes.c_int8, "i16": ctypes.c_int16, "i32": ctypes.c_int32,
+    "i64": ctypes.c_int64, "u8": ctypes.c_uint8, "u16": ctypes.c_uint16, "u32": ctypes.c_uint32,
+    "u64": ctypes.c_uint64, "f32": ctypes.c_float, "f64": ctypes.c_double,
+}
+
+# ---------------------------------------------------------------------------
+# launch sharding (multi-GPU): a thread-local program-range restriction
+# ---------------------------------------------------------------------------
+
+_shard = threading.local()
+
+
+@contextmanager
+def program_range(axis: int, start: int, stop: int):
+    """Restrict B200 launches inside the block to programs with
+    ``start <= program_id(axis) < stop``.  Launch contracts and proofs still
+    run on the full grid, and ``program_id``/``num_programs`` keep their
+    global values, so each shard computes exactly its programs' outputs."""
+    prev = getattr(_shard, "value", None)
+    _shard.value = (int(axis), int(start), int(stop))
+    try:
+        yield
+    finally:
+        _shard.value = prev
+
+
+def current_program_range():
+    return getattr(_shard, "value", None)
+
+
+# ---------------------------------------------------------------------------
+# device error words
+# ---------------------------------------------------------------------------
+
+_err_words = {}
+
+
+def _error_word(device):
+    import torch
+    key = device.index
+    w = _err_words.get(key)
+    if w is None:
+        w = _err_words[key] = torch.zeros(1, dtype=torch.int32, device=device)
+    return w
+
+
+def read_device_errors(device=None, reset=True) -> int:
+    """Synchronise and return the first in-kernel error recorded on ``device``
+    (0 = none; high byte = code: 1 mbarrier wait timed out)."""
+    import torch
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = _err_words.get(device.index)
+    if w is None:
+        return 0
+    val = int(w.item()) & 0xFFFFFFFF
+    if reset and val:
+        w.zero_()
+    return val
+
+
+# ---------------------------------------------------------------------------
+# compiled kernels
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Compiled:
+    spec: object
+    library: object
+    kernel: object
+    attrs: dict = None
+
+
+def _pow2_div(v, cap):
+    v = abs(int(v))
+    if v == 0:
+        return cap
+    d = 1
+    while v % (d * 2) == 0 and d < cap:
+        d *= 2
+    return d
+
+
+def binding_facts(tk, tensors) -> dict:
+    """Launch facts that specialise the generated code (a coarse, value-free
+    projection of runtime._binding_signature, runtime.py:1221-1231)."""
+    out = {}
+    for p in list(tk.buffers) + list(tk.ptr_params):
+        t = tensors[p.name]
+        dt = _runtime._tensor_info(t)[0]
+        strides = tuple(int(s) for s in t.stride())
+        is_ptr = p in tk.ptr_params
+        access = p.vtype.access
+        writable = access is not tila.types.READ_ONLY
+        out[p.name] = BufferInfo(
+            name=p.name, dtype=dt, rank=len(strides),
+            unit_last=bool(strides) and strides[-1] == 1,
+            stride_div=tuple(_pow2_div(s, 16) for s in strides),
+            base_align=_pow2_div(t.data_ptr(), 256) if t.data_ptr() else 256,
+            writable=writable, is_ptr=is_ptr)
+    return out
+
+
+def _cache_for(jf):
+    cache = getattr(jf, "_b200_cache", None)
+    if cache is None:
+        cache = jf._b200_cache = {}
+    return cache
+
+
+def _debug():
+    return os.environ.get("TILA_DEBUG", "") == "1"
+
+
+def compile_kernel(jf, consts, facts, num_warps, context=None) -> Compiled:
+    tk = jf.tk
+    key = (tila.intrinsics.INTRINSIC_REGISTRY_SEMANTIC_REVISION, jf.source_fingerprint,
+           tuple((k, "Bool" if type(v) is bool else "Int", v) for k, v in sorted(consts.items())),
+           num_warps, tuple(f.key() for f in facts.values()), _debug(),
+           tila.tir.constant_signature(tk.body))
+    cache = _cache_for(jf)
+    hit = cache.get(key)
+    if hit is not None:
+        return hit
+    try:
+        spec = KernelEmitter(tk, consts, facts, num_warps=num_warps, debug=_debug()).generate()
+    except CodegenError as exc:
+        raise TilaError("TILA-TARGET-009", f"B200 backend cannot lower this kernel: {exc}",
+                        Loc(exc.line),
+                        fixes=["restructure the kernel, or run it on CPU arrays (interpreter)"]) from exc
+    try:
+        cubin = native.compile_cubin(spec.source, spec.name)
+        lib = native.Library(cubin)
+        kern = lib.kernel(spec.name)
+    except native.NativeError as exc:
+        raise _failure(exc, "compile" if exc.status == native.TILA_ERR_COMPILE else "load",
+                       spec.source, context or {}) from exc
+    entry = Compiled(spec, lib, kern)
+    cache[key] = entry
+    return entry
+
+
+def _failure(exc, phase, source, context, resource=None):
+    """A TILA-TARGET-010/011 error with the reference's replayable artifact
+    (backend.failure, backend.py:30-58)."""
+    if resource is not None:
+        class _Res(Exception):
+            pass
+        r = _Res(str(exc))
+        r.name, r.required, r.limit = resource
+        return tila.backend.failure(r, phase="resources", source=source, source_map={},
+                                    context=context, resource=True)
+    return tila.backend.failure(exc, phase=phase, source=source, source_map={}, context=context)
+
+
+def preflight(entry: Compiled, context) -> dict:
+    """Resource check before the first launch on a device (backend.py:61-88)."""
+    attrs = entry.kernel.attributes()
+    spec = entry.spec
+    limit = attrs["max_dynamic_smem_bytes"]
+    if spec.smem_bytes > limit:
+        raise _failure(RuntimeError("shared memory"), "resources", spec.source, context,
+                       resource=("shared memory", spec.smem_bytes, limit))
+    if spec.threads > attrs["max_threads_per_block"]:
+        raise _failure(RuntimeError("threads"), "resources", spec.source, context,
+                       resource=("threads", spec.threads, attrs["max_threads_per_block"]))
+    return {"shared_bytes": spec.smem_bytes + attrs["static_smem_bytes"],
+            "shared_limit_bytes": limit + attrs["static_smem_bytes"],
+            "threads": spec.threads, "max_threads": attrs["max_threads_per_block"],
+            "registers_per_thread": attrs["registers_per_thread"],
+            "spill_count": attrs["local_bytes_per_thread"],
+            "tmem_columns": spec.tmem_cols,
+            "performance_only": ["registers_per_thread", "spill_count"]}
+
+
+def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word):
+    args = []
+    for kind, name, ct in entry.spec.params:
+        if kind in ("buffer", "ptr"):
+            args.append(ctypes.c_uint64(tensors[name].data_ptr()))
+        elif kind == "scalar":
+            p = next(s for s in tk.scalars if s.name == name)
+            v = scalar_vals[name]
+            dn = p.dtype.name
+            if dn in ("f16", "bf16"):
+                import numpy as np
+                if dn == "f16":
+                    bits = int(np.asarray(v, dtype=np.float16).view(np.uint16))
+                else:
+                    import ml_dtypes
+                    bits = int(np.asarray(v, dtype=np.float32).astype(ml_dtypes.bfloat16).view(np.uint16))
+                args.append(ctypes.c_uint16(bits))
+            else:
+                args.append(SCALAR_CTYPES[dn](v))
+        elif kind == "nprog":
+            args.append(ctypes.c_int32(grid[name]))
+        elif kind == "pid_off":
+            args.append(ctypes.c_int32(pid_off[name]))
+        elif kind == "err":
+            args.append(ctypes.c_uint64(err_word.data_ptr()))
+        elif kind == "tensormap":
+            args.append(name)   # prepared TensorMap object
+        else:
+            raise AssertionError(kind)
+    return args
+
+
+def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
+    """Compile (cached) and launch a checked kernel on the tensors' device."""
+    import torch
+    jf, tk = launcher.jf, launcher.jf.tk
+    device = next(iter(tensors.values())).device
+    facts = binding_facts(tk, tensors)
+    context = {"kernel": tk.name, "tila_source": jf.tila_source,
+               "source_file": jf.fn.__code__.co_filename,
+               "source_start_line": jf.source_start_line, "consts": consts,
+               "scalars": scalar_vals, "grid": grid, "num_warps": launcher.num_warps,
+               "debug": _debug(), "backend": "b200",
+               "target": asdict(launcher.target) if launcher.target is not None else None}
+    with torch.cuda.device(device):
+        entry = compile_kernel(jf, consts, facts, launcher.num_warps, context)
+        if entry.attrs is None or entry.attrs.get("_device") != device.index:
+            entry.attrs = preflight(entry, context)
+            entry.attrs["_device"] = device.index
+        jf.last_backend_resources = {k: v for k, v in entry.attrs.items() if k != "_device"}
+        g = tuple(grid) + (1,) * (3 - len(grid))
+        launch_grid, pid_off = list(g), [0, 0, 0]
+        shard = current_program_range()
+        if shard is not None:
+            ax, lo, hi = shard
+            lo, hi = max(0, lo), min(g[ax], hi)
+            if hi <= lo:
+                return
+            launch_grid[ax] = hi - lo
+            pid_off[ax] = lo
+        err = _error_word(device)
+        args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        record = LaunchRecord(entry, tuple(launch_grid), args, device)
+        jf._b200_last_launch = record
+        try:
+            record.launch(stream)
+        except native.NativeError as exc:
+            if exc.status == native.TILA_ERR_RESOURCES:
+                raise _failure(exc, "resources", entry.spec.source, context,
+                               resource=("launch", entry.spec.smem_bytes, exc.log)) from exc
+            raise _failure(exc, "launch", entry.spec.source, context) from exc
+
+
+class LaunchRecord:
+    """One prepared launch (kernel, geometry, packed arguments).  Re-issuing it
+    skips Tila's host-side contract checks, so benchmarks can time the kernel
+    alone; the tensors it points at must stay alive and unchanged in shape."""
+
+    def __init__(self, entry, grid, args, device):
+        self.entry, self.grid, self.args, self.device = entry, grid, args, device
+
+    def launch(self, stream=None):
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.entry.kernel.launch(self.grid, (self.entry.spec.threads, 1, 1), self.args,
+                                 smem_bytes=self.entry.spec.smem_bytes, stream=stream)
+
+    @property
+    def kernel_name(self):
+        return self.entry.spec.name
+
+
+def last_launch(jf) -> LaunchRecord:
+    """The most recent B200 launch of ``jf`` (see :class:`LaunchRecord`)."""
+    rec = getattr(jf, "_b200_last_launch", None)
+    if rec is None:
+        raise RuntimeError(f"{jf.__name__} has not been launched on the B200 backend")
+    return rec
+
+
+def generated_source(jf, consts, tensors, num_warps=4) -> str:
+    """CUDA C++ the backend generates for a binding (inspection / CLI)."""
+    facts = binding_facts(jf.tk, tensors)
+    return KernelEmitter(jf.tk, consts, facts, num_warps=num_warps).generate().source

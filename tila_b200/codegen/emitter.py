@@ -1,0 +1,1732 @@
+"""TIR -> CUDA C++ code generator for sm_100a (one CTA per Tila program).
+
+Input: a checked ``TKernel`` (tir.py:357) specialised with its Const values,
+plus launch facts (buffer dtypes, unit strides, alignment).  Output: the
+source of one ``extern "C" __global__`` kernel that includes the tile library
+(``csrc/tile/tila_tile.cuh``), and a :class:`KernelSpec` saying how to launch
+it.  It replaces ``Lowering.kernel_source`` (lowering.py:136-182) and keeps
+its ABI order: buffer pointers, Ptr parameters, scalars (lowering.py:204-213);
+Consts become compile-time constants of the generated source.
+
+Values of the program are represented as
+
+* ``scalar``  uniform C++ expressions (pids, scalars, loop variables, full
+  reductions, scalar loads) - every thread computes the same value;
+* ``func``    index-functional tiles (arange, broadcasts of scalars, masks,
+  and element-wise functions of those): no storage, an element is a C++
+  expression of its index, re-evaluated where it is used;
+* ``reg``     materialised tiles: a per-thread register array in a
+  :mod:`layouts` layout;
+* ``tmem``    f32 dot accumulators resident in tensor memory.
+
+Element-wise operations read their operands in the consumer's layout.  When a
+register operand's layout does not hold the needed element in the same
+thread at a compile-time slot, it is redistributed through shared memory.
+Reductions fold inside a thread, then across threads with xor shuffles and a
+shared-memory stage (NaN-propagating max, ADR-008).  Loads and stores are
+masked per element; groups of consecutive, aligned, fully active elements
+move with 128-bit accesses.  ``dot`` runs on the 5th-generation tensor core:
+operands are staged into shared memory in the UMMA K-major layout,
+``tcgen05.mma`` accumulates into TMEM, and ``tcgen05.ld`` reads the result
+into the TMEM-row layout.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .._reference import tila
+from . import dtypes as DT
+from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_predicate,
+                      source_slot_map)
+
+T_ = tila.tir
+TY = tila.types
+D = tila.dtypes
+dims_mod = tila.dims
+
+
+class CodegenError(Exception):
+    """The TIR uses something this backend does not lower (TILA-TARGET-009)."""
+
+    def __init__(self, message, line=0):
+        super().__init__(message)
+        self.line = line
+
+
+# ---------------------------------------------------------------------------
+# values
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Val:
+    kind: str                 # scalar | func | reg | tmem | ptr
+    dt: object
+    shape: tuple = ()
+    expr: str = None          # scalar
+    fn: object = None         # func: callable(idx: tuple[str]) -> str
+    name: str = None          # reg: C++ array name
+    layout: Layout = None     # reg
+    tmem_col: int = 0         # tmem: column offset of the accumulator
+    ptr: tuple = None         # ptr: (param name, offset Val)
+    zero: bool = False        # func known to be all zeros
+    const: object = None      # compile-time known python value (scalars)
+
+    @property
+    def is_tile(self):
+        return bool(self.shape)
+
+
+@dataclass
+class BufferInfo:
+    """Launch facts about one Buffer / Ptr binding (part of the cache key)."""
+    name: str
+    dtype: object
+    rank: int
+    unit_last: bool            # last-dim element stride == 1
+    stride_div: tuple          # per dim: largest power of two (<= 16) dividing the stride
+    base_align: int            # largest power of two (<= 256) dividing the base address
+    writable: bool
+    is_ptr: bool = False
+
+    def key(self):
+        return (self.name, self.dtype.name, self.rank, self.unit_last, self.stride_div,
+                self.base_align, self.writable, self.is_ptr)
+
+
+@dataclass
+class KernelSpec:
+    """Everything the host needs to launch a generated kernel."""
+    name: str
+    source: str
+    threads: int
+    smem_bytes: int
+    params: list               # [(kind, name, ctype)] in launch order
+    tmem_cols: int = 0
+    notes: list = field(default_factory=list)
+    tensor_maps: list = field(default_factory=list)
+    persistent: bool = False
+    grid_override: object = None
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def _eval_dim(d, consts):
+    if isinstance(d, int):
+        return d
+    v = dims_mod.eval_num(d, consts)
+    return int(v)
+
+
+def _stmt_names_assigned(stmts, out=None):
+    out = set() if out is None else out
+    for s in stmts:
+        if isinstance(s, T_.TAssign):
+            out.add(s.name)
+        elif isinstance(s, (T_.TIf, T_.TStaticIf)):
+            _stmt_names_assigned(s.then_body, out)
+            _stmt_names_assigned(s.else_body, out)
+        elif isinstance(s, T_.TFor):
+            out.add(s.var)
+            _stmt_names_assigned(s.body, out)
+    return out
+
+
+class _Smem:
+    """Linear plan of the kernel's dynamic shared memory."""
+
+    def __init__(self):
+        self.top = 0
+        self.scratch = 0        # size of the shared redistribution/reduction scratch
+
+    def alloc(self, nbytes, align=16):
+        self.top = (self.top + align - 1) // align * align
+        off = self.top
+        self.top += nbytes
+        return off
+
+    def need_scratch(self, nbytes):
+        self.scratch = max(self.scratch, nbytes)
+
+
+# ---------------------------------------------------------------------------
+# the emitter
+# ---------------------------------------------------------------------------
+
+class KernelEmitter:
+    MAX_SCRATCH = 96 * 1024
+
+    def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
+                 entry_name=None, debug=False):
+        self.tk = tk
+        self.consts = dict(consts)
+        self.buffers = buffers
+        self.T = 32 * num_warps
+        self.debug = debug
+        self.entry = entry_name or f"tila_{tk.name}"
+        self.lines = []
+        self.indent = 1
+        self.env = {}
+        self.counter = 0
+        self.smem = _Smem()
+        self.smem.top = 64
+        self.tmem_cols = 0
+        self.uses_tmem = False
+        self.uses_mma = False
+        self.conv_cache = {}
+        self.slot_cache = {}
+        self.scalar_params = {s.name: s for s in tk.scalars}
+        self.const_names = {c.name for c in tk.consts}
+        self.buffer_params = {b.name: b for b in tk.buffers}
+        self.ptr_params = {p.name: p for p in tk.ptr_params}
+        self.dot_rows = set()
+        self._scan_dots(tk.body)
+
+    # -- small utilities ---------------------------------------------------
+
+    def fresh(self, base="t"):
+        self.counter += 1
+        return f"{base}_{self.counter}"
+
+    def emit(self, line=""):
+        self.lines.append("  " * self.indent + line if line else "")
+
+    def fail(self, msg, line=0):
+        raise CodegenError(msg, line)
+
+    def dims(self, vt):
+        return tuple(_eval_dim(d, self.consts) for d in vt.dims)
+
+    def vt_info(self, vt):
+        """(dtype, shape, is_pointer) of a TIR value type."""
+        if isinstance(vt, TY.ScalarT):
+            return vt.dtype, (), False
+        if isinstance(vt, TY.MaskT):
+            return D.bool_, self.dims(vt), False
+        if isinstance(vt, TY.BlockT):
+            if isinstance(vt.elem, TY.ScalarT):
+                return vt.elem.dtype, self.dims(vt), False
+            if isinstance(vt.elem, TY.PtrT):
+                return vt.elem.element, self.dims(vt), True
+        if isinstance(vt, TY.PtrT):
+            return vt.element, (), True
+        if isinstance(vt, TY.ConstT):
+            return vt.dtype, (), False
+        self.fail(f"unsupported value type {vt!r}")
+
+    def _scan_dots(self, stmts):
+        """Row counts of dot results: 2-D tiles with that many rows default to
+        the TMEM-row layout so that soft-max style code around a dot needs no
+        redistribution."""
+        def visit(node):
+            if isinstance(node, T_.TDot):
+                dt, shape, _ = self.vt_info(node.vt)
+                self.dot_rows.add(tuple(shape))
+            if dataclasses.is_dataclass(node):
+                for f in dataclasses.fields(node):
+                    if f.name in ("vt", "definition", "effect"):
+                        continue
+                    v = getattr(node, f.name)
+                    if isinstance(v, list):
+                        for x in v:
+                            visit(x)
+                    elif dataclasses.is_dataclass(v):
+                        visit(v)
+        for s in stmts:
+            visit(s)
+
+    # -- layouts -----------------------------------------------------------
+
+    def default_layout(self, shape, dt=None) -> Layout:
+        if len(shape) == 2 and shape[0] <= 128 and any(
+                shape[0] == m and shape[1] in (n, 1) for m, n in self.dot_rows):
+            return TmemRows(tuple(shape), self.T)
+        if len(shape) not in (1, 2):
+            self.fail(f"tiles of rank {len(shape)} are not supported by the B200 backend")
+        last = shape[-1]
+        V = 4
+        if dt is not None and DT.size(dt) == 2:
+            V = 8
+        if dt is not None and DT.size(dt) == 8:
+            V = 2
+        return Blocked(tuple(shape), self.T, min(V, last))
+
+    def slot_map(self, src: Layout, dst: Layout, dst_shape):
+        key = (src.key(), dst.key(), tuple(dst_shape))
+        if key not in self.slot_cache:
+            self.slot_cache[key] = source_slot_map(src, dst, dst_shape)
+        return self.slot_cache[key]
+
+    # -- element access ------------------------------------------------------
+
+    @staticmethod
+    def bcast_idx(idx, shape):
+        """Index of an operand of ``shape`` broadcast to a consumer index."""
+        rank = len(shape)
+        idx = tuple(idx)[len(idx) - rank:] if rank else ()
+        return tuple("0" if n == 1 else i for i, n in zip(idx, shape))
+
+    def elem(self, v: Val, layout: Layout, r, smap=None) -> str:
+        """C++ expression of operand ``v`` at consumer slot ``r`` of ``layout``."""
+        if v.kind == "scalar":
+            return v.expr
+        if v.kind == "func":
+            return v.fn(self.bcast_idx(layout.coord(r), v.shape))
+        if v.kind == "reg":
+            if isinstance(r, int) and smap is not None:
+                return f"{v.name}[{smap[r]}]"
+            aff = getattr(v, "_affine", None)
+            if aff is not None and aff != (0, 1):
+                a, b = aff
+                if isinstance(r, int):
+                    return f"{v.name}[{a + b * r}]"
+                return f"{v.name}[{a}]" if b == 0 else f"{v.name}[{a} + {b} * ({r})]"
+            return f"{v.name}[{r}]"
+        self.fail(f"value of kind {v.kind} used as an element-wise operand")
+
+    def prepare_operands(self, operands, layout, shape):
+        """Make every register operand readable in ``layout``; returns
+        (operands, maps, straight) where ``straight`` asks for unrolled code."""
+        out, maps, straight = [], [], False
+        for v in operands:
+            if v.kind == "tmem":
+                v = self.tmem_to_reg(v)
+            if v.kind == "ptr":
+                self.fail("pointer tiles are not supported in element-wise code yet")
+            if v.kind == "reg":
+                m = self.slot_map(v.layout, layout, shape)
+                if m is None:
+                    v = self.convert(v, layout, shape)
+                    m = self.slot_map(v.layout, layout, shape)
+                    assert m is not None
+                aff = _affine_map(m)
+                if aff is None:
+                    straight = True
+                elif aff != (0, 1):
+                    # read through an affine slot expression in loop form
+                    v = dataclasses.replace(v, name=v.name, layout=v.layout)
+                    v._affine = aff
+                maps.append(m)
+            else:
+                maps.append(None)
+            out.append(v)
+        if not straight:
+            maps = [None] * len(out)
+        return out, maps, straight
+
+    def pick_layout(self, operands, shape, dt):
+        for v in operands:
+            if v.kind == "reg" and tuple(v.shape) == tuple(shape):
+                return v.layout
+        for v in operands:
+            if v.kind == "tmem" and tuple(v.shape) == tuple(shape):
+                return TmemRows(tuple(shape), self.T)
+        return self.default_layout(shape, dt)
+
+    def materialize_elementwise(self, dt, shape, operands, make_expr, layout=None, base="v"):
+        """New register tile: element r = make_expr([operand exprs at r])."""
+        layout = layout or self.pick_layout(operands, shape, dt)
+        ops, maps, straight = self.prepare_operands(operands, layout, shape)
+        name = self.fresh(base)
+        self.emit(f"{DT.ctype(dt)} {name}[{layout.nreg}];")
+        if straight:
+            for r in range(layout.nreg):
+                exprs = [self.elem(v, layout, r, m) for v, m in zip(ops, maps)]
+                self.emit(f"{name}[{r}] = {make_expr(exprs)};")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+            exprs = [self.elem(v, layout, "r") for v in ops]
+            self.emit(f"  {name}[r] = {make_expr(exprs)};")
+            self.emit("}")
+        return Val("reg", dt, tuple(shape), name=name, layout=layout)
+
+    def materialize(self, v: Val, layout=None) -> Val:
+        if v.kind == "reg" and (layout is None or v.layout == layout):
+            return v
+        if v.kind == "tmem" and layout is None:
+            return self.tmem_to_reg(v)
+        if v.kind == "scalar":
+            self.fail("cannot materialise a scalar as a tile")
+        if v.kind == "reg":
+            return self.convert(v, layout, v.shape)
+        layout = layout or self.default_layout(v.shape, v.dt)
+        return self.materialize_elementwise(v.dt, v.shape, [v], lambda e: e[0], layout)
+
+    # -- shared-memory redistribution --------------------------------------
+
+    def convert(self, v: Val, layout: Layout, shape) -> Val:
+        """Redistribute register tile ``v`` so that ``layout`` (consumer shape
+        ``shape``) can read it in place: owners write the tile to shared
+        memory, every thread reads back the elements its consumer slots need."""
+        key = (v.name, v.layout.key(), layout.key(), tuple(shape))
+        if key in self.conv_cache:
+            return self.conv_cache[key]
+        src = v.layout
+        numel = int(np.prod(v.shape)) if v.shape else 1
+        ct = DT.ctype(v.dt)
+        stype = ct if ct in ("float", "double", "tila::i32", "tila::u32", "tila::i64", "tila::u64") else "tila::i32"
+        esize = 8 if stype in ("double", "tila::i64", "tila::u64") else 4
+        nbytes = numel * esize
+        if nbytes > self.MAX_SCRATCH:
+            self.fail(f"tile of {numel} elements too large to redistribute through shared memory")
+        self.smem.need_scratch(nbytes)
+        dst_layout = self._layout_for_operand(layout, shape, v.shape)
+        name = self.fresh("cv")
+        self.emit(f"{ct} {name}[{dst_layout.nreg}];")
+        self.emit(f"{{ // redistribute {v.name}: {type(src).__name__} -> {type(dst_layout).__name__}")
+        self.indent += 1
+        buf = self.fresh("xs")
+        self.emit("__syncthreads();")
+        self.emit(f"{stype}* {buf} = reinterpret_cast<{stype}*>(tila_scratch);")
+        sdims = list(v.shape)
+        strides = [int(np.prod(sdims[i + 1:])) for i in range(len(sdims))]
+
+        def flat_of(crd):
+            return " + ".join(f"({c}) * {st}" for c, st in zip(crd, strides)) or "0"
+
+        own = owner_predicate(src)
+        if own == "PER_SLOT" or (isinstance(src, Derived) and not src.reg_affine()):
+            for r in range(src.nreg):
+                cond = self._owner_cond(src, r)
+                pre = f"if ({cond}) " if cond else ""
+                self.emit(f"{pre}{buf}[{flat_of(src.coord(r))}] = ({stype}){v.name}[{r}];")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {src.nreg}; ++r) {{")
+            pre = f"if ({own}) " if own else ""
+            self.emit(f"  {pre}{buf}[{flat_of(src.coord('r'))}] = ({stype}){v.name}[r];")
+            self.emit("}")
+        self.emit("__syncthreads();")
+        dvalid = dst_layout.valid_expr()
+        zero = DT.literal(v.dt, 0)
+
+        def rd(fl):
+            return f"({dvalid}) ? ({ct}){buf}[{fl}] : {zero}" if dvalid else f"({ct}){buf}[{fl}]"
+        if isinstance(dst_layout, Derived) and not dst_layout.reg_affine():
+            for r in range(dst_layout.nreg):
+                self.emit(f"{name}[{r}] = {rd(flat_of(dst_layout.coord(r)))};")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {dst_layout.nreg}; ++r) {name}[r] = {rd(flat_of(dst_layout.coord('r')))};")
+        self.indent -= 1
+        self.emit("}")
+        out = Val("reg", v.dt, tuple(v.shape), name=name, layout=dst_layout)
+        self.conv_cache[key] = out
+        return out
+
+    def _layout_for_operand(self, consumer: Layout, cshape, oshape) -> Layout:
+        """A layout of shape ``oshape`` whose slots line up with ``consumer``
+        (shape ``cshape``) under broadcasting, i.e. thread t slot r holds the
+        operand element that consumer slot r of thread t needs."""
+        oshape = tuple(oshape)
+        cshape = tuple(cshape)
+        if oshape == cshape:
+            return consumer
+        return _BroadcastView(consumer, cshape, oshape)
+
+    # -- TMEM --------------------------------------------------------------
+
+    def tmem_to_reg(self, v: Val) -> Val:
+        layout = TmemRows(tuple(v.shape), self.T)
+        name = self.fresh("acc")
+        n = layout.nreg
+        self.emit(f"float {name}[{n}];")
+        col = f"tila_tmem + {v.tmem_col}" + (f" + (tid >> 7) * {layout.cpg}" if layout.groups > 1 else "")
+        self.emit(f"tila::tc_fence_after();")
+        self.emit(f"tila::tmem_load_row<{n}>({col} + ((tid & 96u) << 16), {name});")
+        return Val("reg", v.dt, v.shape, name=name, layout=layout)
+
+    # -- operands -------------------------------------------------------------
+
+    def value(self, x) -> Val:
+        if isinstance(x, T_.TName):
+            return self.name_value(x.name)
+        if isinstance(x, T_.TLit):
+            return self.literal(x)
+        return self.expr(x)
+
+    def name_value(self, name) -> Val:
+        if name in self.env:
+            return self.env[name]
+        if name in self.consts:
+            c = self.consts[name]
+            if type(c) is bool:
+                return Val("scalar", D.bool_, expr="true" if c else "false", const=c)
+            return Val("scalar", D.i32, expr=DT.int_literal(D.i32, c), const=c)
+        if name in self.scalar_params:
+            p = self.scalar_params[name]
+            return Val("scalar", p.dtype, expr=self.scalar_param_expr(p))
+        if name in self.ptr_params:
+            return Val("ptr", self.ptr_params[name].vtype.elem, ptr=(name, None))
+        self.fail(f"unbound name {name!r}")
+
+    def scalar_param_expr(self, p):
+        n = f"p_{p.name}"
+        if p.dtype.name == "f16":
+            return f"tila::h2f({n})"
+        if p.dtype.name == "bf16":
+            return f"tila::bf2f({n})"
+        return n
+
+    def literal(self, x, dt=None) -> Val:
+        dt = x.dtype or dt
+        v = x.value
+        if dt is None:
+            if isinstance(v, bool):
+                dt = D.bool_
+            elif isinstance(v, int):
+                dt = D.i32
+            else:
+                dt = D.f32
+        return Val("scalar", dt, expr=DT.literal(dt, v), const=v)
+
+    # -- expressions -------------------------------------------------------
+
+    def expr(self, x) -> Val:
+        m = getattr(self, f"e_{type(x).__name__}", None)
+        if m is None:
+            self.fail(f"unsupported TIR expression {type(x).__name__}", getattr(x, "line", 0))
+        return m(x)
+
+    def e_TPid(self, x):
+        return Val("scalar", D.i32, expr=f"pid_{x.axis}")
+
+    def e_TNumPrograms(self, x):
+        return Val("scalar", D.i32, expr=f"nprog_{x.axis}")
+
+    def e_TArange(self, x):
+        end = self.value(x.end)
+        start = int(x.start)
+        _, shape, _ = self.vt_info(x.vt)
+        return Val("func", D.i32, shape,
+                   fn=lambda idx, s=start: f"((tila::i32)({s} + ({idx[0]})))" if s else f"((tila::i32)({idx[0]}))")
+
+    def e_TZeros(self, x):
+        dt, shape, _ = self.vt_info(x.vt)
+        zero = DT.literal(dt, 0)
+        return Val("func", dt, shape, fn=lambda idx, z=zero: z, zero=True)
+
+    def e_TConstant(self, x):
+        return Val("scalar", x.dtype, expr=DT.constant_bits(x.dtype, x.bits))
+
+    def e_TExpand(self, x):
+        v = self.value(x.operand)
+        if v.kind == "scalar" or len(v.shape) != 1:
+            self.fail("expand is supported on 1-D tiles only")
+        n = v.shape[0]
+        shape = (n, 1) if x.axis == 1 else (1, n)
+        if v.kind == "func":
+            if x.axis == 1:
+                return Val("func", v.dt, shape, fn=lambda idx, f=v.fn: f((idx[0],)), zero=v.zero)
+            return Val("func", v.dt, shape, fn=lambda idx, f=v.fn: f((idx[1],)), zero=v.zero)
+        if v.kind == "reg":
+            lay = Derived(v.layout, ("expand", x.axis), shape, tuple(range(v.layout.nreg)))
+            return Val("reg", v.dt, shape, name=v.name, layout=lay)
+        self.fail("expand of this value kind is not supported")
+
+    def e_TReshape(self, x):
+        v = self.value(x.operand)
+        dt, shape, _ = self.vt_info(x.vt)
+        if v.kind == "func":
+            old = v.shape
+            def fn(idx, f=v.fn, old=old, new=shape):
+                flat = " + ".join(f"({i}) * {int(np.prod(new[k + 1:]))}" for k, i in enumerate(idx))
+                oidx = tuple(f"((({flat}) / {int(np.prod(old[k + 1:]))}) % {old[k]})"
+                             for k in range(len(old)))
+                return f(oidx)
+            return Val("func", v.dt, shape, fn=fn, zero=v.zero)
+        if v.kind == "tmem":
+            v = self.tmem_to_reg(v)
+        if v.kind == "reg":
+            lay = Derived(v.layout, ("reshape", shape), shape, tuple(range(v.layout.nreg)))
+            return Val("reg", v.dt, shape, name=v.name, layout=lay)
+        self.fail("reshape of this value kind is not supported")
+
+    def e_TCast(self, x):
+        v = self.value(x.operand)
+        dst = x.dtype
+        if v.kind == "scalar":
+            return Val("scalar", dst, expr=DT.convert(v.dt, dst, v.expr))
+        if v.kind == "func":
+            return Val("func", dst, v.shape, fn=lambda idx, f=v.fn, s=v.dt: DT.convert(s, dst, f(idx)),
+                       zero=v.zero)
+        return self.materialize_elementwise(dst, v.shape, [v], lambda e, s=v.dt: DT.convert(s, dst, e[0]))
+
+    def e_TWhere(self, x):
+        dt, shape, _ = self.vt_info(x.vt)
+        c, a, b = self.value(x.cond), self.value(x.a), self.value(x.b)
+        a = self.coerce(a, dt)
+        b = self.coerce(b, dt)
+        def mk(e):
+            return f"(({e[0]}) ? ({e[1]}) : ({e[2]}))"
+        return self.combine(dt, shape, [c, a, b], mk)
+
+    def coerce(self, v: Val, dt) -> Val:
+        """Literal / differently typed operand -> value of dtype dt."""
+        if v.dt is dt or v.dt.name == dt.name:
+            return v
+        if v.kind == "scalar":
+            if v.const is not None and not isinstance(v.const, bool) and v.expr is not None \
+                    and not v.expr.startswith("p_"):
+                try:
+                    return Val("scalar", dt, expr=DT.literal(dt, v.const), const=v.const)
+                except (ValueError, OverflowError):
+                    pass
+            return Val("scalar", dt, expr=DT.convert(v.dt, dt, v.expr))
+        if v.kind == "func":
+            return Val("func", dt, v.shape, fn=lambda idx, f=v.fn, s=v.dt: DT.convert(s, dt, f(idx)),
+                       zero=v.zero)
+        return self.materialize_elementwise(dt, v.shape, [v], lambda e, s=v.dt: DT.convert(s, dt, e[0]))
+
+    def combine(self, dt, shape, operands, mk):
+        """Element-wise combination: scalar if all scalar, func if no operand
+        is materialised, else a new register tile."""
+        if not shape:
+            if all(o.kind == "scalar" for o in operands):
+                return Val("scalar", dt, expr=mk([o.expr for o in operands]))
+            self.fail("scalar result from tile operands")
+        if all(o.kind in ("scalar", "func") for o in operands):
+            def fn(idx, ops=tuple(operands), shape=tuple(shape)):
+                es = []
+                for o in ops:
+                    if o.kind == "scalar":
+                        es.append(o.expr)
+                    else:
+                        es.append(o.fn(self.bcast_idx(idx, o.shape)))
+                return mk(es)
+            return Val("func", dt, tuple(shape), fn=fn)
+        return self.materialize_elementwise(dt, shape, operands, mk)
+
+    def e_TUna(self, x):
+        v = self.value(x.operand)
+        dt, shape, _ = self.vt_info(x.vt)
+        op = x.op
+        if op in ("any", "all"):
+            return self.reduce_mask(v, op)
+        if op in ("exp", "exp2"):
+            fn = "exp" if op == "exp" else "exp2"
+            if dt.name == "f64":
+                mk = lambda e: f"{fn}((double)({e[0]}))"
+            else:
+                mk = lambda e: DT.round_to(dt, f"{fn}f((float)({e[0]}))")
+            if v.kind == "scalar":
+                return Val("scalar", dt, expr=mk([v.expr]))
+            v = self.coerce(v, dt) if v.dt.name != dt.name else v
+            # transcendental results are always materialised (no re-evaluation)
+            return self.materialize_elementwise(dt, shape, [v], mk)
+        if op == "-":
+            if DT.is_int(dt) and not x.staged:
+                mk = lambda e: f"tila::wneg<{DT.ctype(dt)}>({e[0]})"
+            elif DT.is_float(dt):
+                mk = lambda e: f"(-({e[0]}))"
+            else:
+                mk = lambda e: f"(-({e[0]}))"
+            if v.kind == "scalar" and v.const is not None and x.staged:
+                return Val("scalar", dt, expr=DT.literal(dt, -v.const), const=-v.const)
+        elif op == "+":
+            mk = lambda e: e[0]
+        elif op == "~":
+            if dt.name == "bool":
+                mk = lambda e: f"(!({e[0]}))"
+            else:
+                mk = lambda e: f"(({DT.ctype(dt)})(~({e[0]})))"
+        elif op == "not":
+            mk = lambda e: f"(!({e[0]}))"
+        else:
+            self.fail(f"unsupported unary op {op}")
+        return self.combine(dt, shape, [v], mk)
+
+    def e_TBin(self, x):
+        dt, shape, is_ptr = self.vt_info(x.vt)
+        op = x.op
+        l = self.value(x.left)
+        if op in ("and", "or") and l.kind == "scalar" and l.const is not None:
+            if op == "and" and not l.const:
+                return Val("scalar", D.bool_, expr="false", const=False)
+            if op == "or" and l.const:
+                return Val("scalar", D.bool_, expr="true", const=True)
+        r = self.value(x.right)
+        if is_ptr:
+            self.fail("pointer arithmetic tiles are not supported yet")
+        if x.staged and l.const is not None and r.const is not None:
+            val = self._py_bin(op, l.const, r.const)
+            rdt = dt if dt.name != "bool" or isinstance(val, bool) else D.bool_
+            return Val("scalar", rdt, expr=DT.literal(rdt, val), const=val)
+        odt = x.operand_dtype or (dt if dt.name != "bool" else None)
+        if odt is None:
+            odt = l.dt if l.const is None else r.dt
+        if op in ("and", "or"):
+            mk = (lambda e: f"(({e[0]}) && ({e[1]}))") if op == "and" else (lambda e: f"(({e[0]}) || ({e[1]}))")
+            return self.combine(D.bool_, shape, [l, r], mk)
+        l = self.coerce(l, odt)
+        r = self.coerce(r, odt)
+        mk = self._bin_maker(op, odt, dt)
+        return self.combine(dt, shape, [l, r], mk)
+
+    @staticmethod
+    def _py_bin(op, a, b):
+        import operator as o
+        return {"+": o.add, "-": o.sub, "*": o.mul, "//": o.floordiv, "%": o.mod,
+                "<": o.lt, "<=": o.le, ">": o.gt, ">=": o.ge, "==": o.eq, "!=": o.ne,
+                "&": o.and_, "|": o.or_, "^": o.xor, "<<": o.lshift, ">>": o.rshift,
+                "/": o.truediv}[op](a, b)
+
+    def _bin_maker(self, op, odt, rdt):
+        ct = DT.ctype(odt)
+        if op in ("<", "<=", ">", ">=", "==", "!="):
+            return lambda e: f"(({e[0]}) {op} ({e[1]}))"
+        if odt.name == "bool":
+            if op in ("&", "|", "^"):
+                return lambda e: f"((bool)(({e[0]}) {op} ({e[1]})))"
+            self.fail(f"operator {op} on masks")
+        if DT.is_float(odt):
+            if op in ("+", "-", "*", "/"):
+                return lambda e: DT.round_to(rdt, f"(({e[0]}) {op} ({e[1]}))")
+            if op == "//":
+                return lambda e: DT.round_to(rdt, f"tila::py_floordiv(({e[0]}), ({e[1]}))")
+            if op == "%":
+                return lambda e: DT.round_to(rdt, f"tila::py_mod(({e[0]}), ({e[1]}))")
+            self.fail(f"operator {op} on floats")
+        # integers: wrapping, floor division (ADR-007)
+        if op == "+":
+            return lambda e: f"tila::wadd<{ct}>({e[0]}, {e[1]})"
+        if op == "-":
+            return lambda e: f"tila::wsub<{ct}>({e[0]}, {e[1]})"
+        if op == "*":
+            return lambda e: f"tila::wmul<{ct}>({e[0]}, {e[1]})"
+        if op == "//":
+            mn = DT.int_literal(odt, DT.int_min(odt))
+            return lambda e: f"tila::floordiv<{ct}>({e[0]}, {e[1]}, {mn})"
+        if op == "%":
+            mn = DT.int_literal(odt, DT.int_min(odt))
+            return lambda e: f"tila::floormod<{ct}>({e[0]}, {e[1]}, {mn})"
+        if op in ("&", "|", "^"):
+            return lambda e: f"(({ct})(({e[0]}) {op} ({e[1]})))"
+        if op == "<<":
+            ut = DT.ctype(self._unsigned(odt))
+            return lambda e: f"(({ct})(({ut})({e[0]}) << ({e[1]})))"
+        if op == ">>":
+            return lambda e: f"(({ct})(({e[0]}) >> ({e[1]})))"
+        if op == "/":
+            return lambda e: f"((float)({e[0]}) / (float)({e[1]}))"
+        self.fail(f"unsupported binary op {op}")
+
+    @staticmethod
+    def _unsigned(dt):
+        return {"i8": D.u8, "i16": D.u16, "i32": D.u32, "i64": D.u64}.get(dt.name, dt)
+
+    # -- reductions ----------------------------------------------------------
+
+    def reduce_mask(self, v: Val, op):
+        """any/all of a Mask -> scalar bool (interp.py:261-264)."""
+        if v.kind == "scalar":
+            return Val("scalar", D.bool_, expr=f"((bool)({v.expr}))")
+        m = self.materialize(v)
+        as_int = Val("reg", D.i32, m.shape, name=None, layout=m.layout)
+        name = self.fresh("mi")
+        lay = m.layout
+        self.emit(f"tila::i32 {name}[{lay.nreg}];")
+        want = "1" if op == "any" else "0"
+        self.emit("#pragma unroll")
+        self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) {name}[r] = ({m.name}[r] ? 1 : 0) == {want} ? 1 : 0;")
+        as_int.name = name
+        total = self._full_reduce(as_int, "max", D.i32)
+        return Val("scalar", D.bool_, expr=f"(({total.expr}) {'!=' if op == 'any' else '=='} 0)")
+
+    def e_TReduce(self, x):
+        v = self.value(x.operand)
+        dt, shape, _ = self.vt_info(x.vt)
+        acc_dt = x.accumulation_dtype
+        if v.kind == "scalar":
+            self.fail("reduction of a scalar")
+        if v.kind == "tmem":
+            v = self.tmem_to_reg(v)
+        if v.kind == "func":
+            v = self.materialize(v)
+        rank = len(v.shape)
+        axis = x.axis
+        if rank == 1:
+            res = self._full_reduce(v, x.op, acc_dt)
+            return Val("scalar", dt, expr=DT.convert(acc_dt, dt, res.expr) if acc_dt is not dt else res.expr)
+        return self._axis_reduce(v, x.op, axis, acc_dt, dt)
+
+    def _fold(self, op, dt):
+        if op == "sum":
+            if DT.is_int(dt):
+                return lambda a, b: f"tila::wadd<{DT.ctype(dt)}>({a}, {b})"
+            return lambda a, b: f"(({a}) + ({b}))"
+        if DT.is_float(dt):
+            return lambda a, b: f"tila::max_nan({a}, {b})"
+        return lambda a, b: f"tila::max_int<{DT.ctype(dt)}>({a}, {b})"
+
+    def _identity(self, op, dt):
+        if op == "sum":
+            return DT.literal(dt, 0)
+        if DT.is_float(dt):
+            return "(-__int_as_float(0x7f800000))" if dt.name != "f64" else "(-__longlong_as_double(0x7ff0000000000000LL))"
+        if DT.is_signed(dt):
+            return DT.int_literal(dt, DT.int_min(dt))
+        return DT.int_literal(dt, 0)
+
+    def _owner_cond(self, layout, r):
+        own = owner_predicate(layout)
+        if own is None:
+            return None
+        if own == "PER_SLOT":
+            from .layouts import _tid_set_expr
+            coords, owners = layout._tables
+            tids = np.nonzero(owners[:, r])[0]
+            e = _tid_set_expr(tids, layout.T)
+            if e is None:
+                e = " || ".join(f"tid == {t}" for t in tids) or "false"
+            return e
+        return own
+
+    def _full_reduce(self, v: Val, op, acc_dt) -> Val:
+        """Reduce every element of a register tile to one uniform scalar."""
+        lay = v.layout
+        ct = DT.ctype(acc_dt)
+        fold = self._fold(op, acc_dt)
+        part = self.fresh("part")
+        self.emit(f"{ct} {part} = {self._identity(op, acc_dt)};")
+        own = owner_predicate(lay)
+        src_dt = v.dt
+        conv = (lambda e: DT.convert(src_dt, acc_dt, e)) if src_dt.name != acc_dt.name else (lambda e: e)
+        if own == "PER_SLOT":
+            for r in range(lay.nreg):
+                c = self._owner_cond(lay, r)
+                self.emit(f"if ({c}) {part} = {fold(part, conv(f'{v.name}[{r}]'))};")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) {part} = {fold(part, conv(f'{v.name}[r]'))};")
+            if own is not None:
+                self.emit(f"if (!({own})) {part} = {self._identity(op, acc_dt)};")
+        return Val("scalar", acc_dt, expr=self._cta_allreduce(part, op, acc_dt))
+
+    def _cta_allreduce(self, part, op, dt) -> str:
+        """All threads' partials -> one value visible to every thread."""
+        ct = DT.ctype(dt)
+        fold = self._fold(op, dt)
+        for m in (16, 8, 4, 2, 1):
+            self.emit(f"{part} = {fold(part, f'tila::shfl_xor({part}, {m})')};")
+        W = self.T // 32
+        if W == 1:
+            return part
+        esize = 8 if DT.size(dt) == 8 else 4
+        self.smem.need_scratch(W * esize)
+        buf = self.fresh("red")
+        out = self.fresh("tot")
+        self.emit("__syncthreads();")
+        self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_scratch);")
+        self.emit(f"if ((tid & 31) == 0) {buf}[tid >> 5] = {part};")
+        self.emit("__syncthreads();")
+        self.emit(f"{ct} {out} = {buf}[0];")
+        self.emit("#pragma unroll")
+        self.emit(f"for (int w = 1; w < {W}; ++w) {out} = {fold(out, f'{buf}[w]')};")
+        return out
+
+    def _axis_reduce(self, v: Val, op, axis, acc_dt, out_dt) -> Val:
+        lay = v.layout
+        if v.shape[axis] == 1:
+            # reducing a unit axis: the value itself, re-typed (interp np.sum/np.max)
+            keep = tuple(n for i, n in enumerate(v.shape) if i != axis)
+            dl = Derived(lay, ("slice", axis), keep, tuple(range(lay.nreg)))
+            conv = lambda e: DT.convert(v.dt, out_dt, DT.convert(v.dt, acc_dt, e[0]))
+            src = Val("reg", v.dt, keep, name=v.name, layout=dl)
+            return self.materialize_elementwise(out_dt, keep, [src], conv, layout=dl)
+        if isinstance(lay, Derived) or not hasattr(lay, "reduce_bits"):
+            lay2 = self.default_layout(v.shape, v.dt)
+            if isinstance(lay2, (Blocked, TmemRows)) and lay2 != lay:
+                v = self.materialize(v, lay2)
+                lay = lay2
+            elif not isinstance(lay, (Blocked, TmemRows)):
+                lay = Blocked(tuple(v.shape), self.T, 1)
+                v = self.materialize(v, lay)
+        coords, owners = lay._tables
+        keep_shape = tuple(n for i, n in enumerate(v.shape) if i != axis)
+        # group the thread's slots by output coordinate (thread independent)
+        t0 = coords[0]
+        groups = {}
+        for r in range(lay.nreg):
+            key = tuple(int(c) for i, c in enumerate(t0[r]) if i != axis)
+            groups.setdefault(key, []).append(r)
+        outs = list(groups.values())
+        # the output slot's representative parent slot
+        regs = tuple(g[0] for g in outs)
+        ct = DT.ctype(acc_dt)
+        fold = self._fold(op, acc_dt)
+        ident = self._identity(op, acc_dt)
+        conv = (lambda e: DT.convert(v.dt, acc_dt, e)) if v.dt.name != acc_dt.name else (lambda e: e)
+        name = self.fresh("rd")
+        n = len(outs)
+        self.emit(f"{ct} {name}[{n}];")
+        own = owner_predicate(lay)
+        for k, g in enumerate(outs):
+            terms = ident
+            for r in g:
+                terms = fold(terms, conv(f"{v.name}[{r}]"))
+            self.emit(f"{name}[{k}] = {terms};")
+        if own is not None and own != "PER_SLOT":
+            self.emit(f"if (!({own})) {{")
+            self.emit(f"  #pragma unroll")
+            self.emit(f"  for (int k = 0; k < {n}; ++k) {name}[k] = {ident};")
+            self.emit("}")
+        bits = lay.reduce_bits(axis)
+        lane_bits = [b for b in bits if b < 5]
+        warp_bits = [b for b in bits if b >= 5]
+        for b in lane_bits:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int k = 0; k < {n}; ++k) {name}[k] = {fold(f'{name}[k]', f'tila::shfl_xor({name}[k], {1 << b})')};")
+        if warp_bits:
+            # shared-memory stage across warps: slot [output][group]
+            G = 1 << len(warp_bits)
+            numel_out = int(np.prod(keep_shape))
+            esize = 8 if DT.size(acc_dt) == 8 else 4
+            self.smem.need_scratch(numel_out * G * esize)
+            buf = self.fresh("rs")
+            self.emit("__syncthreads();")
+            self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_scratch);")
+            gexpr = " | ".join(f"(((tid >> {b}) & 1) << {i})" for i, b in enumerate(warp_bits))
+            lane_mask = sum(1 << b for b in lane_bits)
+            out_lay = Derived(lay, ("slice", axis), keep_shape, regs)
+            oc = out_lay.coord("k") if False else None
+            self.emit(f"const int {buf}_g = {gexpr};")
+            lvalid = lay.valid_expr()
+            for k in range(n):
+                crd = out_lay.coord(k)
+                flat = " + ".join(f"({c}) * {int(np.prod(keep_shape[i + 1:]))}" for i, c in enumerate(crd)) or "0"
+                conds = ([f"(tid & {lane_mask}) == 0"] if lane_mask else []) + ([f"({lvalid})"] if lvalid else [])
+                cond = f"if ({' && '.join(conds)}) " if conds else ""
+                self.emit(f"{cond}{buf}[({flat}) * {G} + {buf}_g] = {name}[{k}];")
+            self.emit("__syncthreads();")
+            for k in range(n):
+                crd = out_lay.coord(k)
+                flat = " + ".join(f"({c}) * {int(np.prod(keep_shape[i + 1:]))}" for i, c in enumerate(crd)) or "0"
+                acc = f"{buf}[({flat}) * {G}]"
+                for gi in range(1, G):
+                    acc = fold(acc, f"{buf}[({flat}) * {G} + {gi}]")
+                pre = f"if ({lvalid}) " if lvalid else ""
+                self.emit(f"{pre}{name}[{k}] = {acc};")
+        out_lay = Derived(lay, ("slice", axis), keep_shape, regs, owner_fn=dedupe_owner)
+        res = Val("reg", acc_dt, keep_shape, name=name, layout=out_lay)
+        if acc_dt.name != out_dt.name:
+            res = self.materialize_elementwise(out_dt, keep_shape, [res],
+                                              lambda e: DT.convert(acc_dt, out_dt, e[0]), layout=out_lay)
+        return res
+
+    # -- memory ----------------------------------------------------------------
+
+    def _buffer_base(self, name):
+        return f"p_{name}"
+
+    def address_terms(self, buffer, coords, layout, r, smaps):
+        """Element offset (i64 C++ expr) of a buffer access at slot r."""
+        terms = []
+        info = self.buffers.get(buffer)
+        for i, c in enumerate(coords):
+            e = self.elem(c, layout, r, smaps[i]) if layout is not None else c.expr
+            if info is not None and info.unit_last and i == len(coords) - 1:
+                terms.append(f"(tila::i64)({e})")
+            else:
+                terms.append(f"(tila::i64)p_{buffer}_stride{i} * (tila::i64)({e})")
+        return " + ".join(terms) if terms else "0"
+
+    def _affine_last(self, node, depth=0):
+        """Coefficient of the tile's last index in a coordinate expression:
+        returns (coef, divisor) where coef in {0, 1, None} and divisor is a
+        power of two dividing the index-independent part (lowering.py:374-416
+        hints, restated as a structural analysis)."""
+        if depth > 40:
+            return None, 1
+        if isinstance(node, T_.TName):
+            if node.name in self.consts:
+                c = self.consts[node.name]
+                return 0, _pow2_div(c) if type(c) is int else 1
+            if node.name in self._defs:
+                return self._affine_last(self._defs[node.name], depth + 1)
+            if node.name in self._loopvars:
+                return 0, self._loopvars[node.name]
+            return (0, 1) if node.name in self.scalar_params or node.name in self._pidnames else (None, 1)
+        if isinstance(node, T_.TLit):
+            return (0, _pow2_div(node.value)) if isinstance(node.value, int) and not isinstance(node.value, bool) else (None, 1)
+        if isinstance(node, T_.TPid):
+            return 0, 1
+        if isinstance(node, T_.TArange):
+            return (1, _pow2_div(int(node.start)))
+        if isinstance(node, T_.TExpand):
+            c, d = self._affine_last(node.operand, depth + 1)
+            if c == 1 and node.axis == 1:
+                return 0, 1 if True else d   # index moved to rows: no longer along the last dim
+            return c, d
+        if isinstance(node, T_.TBin):
+            if node.op in ("+", "-"):
+                c1, d1 = self._affine_last(node.left, depth + 1)
+                c2, d2 = self._affine_last(node.right, depth + 1)
+                if c1 is None or c2 is None:
+                    return None, 1
+                c = c1 + c2 if node.op == "+" else c1 - c2
+                if c not in (0, 1):
+                    return None, 1
+                return c, min(d1, d2)
+            if node.op == "*":
+                c1, d1 = self._affine_last(node.left, depth + 1)
+                c2, d2 = self._affine_last(node.right, depth + 1)
+                if c1 == 0 and c2 == 0:
+                    return 0, min(256, d1 * d2)
+                return None, 1
+        if isinstance(node, T_.TCast):
+            return self._affine_last(node.operand, depth + 1)
+        return None, 1
+
+    def _vector_plan(self, buffer, coord_nodes, coords, layout, shape, dt):
+        """Decide 128-bit access along the last tile dim.  Returns (width,
+        static_aligned) or (1, False)."""
+        info = self.buffers.get(buffer)
+        if info is None or not shape or layout.vec <= 1:
+            return 1, False
+        # which coordinate carries the last tile index?
+        unit_axis = None
+        div = 256
+        for i, (node, c) in enumerate(zip(coord_nodes, coords)):
+            if c.kind == "scalar":
+                d = self._affine_last(node)[1] if node is not None else 1
+                div = min(div, d * info.stride_div[i])
+                continue
+            # a coordinate tile that does not vary along the last dim of the
+            # access shape must be a broadcast (size 1 there)
+            if c.shape and c.shape[-1] == 1 and len(c.shape) == len(shape):
+                d = self._affine_last(node)[1] if node is not None else 1
+                div = min(div, max(d, 1) * info.stride_div[i])
+                continue
+            coef, d = self._affine_last(node) if node is not None else (None, 1)
+            if coef != 1 or c.kind not in ("func",):
+                return 1, False
+            if unit_axis is not None:
+                return 1, False
+            unit_axis = i
+            div = min(div, d)
+        if unit_axis is None or unit_axis != len(coords) - 1 or not info.unit_last:
+            return 1, False
+        esize = DT.size(dt)
+        width = min(layout.vec, 16 // esize) if esize <= 16 else 1
+        if width < 2:
+            return 1, False
+        aligned = (info.base_align >= width * esize) and (div % width == 0)
+        return width, aligned
+
+    def e_TLoad(self, x):
+        dt, shape, _ = self.vt_info(x.vt)
+        if x.buffer is None:
+            return self.ptr_load(x, dt, shape)
+        coords = [self.value(c) for c in x.coords]
+        coords = [self.coerce(c, D.i64) if c.dt.name not in ("i32", "i64", "i16", "i8", "u8", "u16", "u32", "u64") else c
+                  for c in coords]
+        mask = self.value(x.mask) if x.mask is not None else None
+        other = self.value(x.other) if x.other is not None else None
+        if other is not None:
+            other = self.coerce(other, dt)
+        if not shape:
+            return self._scalar_load(x.buffer, coords, mask, other, dt)
+        layout = self.default_layout(shape, dt)
+        return self._tile_load(x.buffer, list(x.coords), coords, mask, other, dt, shape, layout)
+
+    def _scalar_load(self, buffer, coords, mask, other, dt):
+        name = self.fresh("ld")
+        addr = " + ".join(f"(tila::i64)p_{buffer}_stride{i} * (tila::i64)({c.expr})"
+                          for i, c in enumerate(coords)) or "0"
+        fill = other.expr if other is not None else DT.literal(dt, 0)
+        load = DT.load_conv(dt, f"p_{buffer}[{addr}]")
+        if mask is not None:
+            self.emit(f"const {DT.ctype(dt)} {name} = ({mask.expr}) ? {load} : {fill};")
+        else:
+            self.emit(f"const {DT.ctype(dt)} {name} = {load};")
+        return Val("scalar", dt, expr=name)
+
+    def _tile_load(self, buffer, coord_nodes, coords, mask, other, dt, shape, layout):
+        ops = list(coords) + ([mask] if mask is not None else []) + ([other] if other is not None else [])
+        ops, maps, straight = self.prepare_operands(ops, layout, shape)
+        nc = len(coords)
+        coords = ops[:nc]
+        mask = ops[nc] if mask is not None else None
+        other = ops[nc + (1 if mask is not None else 0)] if other is not None else None
+        cm = maps[:nc]
+        mm = maps[nc] if mask is not None else None
+        om = maps[nc + (1 if mask is not None else 0)] if other is not None else None
+        width, aligned = self._vector_plan(buffer, coord_nodes, coords, layout, shape, dt)
+        name = self.fresh("ld")
+        ct, mt = DT.ctype(dt), DT.memtype(dt)
+        self.emit(f"{ct} {name}[{layout.nreg}];")
+        # padding lanes of the layout hold no tile element: never touch memory
+        valid = layout.valid_expr()
+
+        def cond_at(r, smap=None):
+            parts = []
+            if valid is not None:
+                parts.append(f"({valid})")
+            if mask is not None:
+                parts.append(f"({self.elem(mask, layout, r, smap)})")
+            return " && ".join(parts) if parts else None
+
+        fill0 = DT.literal(dt, 0)
+        if width > 1 and not straight:
+            groups = layout.nreg // width
+            vt = _vec_type(DT.size(dt) * width)
+            self.emit("#pragma unroll")
+            self.emit(f"for (int g = 0; g < {groups}; ++g) {{")
+            self.indent += 1
+            self.emit(f"const int r0 = g * {width};")
+            off = self.address_terms(buffer, coords, layout, "r0", cm)
+            self.emit(f"const tila::i64 off = {off};")
+            lane_cond = cond_at("r")
+            if lane_cond is not None:
+                self.emit(f"bool m[{width}];")
+                self.emit("bool all = true;")
+                self.emit("#pragma unroll")
+                self.emit(f"for (int j = 0; j < {width}; ++j) {{ const int r = r0 + j; m[j] = {lane_cond}; all = all && m[j]; }}")
+            else:
+                self.emit("const bool all = true;")
+            cond = "all" if aligned else f"all && ((reinterpret_cast<unsigned long long>(p_{buffer} + off) & {DT.size(dt) * width - 1}) == 0)"
+            self.emit(f"if ({cond}) {{")
+            self.emit(f"  const {vt} w = *reinterpret_cast<const {vt}*>(p_{buffer} + off);")
+            self.emit(f"  const {mt}* e = reinterpret_cast<const {mt}*>(&w);")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int j = 0; j < {width}; ++j) {name}[r0 + j] = {DT.load_conv(dt, 'e[j]')};")
+            self.emit("} else {")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int j = 0; j < {width}; ++j) {{")
+            self.emit("    const int r = r0 + j;")
+            offr = self.address_terms(buffer, coords, layout, "r", cm)
+            fill = self.elem(other, layout, "r") if other is not None else fill0
+            mcond = "m[j]" if lane_cond is not None else "true"
+            self.emit(f"    {name}[r] = {mcond} ? {DT.load_conv(dt, f'p_{buffer}[{offr}]')} : {fill};")
+            self.emit("  }")
+            self.emit("}")
+            self.indent -= 1
+            self.emit("}")
+        else:
+            rng = range(layout.nreg) if straight else ["r"]
+            if not straight:
+                self.emit("#pragma unroll")
+                self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+                self.indent += 1
+            for r in rng:
+                off = self.address_terms(buffer, coords, layout, r, cm)
+                fill = self.elem(other, layout, r, om) if other is not None else fill0
+                ld = DT.load_conv(dt, f"p_{buffer}[{off}]")
+                c = cond_at(r, mm)
+                if c is not None:
+                    self.emit(f"{name}[{r}] = ({c}) ? {ld} : {fill};")
+                else:
+                    self.emit(f"{name}[{r}] = {ld};")
+            if not straight:
+                self.indent -= 1
+                self.emit("}")
+        return Val("reg", dt, tuple(shape), name=name, layout=layout)
+
+    def s_TStore(self, s):
+        if s.buffer is None:
+            return self.ptr_store(s)
+        b = self.buffer_params[s.buffer]
+        dt = b.vtype.elem
+        coords = [self.value(c) for c in s.coords]
+        value = self.value(s.value)
+        mask = self.value(s.mask) if s.mask is not None else None
+        shapes = [c.shape for c in coords] + [value.shape] + ([mask.shape] if mask is not None else [])
+        shape = _broadcast_shapes(shapes)
+        value = self.coerce(value, dt) if value.dt.name != dt.name else value
+        if not shape:
+            addr = " + ".join(f"(tila::i64)p_{s.buffer}_stride{i} * (tila::i64)({c.expr})"
+                              for i, c in enumerate(coords)) or "0"
+            st = f"p_{s.buffer}[{addr}] = {DT.store_conv(dt, value.expr)};"
+            cond = "tid == 0" + (f" && ({mask.expr})" if mask is not None else "")
+            self.emit(f"if ({cond}) {st}")
+            return
+        if value.kind == "tmem":
+            value = self.tmem_to_reg(value)
+        if value.kind == "reg" and tuple(value.shape) == tuple(shape):
+            layout = value.layout
+            if isinstance(layout, Derived) and not layout.reg_affine():
+                pass
+        else:
+            layout = self.default_layout(shape, dt)
+        ops = list(coords) + [value] + ([mask] if mask is not None else [])
+        ops, maps, straight = self.prepare_operands(ops, layout, shape)
+        nc = len(coords)
+        coords, value = ops[:nc], ops[nc]
+        mask = ops[nc + 1] if mask is not None else None
+        cm, vm = maps[:nc], maps[nc]
+        mm = maps[nc + 1] if mask is not None else None
+        own = owner_predicate(layout)
+        width, aligned = self._vector_plan(s.buffer, list(s.coords), coords, layout, shape, dt)
+        if own == "PER_SLOT" or (isinstance(layout, Derived) and not layout.reg_affine()):
+            straight = True
+            width = 1
+        mt = DT.memtype(dt)
+        self.emit("{")
+        self.indent += 1
+        if own is not None and own != "PER_SLOT":
+            self.emit(f"if ({own}) {{")
+            self.indent += 1
+        if width > 1 and not straight:
+            groups = layout.nreg // width
+            vt = _vec_type(DT.size(dt) * width)
+            self.emit("#pragma unroll")
+            self.emit(f"for (int g = 0; g < {groups}; ++g) {{")
+            self.indent += 1
+            self.emit(f"const int r0 = g * {width};")
+            self.emit(f"const tila::i64 off = {self.address_terms(s.buffer, coords, layout, 'r0', cm)};")
+            if mask is not None:
+                self.emit(f"bool m[{width}];")
+                self.emit("bool all = true;")
+                self.emit("#pragma unroll")
+                self.emit(f"for (int j = 0; j < {width}; ++j) {{ const int r = r0 + j; m[j] = {self.elem(mask, layout, 'r')}; all = all && m[j]; }}")
+            else:
+                self.emit("const bool all = true;")
+            cond = "all" if aligned else f"all && ((reinterpret_cast<unsigned long long>(p_{s.buffer} + off) & {DT.size(dt) * width - 1}) == 0)"
+            self.emit(f"if ({cond}) {{")
+            self.emit(f"  {vt} w;")
+            self.emit(f"  {mt}* e = reinterpret_cast<{mt}*>(&w);")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int j = 0; j < {width}; ++j) {{ const int r = r0 + j; e[j] = {DT.store_conv(dt, self.elem(value, layout, 'r'))}; }}")
+            self.emit(f"  *reinterpret_cast<{vt}*>(p_{s.buffer} + off) = w;")
+            self.emit("} else {")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int j = 0; j < {width}; ++j) {{")
+            self.emit("    const int r = r0 + j;")
+            offr = self.address_terms(s.buffer, coords, layout, "r", cm)
+            mcond = "m[j]" if mask is not None else "true"
+            self.emit(f"    if ({mcond}) p_{s.buffer}[{offr}] = {DT.store_conv(dt, self.elem(value, layout, 'r'))};")
+            self.emit("  }")
+            self.emit("}")
+            self.indent -= 1
+            self.emit("}")
+        else:
+            rng = range(layout.nreg) if straight else ["r"]
+            if not straight:
+                self.emit("#pragma unroll")
+                self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+                self.indent += 1
+            for r in rng:
+                off = self.address_terms(s.buffer, coords, layout, r, cm)
+                val = DT.store_conv(dt, self.elem(value, layout, r, vm))
+                conds = []
+                if own == "PER_SLOT":
+                    conds.append(self._owner_cond(layout, r))
+                if mask is not None:
+                    conds.append(f"({self.elem(mask, layout, r, mm)})")
+                cond = f"if ({' && '.join(conds)}) " if conds else ""
+                self.emit(f"{cond}p_{s.buffer}[{off}] = {val};")
+            if not straight:
+                self.indent -= 1
+                self.emit("}")
+        if own is not None and own != "PER_SLOT":
+            self.indent -= 1
+            self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+
+    def ptr_load(self, x, dt, shape):
+        self.fail("Ptr-form loads are not supported by the B200 backend yet", x.line)
+
+    def ptr_store(self, s):
+        self.fail("Ptr-form stores are not supported by the B200 backend yet", s.line)
+
+    def e_TBufPtr(self, x):
+        self.fail("buffer pointers are not supported by the B200 backend yet", getattr(x, "line", 0))
+
+    def e_TAtomicAdd(self, x):
+        self.fail("atomic_add is not supported by the B200 backend yet", x.line)
+
+    # -- dot (tcgen05) -------------------------------------------------------
+
+    def e_TDot(self, x):
+        dt, shape, _ = self.vt_info(x.vt)
+        a = self.value(x.a)
+        b = self.value(x.b)
+        acc = self.value(x.acc) if x.acc is not None else None
+        M, K = a.shape
+        K2, N = b.shape
+        if K != K2 or (M, N) != tuple(shape):
+            self.fail("dot shape mismatch")
+        if M > 128:
+            self.fail("dot with more than 128 rows is not supported yet")
+        if N > 256:
+            self.fail("dot with more than 256 columns is not supported yet")
+        Npad = max(16, N)
+        if Npad % 16:
+            self.fail("dot N must be a multiple of 16 or smaller than 16")
+        self.uses_mma = True
+        self.uses_tmem = True
+        cols = _pow2_at_least(max(32, Npad))
+        self.tmem_cols = max(self.tmem_cols, cols)
+        # stage operands: A (M x K) K-major, B as N x K K-major
+        a_off = self.smem.alloc(128 * K * 2, 1024)
+        b_off = self.smem.alloc(Npad * K * 2, 1024)
+        self._stage_operand(a, a_off, K, transpose=False)
+        self._stage_operand(b, b_off, K, transpose=True)
+        # accumulator input
+        accumulate = "0"
+        col = 0
+        if acc is not None and not (acc.kind == "func" and acc.zero):
+            accv = acc if acc.kind != "tmem" else self.tmem_to_reg(acc)
+            if accv.dt.name != "f32":
+                accv = self.coerce(accv, D.f32)
+            lay = TmemRows((M, N), self.T)
+            accv = self.materialize(accv, lay) if not (accv.kind == "reg" and accv.layout == lay) else accv
+            if accv.kind == "scalar":
+                accv = self.materialize_elementwise(D.f32, (M, N), [accv], lambda e: e[0], layout=lay)
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {col}"
+                      + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "")
+                      + f" + ((tid & 96u) << 16), {accv.name});")
+            accumulate = "1"
+        idesc = f"tila::idesc_f16_f32(128, {Npad}, 0, 0)"
+        self.emit("tila::fence_proxy_async_smem();")
+        self.emit("tila::tc_fence_before();")
+        self.emit("__syncthreads();")
+        self.emit("tila::tc_fence_after();")
+        self.emit("if (tid == 0) {")
+        self.emit("  #pragma unroll")
+        self.emit(f"  for (int kk = 0; kk < {K // 16}; ++kk) {{")
+        self.emit(f"    const tila::u64 da = tila::smem_desc(tila::smem_u32(tila_smem + {a_off}) + kk * 256, 128, {K * 16}, 0);")
+        self.emit(f"    const tila::u64 db = tila::smem_desc(tila::smem_u32(tila_smem + {b_off}) + kk * 256, 128, {K * 16}, 0);")
+        self.emit(f"    tila::mma_f16_ss(tila_tmem + {col}, da, db, {idesc}, (kk > 0) ? 1u : {accumulate}u);")
+        self.emit("  }")
+        self.emit("  tila::mma_commit(tila_mma_bar);")
+        self.emit("}")
+        self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
+        self.emit("tila_mma_phase ^= 1u;")
+        self.emit("tila::tc_fence_after();")
+        res = Val("tmem", D.f32, (M, N), tmem_col=col)
+        reg = self.tmem_to_reg(res)
+        if dt.name == "f16":
+            reg = self.materialize_elementwise(dt, (M, N), [reg], lambda e: f"tila::round_f16({e[0]})",
+                                               layout=reg.layout)
+        # the TMEM result is consumed; make sure every warp finished reading before
+        # a later dot overwrites it
+        self.emit("tila::tc_fence_before();")
+        return reg
+
+    def _stage_operand(self, v: Val, off: int, K: int, transpose: bool):
+        """Write an f16 operand into shared memory, K-major, no swizzle.
+        A: element (m, k) -> row m; B (K x N): element (k, n) -> row n."""
+        if v.kind == "tmem":
+            v = self.tmem_to_reg(v)
+        if v.kind == "scalar":
+            self.fail("dot operand must be a tile")
+        if v.kind == "func":
+            v = self.materialize(v)
+        lay = v.layout
+        own = owner_predicate(lay)
+        valid = lay.valid_expr()
+        coords = lay.coord("r")
+        if transpose:
+            p, q = coords[1], coords[0]
+        else:
+            p, q = coords[0], coords[1]
+        conv = (lambda e: f"tila::f2h({e})") if v.dt.name == "f16" else (lambda e: f"tila::f2h((float)({e}))")
+        straight = isinstance(lay, Derived) and not lay.reg_affine() or own == "PER_SLOT"
+        self.emit("__syncthreads();")
+        if straight:
+            for r in range(lay.nreg):
+                c = lay.coord(r)
+                pp, qq = (c[1], c[0]) if transpose else (c[0], c[1])
+                cond = self._owner_cond(lay, r)
+                pre = f"if ({cond}) " if cond else ""
+                self.emit(f"{pre}*reinterpret_cast<tila::u16*>(tila_smem + {off} + tila::kmajor_offset({pp}, {qq}, {K})) = {conv(f'{v.name}[{r}]')};")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) {{")
+            pre = f"if ({valid}) " if valid else ""
+            self.emit(f"  {pre}*reinterpret_cast<tila::u16*>(tila_smem + {off} + tila::kmajor_offset({p}, {q}, {K})) = {conv(f'{v.name}[r]')};")
+            self.emit("}")
+
+    # -- statements ------------------------------------------------------------
+
+    def stmts(self, body):
+        for s in body:
+            self.stmt(s)
+
+    def stmt(self, s):
+        m = getattr(self, f"s_{type(s).__name__}", None)
+        if m is None:
+            self.fail(f"unsupported TIR statement {type(s).__name__}", getattr(s, "line", 0))
+        m(s)
+
+    def s_TAssign(self, s):
+        v = self.value(s.value)
+        if v.kind == "scalar" and v.const is None and not _is_simple(v.expr):
+            name = self.fresh(f"s_{s.name}")
+            self.emit(f"const {DT.ctype(v.dt)} {name} = {v.expr};")
+            v = Val("scalar", v.dt, expr=name)
+        if v.kind == "tmem":
+            v = self.tmem_to_reg(v)
+        self.env[s.name] = v
+        if isinstance(s.value, T_.TPid):
+            self._pidnames.add(s.name)
+        self._defs[s.name] = s.value
+
+    def s_TAssume(self, s):
+        return  # assumptions are proof facts; debug checks are not emitted
+
+    def s_TAtomicStmt(self, s):
+        self.e_TAtomicAdd(s.value)
+
+    def s_TReturn(self, s):
+        self.emit("break;  // return: leave the program body")
+
+    def s_TStaticIf(self, s):
+        c = self._static_cond(s.cond)
+        self.stmts(s.then_body if c else s.else_body)
+
+    def _static_cond(self, node):
+        ev = tila.runtime._eval_const_operand
+        try:
+            return bool(ev(node, self.consts))
+        except Exception:
+            v = self.value(node)
+            if v.const is None:
+                self.fail("static if condition is not a compile-time constant", getattr(node, "line", 0))
+            return bool(v.const)
+
+    def s_TIf(self, s):
+        c = self.value(s.cond)
+        if c.kind != "scalar":
+            self.fail("runtime if needs a scalar condition", s.line)
+        if c.const is not None:
+            self.stmts(s.then_body if c.const else s.else_body)
+            return
+        assigned = _stmt_names_assigned(s.then_body) | _stmt_names_assigned(s.else_body)
+        merged = [n for n in assigned if n in self.env]
+        ends = []
+        for body in (s.then_body, s.else_body):
+            snap = self._snapshot()
+            self.stmts(body)
+            ends.append({n: self.env[n] for n in merged})
+            self._restore(snap)
+        storage = self._declare_merged(merged, [ends[0], ends[1]])
+        self.emit(f"if ({c.expr}) {{")
+        for body in (s.then_body, s.else_body):
+            self.indent += 1
+            saved_env = dict(self.env)
+            self.stmts(body)
+            self._assign_merged(storage)
+            self.env = saved_env
+            self.indent -= 1
+            if body is s.then_body:
+                self.emit("} else {")
+        self.emit("}")
+        for n, st in storage.items():
+            self.env[n] = st
+
+    def s_TFor(self, s):
+        start = self.value(s.start) if s.start is not None else Val("scalar", D.i64, expr="0", const=0)
+        end = self.value(s.end)
+        step = self.value(s.step)
+        if step.const is None:
+            self.fail("loop step must be a compile-time constant", s.line)
+        stepv = int(step.const)
+        if stepv == 0:
+            self.fail("loop step is zero", s.line)
+        assigned = _stmt_names_assigned(s.body)
+        carried = sorted(n for n in assigned if n in self.env and n != s.var)
+        # the loop variable's divisibility (for vector alignment proofs)
+        sdiv = _pow2_div(int(start.const)) if start.const is not None else 1
+        self._loopvars[s.var] = min(sdiv, _pow2_div(abs(stepv)))
+        loop_end_vals = None
+        # two dry runs reach the fixpoint of the carried layouts
+        pre = {n: self.env[n] for n in carried}
+        bound = dict(pre)
+        for _ in range(2):
+            snap = self._snapshot()
+            for n, v in bound.items():
+                self.env[n] = v
+            self.env[s.var] = Val("scalar", D.i32, expr="LOOPVAR")
+            self.indent += 1
+            self.stmts(s.body)
+            self.indent -= 1
+            loop_end_vals = {n: self.env[n] for n in carried}
+            self._restore(snap)
+            bound = {}
+            for n in carried:
+                bound[n] = self._carried_val(pre[n], loop_end_vals[n], n, dry=True)
+        storage = self._declare_carried(carried, pre, loop_end_vals)
+        iv = self.fresh("it")
+        cmp = "<" if stepv > 0 else ">"
+        self.emit(f"for (tila::i64 {iv} = (tila::i64)({start.expr}); {iv} {cmp} (tila::i64)({end.expr}); {iv} += {stepv}) {{")
+        self.indent += 1
+        lv = self.fresh(f"s_{s.var}")
+        self.emit(f"const tila::i32 {lv} = (tila::i32){iv};")
+        for n, st in storage.items():
+            self.env[n] = st
+        self.env[s.var] = Val("scalar", D.i32, expr=lv)
+        self.stmts(s.body)
+        self._assign_merged(storage)
+        self.indent -= 1
+        self.emit("}")
+        for n, st in storage.items():
+            self.env[n] = st
+        self.env.pop(s.var, None)
+
+    # -- merge points (loops and runtime ifs) ------------------------------------
+
+    def _snapshot(self):
+        return (list(self.lines), dict(self.env), self.counter, self.smem.top, self.smem.scratch,
+                self.tmem_cols, dict(self.conv_cache), dict(self._defs), set(self._pidnames),
+                dict(self._loopvars), self.uses_tmem, self.uses_mma, self.indent)
+
+    def _restore(self, snap):
+        (self.lines, self.env, _, self.smem.top, self.smem.scratch, self.tmem_cols, self.conv_cache,
+         self._defs, self._pidnames, self._loopvars, self.uses_tmem, self.uses_mma, self.indent) = snap
+        # keep the counter monotonic so names never collide
+
+    def _carried_val(self, pre, end, name, dry=False):
+        """Representation of a carried variable inside the loop."""
+        if not pre.shape and not end.shape:
+            return Val("scalar", end.dt, expr=f"c_{name}")
+        shape = end.shape or pre.shape
+        dt = end.dt
+        if end.kind == "reg":
+            lay = end.layout
+        elif pre.kind == "reg":
+            lay = pre.layout
+        else:
+            lay = self.default_layout(shape, dt)
+        if isinstance(lay, Derived) and not lay.reg_affine():
+            lay = self.default_layout(shape, dt)
+        return Val("reg", dt, tuple(shape), name=f"c_{name}", layout=lay)
+
+    def _declare_carried(self, carried, pre, end):
+        storage = {}
+        for n in carried:
+            proto = self._carried_val(pre[n], end[n], n)
+            var = self.fresh(f"c_{n}")
+            if not proto.shape:
+                dt = proto.dt
+                src = self.coerce(pre[n], dt) if pre[n].dt.name != dt.name else pre[n]
+                self.emit(f"{DT.ctype(dt)} {var} = {src.expr};")
+                storage[n] = Val("scalar", dt, expr=var)
+            else:
+                lay = proto.layout
+                src = pre[n]
+                if src.kind == "tmem":
+                    src = self.tmem_to_reg(src)
+                if src.dt.name != proto.dt.name:
+                    src = self.coerce(src, proto.dt)
+                self.emit(f"{DT.ctype(proto.dt)} {var}[{lay.nreg}];")
+                ops, maps, straight = self.prepare_operands([src], lay, proto.shape)
+                self._copy_into(var, lay, ops[0], maps[0], straight)
+                storage[n] = Val("reg", proto.dt, proto.shape, name=var, layout=lay)
+        return storage
+
+    def _declare_merged(self, names, ends):
+        storage = {}
+        for n in names:
+            a, b = ends
+            cur = self.env[n]
+            proto = self._carried_val(cur, a if a.kind == "reg" else b, n)
+            var = self.fresh(f"m_{n}")
+            if not proto.shape:
+                self.emit(f"{DT.ctype(proto.dt)} {var} = {self.coerce(cur, proto.dt).expr};")
+                storage[n] = Val("scalar", proto.dt, expr=var)
+            else:
+                lay = proto.layout
+                self.emit(f"{DT.ctype(proto.dt)} {var}[{lay.nreg}];")
+                src = cur if cur.kind != "tmem" else self.tmem_to_reg(cur)
+                ops, maps, straight = self.prepare_operands([self.coerce(src, proto.dt)], lay, proto.shape)
+                self._copy_into(var, lay, ops[0], maps[0], straight)
+                storage[n] = Val("reg", proto.dt, proto.shape, name=var, layout=lay)
+        return storage
+
+    def _assign_merged(self, storage):
+        for n, st in storage.items():
+            cur = self.env[n]
+            if cur.kind == st.kind and cur.name == st.name and cur.expr == st.expr:
+                continue
+            if not st.shape:
+                src = self.coerce(cur, st.dt) if cur.dt.name != st.dt.name else cur
+                self.emit(f"{st.expr} = {src.expr};")
+                continue
+            if cur.kind == "tmem":
+                cur = self.tmem_to_reg(cur)
+            if cur.dt.name != st.dt.name:
+                cur = self.coerce(cur, st.dt)
+            ops, maps, straight = self.prepare_operands([cur], st.layout, st.shape)
+            self._copy_into(st.name, st.layout, ops[0], maps[0], straight)
+
+    def _copy_into(self, var, lay, src, smap, straight):
+        if straight or (isinstance(lay, Derived) and not lay.reg_affine()):
+            for r in range(lay.nreg):
+                self.emit(f"{var}[{r}] = {self.elem(src, lay, r, smap)};")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) {var}[r] = {self.elem(src, lay, 'r')};")
+
+    # -- kernel ----------------------------------------------------------------
+
+    def generate(self) -> KernelSpec:
+        self._defs = {}
+        self._pidnames = set()
+        self._loopvars = {}
+        tk = self.tk
+        params = []
+        sig = []
+        for b in tk.buffers:
+            dt = b.vtype.elem
+            const = "const " if b.vtype.access is TY.READ_ONLY else ""
+            sig.append(f"{const}{DT.memtype(dt)}* __restrict__ p_{b.name}" if b.vtype.access is TY.READ_ONLY
+                       else f"{DT.memtype(dt)}* p_{b.name}")
+            params.append(("buffer", b.name, "ptr"))
+        for p in tk.ptr_params:
+            dt = p.vtype.elem
+            sig.append(f"{DT.memtype(dt)}* p_{p.name}")
+            params.append(("ptr", p.name, "ptr"))
+        for s in tk.scalars:
+            sig.append(f"{DT.memtype(s.dtype)} p_{s.name}")
+            params.append(("scalar", s.name, s.dtype.name))
+        # strides appear as scalars already (x_stride0 ...): also accessible as p_<buf>_stride<i>
+        for ax in range(3):
+            sig.append(f"tila::i32 nprog_{ax}")
+            params.append(("nprog", ax, "i32"))
+        for ax in range(3):
+            sig.append(f"tila::i32 pid_off_{ax}")
+            params.append(("pid_off", ax, "i32"))
+        sig.append("tila::u32* __restrict__ tila_err")
+        params.append(("err", None, "ptr"))
+        body_lines = self.lines
+        self.lines = []
+        self.indent = 2
+        self.stmts(tk.body)
+        body = self.lines
+        out = ['#include "tila_tile.cuh"', ""]
+        out.append(f'extern "C" __global__ void __launch_bounds__({self.T}) {self.entry}(')
+        out.append(",\n".join("    " + x for x in sig) + ") {")
+        out.append("  extern __shared__ __align__(1024) unsigned char tila_smem[];")
+        out.append("  const int tid = threadIdx.x;")
+        out.append("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x + pid_off_0);")
+        out.append("  const tila::i32 pid_1 = (tila::i32)(blockIdx.y + pid_off_1);")
+        out.append("  const tila::i32 pid_2 = (tila::i32)(blockIdx.z + pid_off_2);")
+        # fixed shared-memory head: mbarrier, tmem slot, dead flag; scratch follows the plan
+        scratch_off = (self.smem.top + 127) // 128 * 128
+        # the planned regions start after the head
+        out.append(f"  tila::u64* tila_mma_bar = reinterpret_cast<tila::u64*>(tila_smem);")
+        out.append(f"  tila::u32* tila_tmem_slot = reinterpret_cast<tila::u32*>(tila_smem + 8);")
+        out.append(f"  volatile int& tila_dead = *reinterpret_cast<volatile int*>(tila_smem + 12);")
+        out.append(f"  unsigned char* tila_scratch = tila_smem + {scratch_off};")
+        out.append("  (void)tila_scratch; (void)tila_mma_bar; (void)tila_tmem_slot;")
+        out.append("  tila::u32 tila_mma_phase = 0; (void)tila_mma_phase;")
+        if self.uses_tmem:
+            out.append("  if (tid == 0) { tila::mbar_init(tila_mma_bar, 1); tila::mbar_fence_init(); tila_dead = 0; }")
+            out.append(f"  if (tid < 32) tila::tmem_alloc(tila_tmem_slot, {self.tmem_cols});")
+            out.append("  tila::tc_fence_before();")
+            out.append("  __syncthreads();")
+            out.append("  tila::tc_fence_after();")
+            out.append("  const tila::u32 tila_tmem = *tila_tmem_slot;")
+        out.append("  do {")
+        # the planned smem regions were allocated relative to offset 0 of the plan;
+        # shift them past the head
+        out.extend(body)
+        out.append("  } while (0);")
+        if self.uses_tmem:
+            out.append("  tila::tc_fence_before();")
+            out.append("  __syncthreads();")
+            out.append(f"  if (tid < 32) tila::tmem_dealloc(tila_tmem, {self.tmem_cols});")
+        out.append("}")
+        src = "\n".join(out) + "\n"
+        smem = scratch_off + self.smem.scratch
+        if self.uses_tmem:
+            # keep (resident CTAs) x (TMEM columns) within the SM's 512 columns
+            max_ctas = max(1, 512 // self.tmem_cols)
+            floor_bytes = 233472 // (max_ctas + 1) - 1024 + 1
+            smem = max(smem, floor_bytes)
+        return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols)
+
+
+class _BroadcastView(Layout):
+    """Layout of a broadcast operand that mirrors a consumer layout slot by
+    slot: slot r holds the operand element the consumer's slot r needs."""
+
+    def __init__(self, consumer: Layout, cshape, oshape):
+        self.consumer = consumer
+        self.cshape = tuple(cshape)
+        self.shape = tuple(oshape)
+        self.rank = len(oshape)
+        self.T = consumer.T
+        self.nreg = consumer.nreg
+        self.vec = 1
+
+    def key(self):
+        return ("bview", self.consumer.key(), self.cshape, self.shape)
+
+    def valid_expr(self):
+        return self.consumer.valid_expr()
+
+    def coord(self, r):
+        c = self.consumer.coord(r)
+        c = tuple(c)[len(c) - self.rank:]
+        return tuple("0" if n == 1 else i for i, n in zip(c, self.shape))
+
+    def table(self):
+        coords, owner = self.consumer._tables
+        coords = coords[..., coords.shape[-1] - self.rank:]
+        out = coords.copy()
+        for i, n in enumerate(self.shape):
+            if n == 1:
+                out[..., i] = np.where(coords[..., i] >= 0, 0, -1)
+        return out, np.zeros_like(owner)
+
+
+def _affine_map(m):
+    """(a, b) when slot map m is m[r] = a + b * r, else None."""
+    if not m:
+        return (0, 1)
+    a = m[0]
+    b = m[1] - m[0] if len(m) > 1 else 1
+    if all(x == a + b * i for i, x in enumerate(m)):
+        return (a, b)
+    return None
+
+
+def _pow2_div(v):
+    v = int(v)
+    if v == 0:
+        return 256
+    d = 1
+    while v % (d * 2) == 0 and d < 256:
+        d *= 2
+    return d
+
+
+def _pow2_at_least(n):
+    p = 1
+    while p < n:
+        p *= 2
+    return p
+
+
+def _broadcast_shapes(shapes):
+    shapes = [tuple(s) for s in shapes if s]
+    if not shapes:
+        return ()
+    rank = max(len(s) for s in shapes)
+    out = [1] * rank
+    for s in shapes:
+        s = (1,) * (rank - len(s)) + s
+        for i, n in enumerate(s):
+            if n != 1:
+                out[i] = n
+    return tuple(out)
+
+
+def _vec_type(nbytes):
+    return {16: "uint4", 8: "uint2", 4: "unsigned int", 2: "unsigned short"}[nbytes]
+
+
+def _is_simple(expr):
+    return expr.replace("_", "").isalnum()

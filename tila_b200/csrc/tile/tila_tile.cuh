@@ -1,0 +1,481 @@
+// tila_tile.cuh - sm_100a tile-primitive library used by the kernels that the
+// B200 backend generates from Tila's typed TIR.  Header-only; compiled by
+// NVRTC together with each generated kernel (no host headers are needed).
+//
+// Contents
+//   * scalar semantics of Tila's dtypes (f16/bf16 rounding through f32 the way
+//     NumPy computes them, wrapping integer arithmetic, floor division,
+//     NaN-propagating max) - interp.py:199-333 / numeric.py:56-78 / ADR-008;
+//   * warp/CTA reduction building blocks;
+//   * mbarrier helpers whose waits are bounded and report a timeout through
+//     the kernel's error word instead of hanging;
+//   * TMA tile loads (cp.async.bulk.tensor, no multicast);
+//   * tcgen05 tensor-memory allocation, MMA (kind::f16, f32 accumulate),
+//     commit, tcgen05.ld/st, and shared-memory matrix descriptors.
+#pragma once
+
+namespace tila {
+
+typedef signed char i8;
+typedef short i16;
+typedef int i32;
+typedef long long i64;
+typedef unsigned char u8;
+typedef unsigned short u16;
+typedef unsigned int u32;
+typedef unsigned long long u64;
+
+// ---------------------------------------------------------------------------
+// error reporting
+// ---------------------------------------------------------------------------
+
+enum ErrorCode : u32 {
+  kErrNone = 0,
+  kErrMbarrierTimeout = 1,   // a bounded mbarrier wait gave up
+  kErrTmemAlloc = 2,         // tensor memory allocation failed
+};
+
+// Records the first error of a launch.  `err` points at a device word the
+// host reads after synchronising.
+__device__ __forceinline__ void report_error(u32 *err, u32 code, u32 where) {
+  if (err != nullptr) atomicCAS(err, 0u, (code << 24) | (where & 0xFFFFFFu));
+}
+
+// ---------------------------------------------------------------------------
+// dtype semantics
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float h2f(u16 h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  return f;
+}
+__device__ __forceinline__ u16 f2h(float f) {
+  u16 h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+__device__ __forceinline__ u16 d2h(double d) {
+  u16 h;
+  asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(d));
+  return h;
+}
+__device__ __forceinline__ float bf2f(u16 h) {
+  return __uint_as_float(static_cast<u32>(h) << 16);
+}
+__device__ __forceinline__ u16 f2bf(float f) {
+  u16 h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+__device__ __forceinline__ u16 d2bf(double d) {
+  // f64 -> bf16 with a single rounding: round to f32 with round-to-odd first
+  // so that the second rounding cannot create a double-rounding error.
+  float f;
+  asm("cvt.rn.f32.f64 %0, %1;" : "=f"(f) : "d"(d));
+  double back = static_cast<double>(f);
+  if (back != d && !(d != d)) {
+    u32 bits = __float_as_uint(f);
+    if ((bits & 1u) == 0u) {
+      // move one ulp towards d to make the f32 intermediate odd
+      bits = (back < d) == (f >= 0.0f) ? bits + 1u : bits - 1u;
+      f = __uint_as_float(bits);
+    }
+  }
+  return f2bf(f);
+}
+// Round an f32 to the nearest f16 / bf16 value and widen back (the register
+// representation of f16/bf16 tiles is an f32 holding a representable value).
+__device__ __forceinline__ float round_f16(float f) { return h2f(f2h(f)); }
+__device__ __forceinline__ float round_bf16(float f) { return bf2f(f2bf(f)); }
+
+// NumPy's maximum propagates NaN (ADR-008); PTX max.NaN does the same.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ double max_nan(double a, double b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  return a > b ? a : b;
+}
+template <typename T>
+__device__ __forceinline__ T max_int(T a, T b) { return a > b ? a : b; }
+
+// Wrapping integer arithmetic: compute in the unsigned type of the same width.
+template <typename T> struct Unsigned;
+template <> struct Unsigned<i8> { typedef u8 type; };
+template <> struct Unsigned<i16> { typedef u16 type; };
+template <> struct Unsigned<i32> { typedef u32 type; };
+template <> struct Unsigned<i64> { typedef u64 type; };
+template <> struct Unsigned<u8> { typedef u8 type; };
+template <> struct Unsigned<u16> { typedef u16 type; };
+template <> struct Unsigned<u32> { typedef u32 type; };
+template <> struct Unsigned<u64> { typedef u64 type; };
+
+template <typename T>
+__device__ __forceinline__ T wadd(T a, T b) {
+  typedef typename Unsigned<T>::type U;
+  return static_cast<T>(static_cast<U>(static_cast<U>(a) + static_cast<U>(b)));
+}
+template <typename T>
+__device__ __forceinline__ T wsub(T a, T b) {
+  typedef typename Unsigned<T>::type U;
+  return static_cast<T>(static_cast<U>(static_cast<U>(a) - static_cast<U>(b)));
+}
+template <typename T>
+__device__ __forceinline__ T wmul(T a, T b) {
+  typedef typename Unsigned<T>::type U;
+  return static_cast<T>(static_cast<U>(static_cast<U>(a) * static_cast<U>(b)));
+}
+template <typename T>
+__device__ __forceinline__ T wneg(T a) {
+  typedef typename Unsigned<T>::type U;
+  return static_cast<T>(static_cast<U>(U(0) - static_cast<U>(a)));
+}
+
+// Floor division and modulo with Python semantics; MIN // -1 wraps to MIN
+// and MIN % -1 is 0 (lowering.py:24-38).  Division by zero is excluded by
+// the launch-time integer gate.
+template <typename T>
+__device__ __forceinline__ T floordiv(T a, T b, T minv) {
+  if (static_cast<T>(-1) > static_cast<T>(0)) return b == 0 ? T(0) : a / b;  // unsigned
+  if (a == minv && b == static_cast<T>(-1)) return minv;
+  if (b == 0) return T(0);
+  T q = a / b;
+  T r = a % b;
+  if (r != 0 && ((r < 0) != (b < 0))) q = q - 1;
+  return q;
+}
+template <typename T>
+__device__ __forceinline__ T floormod(T a, T b, T minv) {
+  if (static_cast<T>(-1) > static_cast<T>(0)) return b == 0 ? T(0) : a % b;
+  if (a == minv && b == static_cast<T>(-1)) return T(0);
+  if (b == 0) return T(0);
+  T r = a % b;
+  if (r != 0 && ((r < 0) != (b < 0))) r = r + b;
+  return r;
+}
+
+// Python float floor division / modulo (NumPy's npy_divmod): the remainder
+// takes the divisor's sign and the quotient is floor((a - mod) / b).
+template <typename F>
+__device__ __forceinline__ F py_mod(F a, F b) {
+  F m = fmod(a, b);
+  if (m != F(0)) {
+    if ((b < F(0)) != (m < F(0))) m += b;
+  } else {
+    m = copysign(F(0), b);
+  }
+  return m;
+}
+template <typename F>
+__device__ __forceinline__ F py_floordiv(F a, F b) {
+  if (b == F(0)) return a / b;
+  F m = fmod(a, b);
+  F div = (a - m) / b;
+  if (m != F(0) && ((b < F(0)) != (m < F(0)))) div -= F(1);
+  F fl;
+  if (div != F(0)) {
+    fl = floor(div);
+    if (div - fl > F(0.5)) fl += F(1);
+  } else {
+    fl = copysign(F(0), a / b);
+  }
+  return fl;
+}
+
+// ---------------------------------------------------------------------------
+// reductions
+// ---------------------------------------------------------------------------
+
+struct SumOp {
+  template <typename T> __device__ __forceinline__ T operator()(T a, T b) const { return a + b; }
+};
+struct MaxOp {
+  __device__ __forceinline__ float operator()(float a, float b) const { return max_nan(a, b); }
+  __device__ __forceinline__ double operator()(double a, double b) const { return max_nan(a, b); }
+  template <typename T> __device__ __forceinline__ T operator()(T a, T b) const { return max_int(a, b); }
+};
+struct WrapSumOp {
+  template <typename T> __device__ __forceinline__ T operator()(T a, T b) const { return wadd(a, b); }
+};
+
+template <typename T>
+__device__ __forceinline__ T shfl_xor(T v, int mask) {
+  return __shfl_xor_sync(0xffffffffu, v, mask);
+}
+__device__ __forceinline__ double shfl_xor(double v, int mask) {
+  return __shfl_xor_sync(0xffffffffu, v, mask);
+}
+__device__ __forceinline__ bool shfl_xor(bool v, int mask) {
+  return __shfl_xor_sync(0xffffffffu, static_cast<int>(v), mask) != 0;
+}
+
+// ---------------------------------------------------------------------------
+// shared memory / proxies
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ u32 smem_u32(const void *p) {
+  return static_cast<u32>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier (bounded waits)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(u64 *bar, u32 count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(u64 *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(u64 *bar, u32 bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(u64 *bar, u32 parity) {
+  u32 ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ u64 globaltimer_ns() {
+  u64 t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Time limit of one mbarrier wait.  A healthy wait ends in microseconds; a
+// wait that reaches this limit is treated as dead.
+#ifndef TILA_WAIT_NS
+#define TILA_WAIT_NS 1000000000ull
+#endif
+
+// Waits for the phase with the given parity to complete.  Returns false (and
+// records kErrMbarrierTimeout) when the time limit passes; callers stop
+// issuing work and fall through to their cleanup.  `*dead` is shared state:
+// once any wait failed, later waits return immediately.
+__device__ __forceinline__ bool mbar_wait(u64 *bar, u32 parity, u32 *err, u32 where,
+                                          volatile int *dead) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const u64 start = globaltimer_ns();
+  for (u32 i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0u) {
+      if (dead != nullptr && *dead) return false;
+      if (globaltimer_ns() - start > TILA_WAIT_NS) break;
+    }
+  }
+  report_error(err, kErrMbarrierTimeout, where);
+  if (dead != nullptr) *dead = 1;
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor memory accelerator) tile loads - single CTA, no multicast
+// ---------------------------------------------------------------------------
+
+struct __align__(64) TensorMap { u64 opaque[16]; };
+
+__device__ __forceinline__ void tma_prefetch_desc(const TensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<u64>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const TensorMap *map, u64 *bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<u64>(map)), "r"(smem_u32(bar)),
+        "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void *dst, const TensorMap *map, u64 *bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<u64>(map)), "r"(smem_u32(bar)),
+        "r"(x), "r"(y), "r"(z) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void *dst, const TensorMap *map, u64 *bar,
+                                            int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cta.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<u64>(map)), "r"(smem_u32(bar)),
+        "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory and the 5th-generation tensor core
+// ---------------------------------------------------------------------------
+
+// Allocates `ncols` (power of two >= 32) TMEM columns; executed by one whole
+// warp.  The base address is written to *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(u32 *slot, u32 ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(slot)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(u32 taddr, u32 ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 "matrix descriptor"):
+//   [0,14) start address >> 4, [16,30) leading byte offset >> 4,
+//   [32,46) stride byte offset >> 4, [46,48) version = 1,
+//   [49,52) base offset, [52] LBO mode, [61,64) swizzle mode
+//   (0 none, 2 = 128B, 4 = 64B, 6 = 32B).
+__device__ __forceinline__ u64 smem_desc(u32 saddr, u32 lbo, u32 sbo, u32 swizzle) {
+  u64 d = 0;
+  d |= static_cast<u64>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<u64>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<u64>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<u64>(1) << 46;
+  d |= static_cast<u64>(swizzle & 7u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with f16 inputs and f32 accumulate:
+//   [4,6) D format (1 = f32), [7,10) A format (0 = f16), [10,13) B format,
+//   [15] A major (0 = K-major, 1 = MN-major), [16] B major,
+//   [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr u32 idesc_f16_f32(u32 m, u32 n, u32 a_mn_major, u32 b_mn_major) {
+  return (1u << 4) | (a_mn_major << 15) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]; issued by a single thread.
+__device__ __forceinline__ void mma_f16_ss(u32 d_tmem, u64 a_desc, u64 b_desc, u32 idesc,
+                                           u32 accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]; A is read from tensor memory.
+__device__ __forceinline__ void mma_f16_ts(u32 d_tmem, u32 a_tmem, u64 b_desc, u32 idesc,
+                                           u32 accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive on `bar` once all previously issued tcgen05.mma of this thread are done.
+__device__ __forceinline__ void mma_commit(u64 *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+// tcgen05.ld / st, shape 32x32b: lane i of the warp accesses TMEM lane
+// (32 * (warp % 4) + i), registers walk consecutive columns.
+__device__ __forceinline__ void tmem_ld8(u32 taddr, float *v) {
+  u32 r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld32(u32 taddr, float *v) {
+  u32 r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st8(u32 taddr, const float *v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+                 "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+                 "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])) : "memory");
+}
+__device__ __forceinline__ void tmem_st32(u32 taddr, const float *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+        "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
+        "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Loads `n` (multiple of 8) consecutive f32 columns of this thread's TMEM lane.
+template <int N>
+__device__ __forceinline__ void tmem_load_row(u32 taddr, float *v) {
+  static_assert(N % 8 == 0, "TMEM row loads move multiples of 8 columns");
+  int c = 0;
+#pragma unroll
+  for (; c + 32 <= N; c += 32) tmem_ld32(taddr + c, v + c);
+#pragma unroll
+  for (; c < N; c += 8) tmem_ld8(taddr + c, v + c);
+  tmem_wait_ld();
+}
+template <int N>
+__device__ __forceinline__ void tmem_store_row(u32 taddr, const float *v) {
+  static_assert(N % 8 == 0, "TMEM row stores move multiples of 8 columns");
+  int c = 0;
+#pragma unroll
+  for (; c + 32 <= N; c += 32) tmem_st32(taddr + c, v + c);
+#pragma unroll
+  for (; c < N; c += 8) tmem_st8(taddr + c, v + c);
+  tmem_wait_st();
+}
+
+// ---------------------------------------------------------------------------
+// operand staging layouts for register-sourced MMA operands
+// ---------------------------------------------------------------------------
+
+// Byte offset of element (p, q) of a P x Q f16 operand stored K-major without
+// swizzle: p indexes M (or N), q indexes K.  Core matrices are 8 rows x 16 B;
+// the two core matrices of one K=16 step are LBO = 128 B apart and 8-row
+// groups are SBO = Q * 16 B apart.
+__device__ __forceinline__ u32 kmajor_offset(int p, int q, int Q) {
+  return static_cast<u32>(((p >> 3) * (Q * 16)) + ((q >> 3) * 128) + ((p & 7) * 16) + ((q & 7) * 2));
+}
+
+}  // namespace tila
