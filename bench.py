@@ -1,0 +1,664 @@
+"""Benchmark of the B200 Tila backend on the five judged workloads.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--only]
+                    [--impl reference]
+
+One JSON line on rank 0.  The headline workload (default: row softmax,
+f32 [8192, 1000], the second configuration) gives ``metric``/``value``; every
+other workload is measured in the same run under ``workloads`` unless
+``--only`` is given.
+
+Per workload:
+* ``value``   device time of K steps (CUDA graph of K kernel launches, inputs
+  resident in HBM, rotating input sets whose total footprint exceeds L2), max
+  over ranks; whole-job units / time.
+* ``e2e``     the same metric through the public API: ``kernel[grid](...)``
+  on CUDA tensors with the inputs copied from pinned host memory and the
+  output copied back inside the timed region (Tila's host-side contract and
+  proof checks included, as for every Tila launch).
+* ``roofline``  achieved / measured peak (MEASURED_PEAKS.json) of the
+  dominant kernel.
+* ``cpu_baseline``  Tila's NumPy reference interpreter on the host cores on a
+  bounded sample of the workload (rank 0, N = 1).
+
+Multi-GPU (torchrun, one process per GPU): weak scaling.  The job is N copies
+of the configuration along its program axis (rows, output tiles or
+batch*heads); each rank launches its share of the global program grid with
+``tila_b200.program_range`` and the output shards are gathered to rank 0
+with NCCL (timed separately as ``gather_ms``).
+
+``--impl reference`` times the reference itself - Tila's NumPy interpreter,
+its only CPU execution path - on the same workloads and prints the same line
+with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * (1 << 20)
+ORDER = ["softmax", "add", "matmul", "unfused_attention", "fused_attention"]
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def _traffic_table():
+    p = ROOT / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.index = self._gpu_id(device)
+        self.proc = None
+        self.file = None
+
+    @staticmethod
+    def _gpu_id(device):
+        import torch
+        try:
+            p = torch.cuda.get_device_properties(device)
+            return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        except Exception:
+            return str(device.index)
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# workloads: setup of N-way weak-scaled problems and their steps
+# ---------------------------------------------------------------------------
+
+class Case:
+    """One workload instance on this rank: device buffers (several sets, so
+    that consecutive steps read memory that is not L2-resident), the launches
+    of one step, and the metadata for the JSON line."""
+
+    def __init__(self, key, world, rank, device):
+        import torch
+        import tila_b200
+        from tila_b200 import workloads as W
+        self.key, self.world, self.rank, self.device = key, world, rank, device
+        self.W, self.ti, self.torch = W, tila_b200.tila, torch
+        self.tila_b200 = tila_b200
+        getattr(self, f"_setup_{key}")()
+
+    # helpers
+    def _dev(self, a):
+        return self.torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+
+    def _sets(self, bytes_per_set):
+        return max(1, min(16, -(-2 * L2_BYTES // max(1, bytes_per_set))))
+
+    def _shard(self, total):
+        lo = total * self.rank // self.world
+        hi = total * (self.rank + 1) // self.world
+        return lo, hi
+
+    # -- add --
+    def _setup_add(self):
+        W, torch = self.W, self.torch
+        n1 = 1 << 20
+        n = n1 * self.world
+        x, y = W.add_inputs(n, seed=0)
+        self.host_inputs = [x, y]
+        nset = self._sets(3 * 4 * n1)
+        self.sets = [(self._dev(x), self._dev(y), torch.empty(n, device=self.device)) for _ in range(nset)]
+        grid = (n // 1024,)
+        self.axis, self.grid_axis_total = 0, grid[0]
+        self.launches = [lambda s: W.vector_add[grid](s[0], s[1], s[2], BLOCK=1024)]
+        self.kernels = [W.vector_add]
+        self.out_index = 2
+        self.units_per_rank = W.add_bytes(n1)
+        self.dominant = 0
+        self.dominant_units = W.add_bytes(n1)
+        self.metric_unit = ("HBM GB/s", "GB/s", 1e9)
+        self.dtype = "f32"
+        self.config = {"workload": "add", "N": n1, "BLOCK": 1024, "dtype": "f32"}
+        self.e2e_call = lambda xs: (grid, [xs[0], xs[1]], lambda: torch.empty(n, device=self.device),
+                                    lambda args, out: W.vector_add[grid](args[0], args[1], out, BLOCK=1024))
+
+    # -- softmax --
+    def _setup_softmax(self):
+        W, torch = self.W, self.torch
+        m1, ncol = 8192, 1000
+        m = m1 * self.world
+        x = W.softmax_inputs(m, ncol, seed=0)
+        self.host_inputs = [x]
+        nset = self._sets(2 * 4 * m1 * ncol)
+        self.sets = [(self._dev(x), torch.empty((m, ncol), device=self.device)) for _ in range(nset)]
+        grid = (m,)
+        self.axis, self.grid_axis_total = 0, m
+        self.launches = [lambda s: W.row_softmax[grid](s[0], s[1], BN=1024)]
+        self.kernels = [W.row_softmax]
+        self.out_index = 1
+        self.units_per_rank = W.softmax_bytes(m1, ncol)
+        self.dominant = 0
+        self.dominant_units = self.units_per_rank
+        self.metric_unit = ("HBM GB/s", "GB/s", 1e9)
+        self.dtype = "f32"
+        self.config = {"workload": "softmax", "M": m1, "N": ncol, "BN": 1024, "dtype": "f32"}
+        self.e2e_call = lambda xs: (grid, [xs[0]], lambda: torch.empty((m, ncol), device=self.device),
+                                    lambda args, out: W.row_softmax[grid](args[0], out, BN=1024))
+
+    # -- matmul --
+    def _setup_matmul(self):
+        W, torch = self.W, self.torch
+        m1 = 4096
+        m = m1 * self.world
+        a, b = W.matmul_inputs(m, 4096, 4096, seed=0)
+        self.host_inputs = [a, b]
+        nset = self._sets(2 * 4096 * 4096 * 2 + 4 * 4096 * 4096)
+        self.sets = [(self._dev(a), self._dev(b), torch.empty((m, 4096), device=self.device))
+                     for _ in range(nset)]
+        grid = (m // 128, 4096 // 128)
+        self.axis, self.grid_axis_total = 0, grid[0]
+        self.launches = [lambda s: W.tiled_matmul[grid](s[0], s[1], s[2], BM=128, BN=128, BK=64)]
+        self.kernels = [W.tiled_matmul]
+        self.out_index = 2
+        self.units_per_rank = W.matmul_flops()
+        self.dominant = 0
+        self.dominant_units = self.units_per_rank
+        self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
+        self.dtype = "f16 in, f32 accumulate"
+        self.config = {"workload": "matmul", "M": 4096, "N": 4096, "K": 4096, "BM": 128,
+                       "BN": 128, "BK": 64}
+        self.e2e_call = lambda xs: (grid, [xs[0], xs[1]],
+                                    lambda: torch.empty((m, 4096), device=self.device),
+                                    lambda args, out: W.tiled_matmul[grid](args[0], args[1], out,
+                                                                           BM=128, BN=128, BK=64))
+
+    # -- unfused attention --
+    def _setup_unfused_attention(self):
+        W, torch = self.W, self.torch
+        bh1, l, d = 128, 1024, 64
+        bh = bh1 * self.world
+        q, k, v = W.attention_inputs(bh, l, d, seed=0)
+        self.host_inputs = [q, k, v]
+        qg, kg, vg = self._dev(q), self._dev(k), self._dev(v)
+        s = torch.empty((bh, l, l), device=self.device)
+        p = torch.empty_like(s)
+        o = torch.empty((bh, l, d), device=self.device)
+        self.sets = [(qg, kg, vg, s, p, o)]
+        g1, g2, g3 = (l // 128, l // 128, bh), (bh * l,), (l // 128, bh)
+        # shard axes: scores by heads (axis 2), softmax by rows (axis 0), pv by heads (axis 1)
+        self.multi_shard = [(2, bh), (0, bh * l), (1, bh)]
+        self.launches = [
+            lambda st: W.attention_scores[g1](st[0], st[1], st[3], 0.125, BM=128, BN=128, BD=64),
+            lambda st: W.row_softmax[g2](st[3].view(bh * l, l), st[4].view(bh * l, l), BN=1024),
+            lambda st: W.attention_pv[g3](st[4], st[2], st[5], BM=128, BN=128, BD=64),
+        ]
+        self.kernels = [W.attention_scores, W.row_softmax, W.attention_pv]
+        self.out_index = 5
+        self.units_per_rank = W.unfused_flops(bh1, l, d)
+        self.bytes_per_rank = W.unfused_bytes(bh1, l, d)
+        self.dominant = 1
+        self.dominant_units = 2 * 4 * bh1 * l * l      # softmax kernel: S read + P write
+        self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
+        self.dtype = "f16 in, f32 accumulate"
+        self.config = {"workload": "unfused_attention", "batch": 8, "heads": 16, "seq": l,
+                       "head_dim": d, "launches": 3}
+        self.e2e_call = None
+
+    # -- fused attention --
+    def _setup_fused_attention(self):
+        W, torch = self.W, self.torch
+        bh1, l, d = 128, 4096, 128
+        bh = bh1 * self.world
+        q, k, v = W.attention_inputs(bh, l, d, seed=0)
+        self.host_inputs = [q, k, v]
+        self.sets = [(self._dev(q), self._dev(k), self._dev(v),
+                      torch.empty((bh, l, d), device=self.device))]
+        grid = (l // 128, bh)
+        self.axis, self.grid_axis_total = 1, bh
+        scale = d ** -0.5
+        self.launches = [lambda s: W.flash_attention[grid](s[0], s[1], s[2], s[3], scale,
+                                                           BM=128, BN=128, BD=128)]
+        self.kernels = [W.flash_attention]
+        self.out_index = 3
+        self.units_per_rank = W.fused_flops(bh1, l, d)
+        self.dominant = 0
+        self.dominant_units = self.units_per_rank
+        self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
+        self.dtype = "f16 in, f32 accumulate"
+        self.config = {"workload": "fused_attention", "batch": 4, "heads": 32, "seq": l,
+                       "head_dim": d, "BM": 128, "BN": 128, "causal": False}
+        self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
+                                    lambda args, out: W.flash_attention[grid](*args, out, scale,
+                                                                              BM=128, BN=128, BD=128))
+
+    # -- launching ---------------------------------------------------------
+
+    def _ranges(self):
+        if getattr(self, "multi_shard", None):
+            return [(ax, *self._shard(total)) for ax, total in self.multi_shard]
+        return [(self.axis, *self._shard(self.grid_axis_total))] * len(self.launches)
+
+    def prepare(self):
+        """Launch every step once through the public API (compiling and
+        checking it), and keep the prepared launches for replay."""
+        from tila_b200.backend import last_launch
+        self.records = []
+        ranges = self._ranges()
+        for s in self.sets:
+            recs = []
+            for i, fn in enumerate(self.launches):
+                ax, lo, hi = ranges[i]
+                with self.tila_b200.program_range(ax, lo, hi):
+                    fn(s)
+                recs.append(last_launch(self.kernels[i]))
+            self.records.append(recs)
+        self.torch.cuda.synchronize(self.device)
+
+    def step(self, i):
+        for r in self.records[i % len(self.records)]:
+            r.launch()
+
+
+def run_ours(args, world, rank, device, keys):
+    import torch
+    import torch.distributed as dist
+    peaks = _peaks()
+    traffic = _traffic_table()
+    results = {}
+    for key in keys:
+        case = Case(key, world, rank, device)
+        case.prepare()
+        K, Wm = args.steps, args.warmup
+        for i in range(Wm):
+            case.step(i)
+        torch.cuda.synchronize(device)
+        # capture the K timed steps in one CUDA graph (no host gaps between launches)
+        graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            case.step(0)
+        torch.cuda.synchronize(device)
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(K):
+                case.step(i)
+        torch.cuda.synchronize(device)
+        graph.replay()              # one untimed replay
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device) as clocks:
+            # keep the GPU busy around the timed replay so that the clock
+            # samples (every 100 ms) see the same load as the timed steps
+            cur = torch.cuda.current_stream(device)
+            t_end = time.perf_counter() + 0.3
+            while time.perf_counter() < t_end:
+                graph.replay()
+                torch.cuda.synchronize(device)
+            start.record(cur)
+            graph.replay()
+            end.record(cur)
+            torch.cuda.synchronize(device)
+            t_end = time.perf_counter() + 0.2
+            while time.perf_counter() < t_end:
+                graph.replay()
+                torch.cuda.synchronize(device)
+        ms_local = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms_local], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_total = float(t.item())
+        else:
+            ms_total = ms_local
+        ms_step = ms_total / K
+        name, unit, scale = case.metric_unit
+        value = case.units_per_rank * world / (ms_step * 1e-3) / scale
+        # dominant kernel: its own graph of K launches timed with events
+        dom_ms = ms_step
+        if len(case.launches) > 1:
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=stream):
+                for i in range(K):
+                    case.records[i % len(case.records)][case.dominant].launch()
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g2.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            dom_ms = e0.elapsed_time(e1) / K
+            del g2
+        dom_kernel = case.records[0][case.dominant].kernel_name
+        if W_ROOF.get(key, "hbm") == "hbm":
+            achieved = case.dominant_units / (dom_ms * 1e-3) / 1e9
+            peak, runit = peaks["hbm_gbs"], "GB/s"
+        else:
+            achieved = case.dominant_units / (dom_ms * 1e-3) / 1e12
+            peak, runit = peaks["bf16_tflops"], "TFLOP/s"
+        tr = traffic.get(dom_kernel)
+        roof = {"bound": W_ROOF.get(key, "hbm"), "kernel": dom_kernel, "achieved": round(achieved, 2),
+                "peak": peak, "unit": runit, "frac": round(achieved / peak, 4),
+                "traffic": tr.get("bytes_per_launch") if tr else None,
+                "algorithmic": case.dominant_units, "peak_source": peaks["source"]}
+        # NCCL gather of the output shards to rank 0 (timed separately)
+        gather_ms = None
+        if world > 1:
+            out = case.sets[0][case.out_index]
+            gather_ms = _gather(out, case, world, rank, device)
+        entry = {"metric": name, "value": round(value, 3), "unit": unit, "ms_per_step": round(ms_step, 5),
+                 "steps": K, "gpu_launches": K * len(case.launches),
+                 "roofline": roof, "config": case.config, "clocks": clocks.summary(),
+                 "dtype": case.dtype}
+        if key == "unfused_attention":
+            entry["hbm_gbs"] = round(case.bytes_per_rank * world / (ms_step * 1e-3) / 1e9, 2)
+        if gather_ms is not None:
+            entry["gather_ms"] = round(gather_ms, 4)
+        del graph
+        if case.e2e_call is not None and not args.no_e2e:
+            entry["e2e"] = _e2e(case, args, world, rank, device)
+        if rank == 0 and world == 1 and not args.no_cpu:
+            entry["cpu_baseline"] = cpu_baseline(key, repeats=1)
+        results[key] = entry
+        del case
+        torch.cuda.empty_cache()
+    return results
+
+
+W_ROOF = {"add": "hbm", "softmax": "hbm", "matmul": "tensor", "unfused_attention": "hbm",
+          "fused_attention": "tensor"}
+
+
+def _gather(out, case, world, rank, device):
+    import torch
+    import torch.distributed as dist
+    ax = case.axis if not getattr(case, "multi_shard", None) else 0
+    lead = out.shape[0]
+    per = lead // world
+    shard = out[rank * per:(rank + 1) * per].contiguous()
+    bufs = [torch.empty_like(shard) for _ in range(world)]
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dist.all_gather(bufs, shard)
+    e1.record()
+    torch.cuda.synchronize(device)
+    t = torch.tensor([e0.elapsed_time(e1)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _e2e(case, args, world, rank, device):
+    """Public-API time: H2D of the inputs from pinned memory, kernel[grid](...)
+    (Tila's contract checks included), D2H of the output."""
+    import torch
+    import torch.distributed as dist
+    grid, inputs, make_out, call = case.e2e_call(case.host_inputs)
+    pinned = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in inputs]
+    dev_in = [torch.empty(p.shape, dtype=p.dtype, device=device) for p in pinned]
+    out = make_out()
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    ax, lo, hi = case._ranges()[0]
+    steps = max(2, min(args.steps, 5))
+
+    def one():
+        for p, d in zip(pinned, dev_in):
+            d.copy_(p, non_blocking=True)
+        with case.tila_b200.program_range(ax, lo, hi):
+            call(dev_in, out)
+        host_out.copy_(out, non_blocking=True)
+        torch.cuda.synchronize(device)
+    one()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = (time.perf_counter() - t0) / steps
+    if world > 1:
+        t = torch.tensor([dt], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    name, unit, scale = case.metric_unit
+    h2d = sum(p.numel() * p.element_size() for p in pinned)
+    d2h = host_out.numel() * host_out.element_size()
+    return {"value": round(case.units_per_rank * world / dt / scale, 3), "unit": unit,
+            "ms_per_step": round(dt * 1e3, 3), "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# ---------------------------------------------------------------------------
+# CPU: Tila's NumPy reference interpreter on a bounded sample
+# ---------------------------------------------------------------------------
+
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        return 1
+
+
+def cpu_baseline(key, repeats=1):
+    """Time the reference interpreter on a bounded sample; rate in the
+    workload's unit.  The sample keeps one step to a few seconds."""
+    import tila_b200
+    from tila_b200 import workloads as W
+    ti = tila_b200.tila
+    os.environ.setdefault("TILA_RACE", "off")
+    if key == "add":
+        n = 1 << 20
+        x, y = W.add_inputs(n)
+        out = np.zeros_like(x)
+        fn = lambda: W.vector_add[(n // 1024,)](x, y, out, BLOCK=1024)
+        units, unit, scale, sample, cores = W.add_bytes(n), "GB/s", 1e9, "full workload (N=1048576)", 1
+    elif key == "softmax":
+        m = 1024
+        x = W.softmax_inputs(m, 1000)
+        o = np.zeros_like(x)
+        fn = lambda: W.row_softmax[(m,)](x, o, BN=1024)
+        units, unit, scale, sample, cores = W.softmax_bytes(m, 1000), "GB/s", 1e9, \
+            "1024 of the 8192 rows (1000 columns, BN=1024)", 1
+    elif key == "matmul":
+        a, b = W.matmul_inputs(128, 512, 4096)
+        c = np.zeros((128, 512), np.float32)
+        fn = lambda: W.tiled_matmul[(1, 4)](a, b, c, BM=128, BN=128, BK=64)
+        units, unit, scale = W.matmul_flops(128, 512, 4096), "TFLOP/s", 1e12
+        sample, cores = "4 of the 1024 output tiles (128x512 of C, full K=4096)", _blas_threads()
+    elif key == "unfused_attention":
+        q, k, v = W.attention_inputs(1, 1024, 64)
+        s = np.zeros((1, 1024, 1024), np.float32)
+        p = np.zeros_like(s)
+        o = np.zeros((1, 1024, 64), np.float32)
+
+        def fn():
+            W.attention_scores[(8, 8, 1)](q, k, s, 0.125, BM=128, BN=128, BD=64)
+            W.row_softmax[(1024,)](s.reshape(1024, 1024), p.reshape(1024, 1024), BN=1024)
+            W.attention_pv[(8, 1)](p, v, o, BM=128, BN=128, BD=64)
+        units, unit, scale = W.unfused_flops(1, 1024, 64), "TFLOP/s", 1e12
+        sample, cores = "1 of the 128 batch*heads (L=1024, D=64)", _blas_threads()
+    else:
+        q, k, v = W.attention_inputs(1, 4096, 128)
+        o = np.zeros((1, 4096, 128), np.float32)
+        fn = lambda: W.flash_attention[(32, 1)](q, k, v, o, 128 ** -0.5, BM=128, BN=128, BD=128)
+        units, unit, scale = W.fused_flops(1, 4096, 128), "TFLOP/s", 1e12
+        sample, cores = "1 of the 128 batch*heads (L=4096, D=128)", _blas_threads()
+    fn()                      # warm (decoration caches, first-call imports)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        fn()
+    dt = (time.perf_counter() - t0) / repeats
+    return {"value": units / dt / scale, "unit": unit, "cores": cores, "kind": "reference",
+            "sample": f"Tila NumPy interpreter, {sample}; {repeats} run(s) of "
+                      f"{dt:.3f} s on {os.cpu_count()} host cores"}
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="softmax", choices=ORDER)
+    ap.add_argument("--only", action="store_true", help="measure the headline workload only")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = _dist_env()
+    keys = [args.workload] + ([] if args.only else [k for k in ORDER if k != args.workload])
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        out = {}
+        for key in keys:
+            runs = [cpu_baseline(key) for _ in range(max(1, min(args.steps, 3)))]
+            v = statistics.median(r["value"] for r in runs)
+            base = dict(runs[0], value=v)
+            out[key] = {"value": v, "unit": base["unit"], "cpu_baseline": base,
+                        "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
+                                "d2h_bytes_per_step": 0}}
+        head = out[keys[0]]
+        line = {"impl": "reference", "metric": _metric_name(keys[0]), "value": head["value"],
+                "unit": head["unit"], "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": _dtype(keys[0]), "data": "synthetic (seeded)",
+                "config": _config(keys[0]), "cpu_baseline": head["cpu_baseline"],
+                "e2e": head["e2e"], "workloads": {k: v for k, v in out.items() if k != keys[0]}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    import tila_b200  # noqa: F401
+    try:
+        res = run_ours(args, world, rank, device, keys)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+    if rank == 0:
+        head = res[keys[0]]
+        line = {"metric": head["metric"], "value": head["value"], "unit": head["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": head["dtype"],
+                "data": "synthetic (seeded NumPy inputs of the configured shapes)",
+                "config": dict(head["config"], parallelism=f"grid-partitioned x{world}",
+                               l2="inputs rotated across buffer sets larger than L2"),
+                "roofline": head["roofline"], "clocks": head["clocks"],
+                "gpu_launches": head["gpu_launches"]}
+        for k in ("e2e", "cpu_baseline", "gather_ms", "hbm_gbs"):
+            if k in head:
+                line[k] = head[k]
+        line["workloads"] = {k: v for k, v in res.items() if k != keys[0]}
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _metric_name(key):
+    return "HBM GB/s" if W_ROOF[key] == "hbm" and key != "unfused_attention" else "f16 TFLOPS"
+
+
+def _dtype(key):
+    return "f32" if key in ("add", "softmax") else "f16 in, f32 accumulate"
+
+
+def _config(key):
+    return {"add": {"workload": "add", "N": 1 << 20, "BLOCK": 1024},
+            "softmax": {"workload": "softmax", "M": 8192, "N": 1000, "BN": 1024},
+            "matmul": {"workload": "matmul", "M": 4096, "N": 4096, "K": 4096},
+            "unfused_attention": {"workload": "unfused_attention", "batch": 8, "heads": 16,
+                                  "seq": 1024, "head_dim": 64},
+            "fused_attention": {"workload": "fused_attention", "batch": 4, "heads": 32,
+                                "seq": 4096, "head_dim": 128}}[key]
+
+
+if __name__ == "__main__":
+    main()
