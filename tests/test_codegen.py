@@ -1,0 +1,75 @@
+"""Code generation on CPU: every workload lowers to CUDA C++ that NVRTC
+compiles for sm_100a, and the lowering picks the intended hardware paths
+(128-bit vector accesses, TMA + tcgen05 pipelines) from the binding facts."""
+
+import pytest
+import torch
+
+import tila_b200
+from tila_b200 import native, workloads as W
+from tila_b200.backend import binding_facts
+from tila_b200.codegen.emitter import KernelEmitter
+
+f16 = torch.float16
+
+
+def gen(jf, tensors, warps=4, **consts):
+    spec = KernelEmitter(jf.tk, consts, binding_facts(jf.tk, tensors), num_warps=warps).generate()
+    native.compile_cubin(spec.source, spec.name)
+    return spec
+
+
+@pytest.mark.parametrize("warps", [4, 8])
+def test_add_vectorised(warps):
+    spec = gen(W.vector_add, dict(x=torch.zeros(4096), y=torch.zeros(4096), out=torch.zeros(4096)),
+               warps, BLOCK=1024)
+    assert "uint4" in spec.source and "tcgen05" not in spec.source
+    assert spec.threads == 32 * warps
+
+
+def test_softmax_reductions():
+    spec = gen(W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
+    src = spec.source
+    assert "tila::max_nan" in src and "expf" in src and "shfl_xor" in src
+
+
+def test_matmul_uses_tma_ring_and_tcgen05():
+    t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
+    spec = gen(W.tiled_matmul, t, BM=128, BN=128, BK=64)
+    assert "pipelined contraction loop" in spec.source
+    assert "tma_load_2d" in spec.source and "mma_f16_ss" in spec.source
+    assert len(spec.tensor_maps) == 2
+    assert spec.smem_bytes <= 110 * 1024      # two CTAs per SM
+
+
+def test_matmul_strided_falls_back_to_register_staging():
+    a = torch.zeros(256, 256, dtype=f16).t()
+    t = dict(a=a, b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
+    spec = gen(W.tiled_matmul, t, BM=128, BN=128, BK=64)
+    assert "kmajor_offset" in spec.source          # operand A staged from registers
+
+
+def test_small_tiles_compile():
+    t = dict(a=torch.zeros(19, 35, dtype=f16), b=torch.zeros(35, 23, dtype=f16), c=torch.zeros(19, 23))
+    gen(W.tiled_matmul, t, BM=16, BN=16, BK=32)
+
+
+def test_attention_kernels_compile():
+    q = torch.zeros(2, 256, 64, dtype=f16)
+    s = gen(W.attention_scores, dict(q=q, k=q.clone(), s=torch.zeros(2, 256, 256)), BM=128, BN=128, BD=64)
+    assert "tma_load_3d" in s.source
+    gen(W.attention_pv, dict(p=torch.zeros(2, 256, 256), v=q.clone(), o=torch.zeros(2, 256, 64)),
+        BM=128, BN=128, BD=64)
+    q = torch.zeros(2, 256, 128, dtype=f16)
+    gen(W.flash_attention, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
+        BM=128, BN=128, BD=128)
+
+
+def test_tmem_budget_and_occupancy():
+    q = torch.zeros(2, 256, 128, dtype=f16)
+    spec = gen(W.flash_attention, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
+               BM=128, BN=128, BD=128)
+    cols = spec.tmem_cols
+    assert cols in (32, 64, 128, 256, 512)
+    resident = 233472 // (spec.smem_bytes + 1024)
+    assert resident * cols <= 512, "co-resident CTAs could exhaust tensor memory"

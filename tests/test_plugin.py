@@ -1,0 +1,62 @@
+"""The drop-in boundary: the B200 target and the execute hook."""
+
+import numpy as np
+import pytest
+
+import tila_b200
+from tila_b200 import plugin, workloads as W
+
+ti = tila_b200.tila
+
+
+def test_installed_on_import():
+    assert tila_b200.installed()
+
+
+def test_b200_capability_matches_the_reference_limits():
+    ref = ti.target.SUPPORTED
+    cap = plugin.B200
+    assert cap.arch == (10, 0)
+    assert cap.grid_limits == ref.grid_limits
+    assert cap.max_tile_elements == ref.max_tile_elements
+    assert cap.dot_inputs == ref.dot_inputs and cap.dot_outputs == ref.dot_outputs
+    assert cap.min_dot_k == ref.min_dot_k
+
+
+def test_cpu_arrays_still_run_on_the_interpreter():
+    x = np.arange(300, dtype=np.float32)
+    out = np.zeros_like(x)
+    W.vector_add[(ti.cdiv(300, 128),)](x, x, out, BLOCK=128)
+    np.testing.assert_array_equal(out, x + x)
+
+
+def test_uninstall_restores_the_reference_methods():
+    L = ti.runtime._Launcher
+    ours = (L._resolve_target, L._execute)
+    tila_b200.uninstall()
+    try:
+        assert (L._resolve_target, L._execute) != ours
+    finally:
+        tila_b200.install()
+    assert tila_b200.installed()
+
+
+def test_non_sm100_device_is_rejected():
+    class Props:
+        major, minor, name, uuid = 8, 6, "NVIDIA GeForce RTX 3090", "x"
+
+    class FakeCuda:
+        @staticmethod
+        def get_device_properties(device):
+            return Props()
+
+    class FakeTorch:
+        cuda = FakeCuda()
+        __version__ = "x"
+        version = type("v", (), {"cuda": "12.8"})
+
+    class Dev:
+        index = 0
+    with pytest.raises(ti.errors.TilaError) as exc:
+        plugin.resolve_b200(FakeTorch, Dev())
+    assert exc.value.code == "TILA-TARGET-007"

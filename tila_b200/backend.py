@@ -120,12 +120,16 @@ def binding_facts(tk, tensors) -> dict:
         is_ptr = p in tk.ptr_params
         access = p.vtype.access
         writable = access is not tila.types.READ_ONLY
+        base_align = _pow2_div(t.data_ptr(), 256) if t.data_ptr() else 256
+        esize = t.element_size()
+        tma_ok = (dt is not None and dt.name == "f16" and len(strides) >= 2 and strides[-1] == 1
+                  and base_align >= 16 and all((s * esize) % 16 == 0 and s > 0 for s in strides[:-1])
+                  and all(0 < n < (1 << 31) for n in t.shape) and not is_ptr)
         out[p.name] = BufferInfo(
             name=p.name, dtype=dt, rank=len(strides),
             unit_last=bool(strides) and strides[-1] == 1,
             stride_div=tuple(_pow2_div(s, 16) for s in strides),
-            base_align=_pow2_div(t.data_ptr(), 256) if t.data_ptr() else 256,
-            writable=writable, is_ptr=is_ptr)
+            base_align=base_align, writable=writable, is_ptr=is_ptr, tma_ok=tma_ok)
     return out
 
 
@@ -201,6 +205,27 @@ def preflight(entry: Compiled, context) -> dict:
             "performance_only": ["registers_per_thread", "spill_count"]}
 
 
+_tmap_cache = {}
+
+
+def _tensor_map(t, info):
+    """TMA descriptor of tensor ``t`` for a generated kernel's box (innermost
+    dimension first; SWIZZLE_128B; out-of-bounds elements read as zero)."""
+    shape, strides = tuple(t.shape), tuple(t.stride())
+    key = (t.data_ptr(), shape, strides, tuple(info["box"]), info["swizzle"], info["dtype"])
+    tm = _tmap_cache.get(key)
+    if tm is None:
+        es = t.element_size()
+        dims = list(reversed(shape))
+        sb = [strides[i] * es for i in reversed(range(len(shape) - 1))]
+        tm = native.encode_tensor_map(info["dtype"], t.data_ptr(), dims, sb, info["box"],
+                                      info["swizzle"])
+        if len(_tmap_cache) > 4096:
+            _tmap_cache.clear()
+        _tmap_cache[key] = tm
+    return tm
+
+
 def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word):
     args = []
     for kind, name, ct in entry.spec.params:
@@ -227,7 +252,7 @@ def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word
         elif kind == "err":
             args.append(ctypes.c_uint64(err_word.data_ptr()))
         elif kind == "tensormap":
-            args.append(name)   # prepared TensorMap object
+            args.append(_tensor_map(tensors[ct["buffer"]], ct))
         else:
             raise AssertionError(kind)
     return args

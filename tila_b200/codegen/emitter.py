@@ -43,6 +43,7 @@ from .._reference import tila
 from . import dtypes as DT
 from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_predicate,
                       source_slot_map)
+from .mma import MmaMixin
 
 T_ = tila.tir
 TY = tila.types
@@ -74,6 +75,7 @@ class Val:
     tmem_col: int = 0         # tmem: column offset of the accumulator
     ptr: tuple = None         # ptr: (param name, offset Val)
     zero: bool = False        # func known to be all zeros
+    smem: object = None       # smem: the shared-memory operand (TMA-loaded tile)
     const: object = None      # compile-time known python value (scalars)
 
     @property
@@ -92,10 +94,11 @@ class BufferInfo:
     base_align: int            # largest power of two (<= 256) dividing the base address
     writable: bool
     is_ptr: bool = False
+    tma_ok: bool = False       # f16, unit last stride, 16-byte aligned base and strides
 
     def key(self):
         return (self.name, self.dtype.name, self.rank, self.unit_last, self.stride_div,
-                self.base_align, self.writable, self.is_ptr)
+                self.base_align, self.writable, self.is_ptr, self.tma_ok)
 
 
 @dataclass
@@ -159,7 +162,7 @@ class _Smem:
 # the emitter
 # ---------------------------------------------------------------------------
 
-class KernelEmitter:
+class KernelEmitter(MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
@@ -438,7 +441,7 @@ class KernelEmitter:
         name = self.fresh("acc")
         n = layout.nreg
         self.emit(f"float {name}[{n}];")
-        col = f"tila_tmem + {v.tmem_col}" + (f" + (tid >> 7) * {layout.cpg}" if layout.groups > 1 else "")
+        col = f"tila_tmem + ({v.tmem_col})" + (f" + (tid >> 7) * {layout.cpg}" if layout.groups > 1 else "")
         self.emit(f"tila::tc_fence_after();")
         self.emit(f"tila::tmem_load_row<{n}>({col} + ((tid & 96u) << 16), {name});")
         return Val("reg", v.dt, v.shape, name=name, layout=layout)
@@ -1244,74 +1247,7 @@ class KernelEmitter:
     def e_TAtomicAdd(self, x):
         self.fail("atomic_add is not supported by the B200 backend yet", x.line)
 
-    # -- dot (tcgen05) -------------------------------------------------------
-
-    def e_TDot(self, x):
-        dt, shape, _ = self.vt_info(x.vt)
-        a = self.value(x.a)
-        b = self.value(x.b)
-        acc = self.value(x.acc) if x.acc is not None else None
-        M, K = a.shape
-        K2, N = b.shape
-        if K != K2 or (M, N) != tuple(shape):
-            self.fail("dot shape mismatch")
-        if M > 128:
-            self.fail("dot with more than 128 rows is not supported yet")
-        if N > 256:
-            self.fail("dot with more than 256 columns is not supported yet")
-        Npad = max(16, N)
-        if Npad % 16:
-            self.fail("dot N must be a multiple of 16 or smaller than 16")
-        self.uses_mma = True
-        self.uses_tmem = True
-        cols = _pow2_at_least(max(32, Npad))
-        self.tmem_cols = max(self.tmem_cols, cols)
-        # stage operands: A (M x K) K-major, B as N x K K-major
-        a_off = self.smem.alloc(128 * K * 2, 1024)
-        b_off = self.smem.alloc(Npad * K * 2, 1024)
-        self._stage_operand(a, a_off, K, transpose=False)
-        self._stage_operand(b, b_off, K, transpose=True)
-        # accumulator input
-        accumulate = "0"
-        col = 0
-        if acc is not None and not (acc.kind == "func" and acc.zero):
-            accv = acc if acc.kind != "tmem" else self.tmem_to_reg(acc)
-            if accv.dt.name != "f32":
-                accv = self.coerce(accv, D.f32)
-            lay = TmemRows((M, N), self.T)
-            accv = self.materialize(accv, lay) if not (accv.kind == "reg" and accv.layout == lay) else accv
-            if accv.kind == "scalar":
-                accv = self.materialize_elementwise(D.f32, (M, N), [accv], lambda e: e[0], layout=lay)
-            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {col}"
-                      + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "")
-                      + f" + ((tid & 96u) << 16), {accv.name});")
-            accumulate = "1"
-        idesc = f"tila::idesc_f16_f32(128, {Npad}, 0, 0)"
-        self.emit("tila::fence_proxy_async_smem();")
-        self.emit("tila::tc_fence_before();")
-        self.emit("__syncthreads();")
-        self.emit("tila::tc_fence_after();")
-        self.emit("if (tid == 0) {")
-        self.emit("  #pragma unroll")
-        self.emit(f"  for (int kk = 0; kk < {K // 16}; ++kk) {{")
-        self.emit(f"    const tila::u64 da = tila::smem_desc(tila::smem_u32(tila_smem + {a_off}) + kk * 256, 128, {K * 16}, 0);")
-        self.emit(f"    const tila::u64 db = tila::smem_desc(tila::smem_u32(tila_smem + {b_off}) + kk * 256, 128, {K * 16}, 0);")
-        self.emit(f"    tila::mma_f16_ss(tila_tmem + {col}, da, db, {idesc}, (kk > 0) ? 1u : {accumulate}u);")
-        self.emit("  }")
-        self.emit("  tila::mma_commit(tila_mma_bar);")
-        self.emit("}")
-        self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
-        self.emit("tila_mma_phase ^= 1u;")
-        self.emit("tila::tc_fence_after();")
-        res = Val("tmem", D.f32, (M, N), tmem_col=col)
-        reg = self.tmem_to_reg(res)
-        if dt.name == "f16":
-            reg = self.materialize_elementwise(dt, (M, N), [reg], lambda e: f"tila::round_f16({e[0]})",
-                                               layout=reg.layout)
-        # the TMEM result is consumed; make sure every warp finished reading before
-        # a later dot overwrites it
-        self.emit("tila::tc_fence_before();")
-        return reg
+    # -- dot (tcgen05): see mma.MmaMixin -----------------------------------
 
     def _stage_operand(self, v: Val, off: int, K: int, transpose: bool):
         """Write an f16 operand into shared memory, K-major, no swizzle.
@@ -1360,7 +1296,11 @@ class KernelEmitter:
         m(s)
 
     def s_TAssign(self, s):
-        v = self.value(s.value)
+        v = None
+        if isinstance(s.value, T_.TLoad):
+            v = self.try_tma_load(s.value, assigned_name=s.name)
+        if v is None:
+            v = self.value(s.value)
         if v.kind == "scalar" and v.const is None and not _is_simple(v.expr):
             name = self.fresh(f"s_{s.name}")
             self.emit(f"const {DT.ctype(v.dt)} {name} = {v.expr};")
@@ -1439,6 +1379,8 @@ class KernelEmitter:
         # the loop variable's divisibility (for vector alignment proofs)
         sdiv = _pow2_div(int(start.const)) if start.const is not None else 1
         self._loopvars[s.var] = min(sdiv, _pow2_div(abs(stepv)))
+        if self.try_contraction_loop(s, start, end, stepv, carried):
+            return
         loop_end_vals = None
         # two dry runs reach the fixpoint of the carried layouts
         pre = {n: self.env[n] for n in carried}
@@ -1574,6 +1516,10 @@ class KernelEmitter:
         self._defs = {}
         self._pidnames = set()
         self._loopvars = {}
+        self._need_barrier_init = []
+        self._phase_vars = []
+        self.tmem_scratch_need = 0
+        self._init_mma()
         tk = self.tk
         params = []
         sig = []
@@ -1599,11 +1545,13 @@ class KernelEmitter:
             params.append(("pid_off", ax, "i32"))
         sig.append("tila::u32* __restrict__ tila_err")
         params.append(("err", None, "ptr"))
-        body_lines = self.lines
         self.lines = []
         self.indent = 2
         self.stmts(tk.body)
         body = self.lines
+        for tm in self.tensor_maps:
+            sig.append(f"const __grid_constant__ tila::TensorMap {tm['param']}")
+            params.append(("tensormap", tm["param"], tm))
         out = ['#include "tila_tile.cuh"', ""]
         out.append(f'extern "C" __global__ void __launch_bounds__({self.T}) {self.entry}(')
         out.append(",\n".join("    " + x for x in sig) + ") {")
@@ -1621,13 +1569,29 @@ class KernelEmitter:
         out.append(f"  unsigned char* tila_scratch = tila_smem + {scratch_off};")
         out.append("  (void)tila_scratch; (void)tila_mma_bar; (void)tila_tmem_slot;")
         out.append("  tila::u32 tila_mma_phase = 0; (void)tila_mma_phase;")
+        for v in self._phase_vars:
+            out.append(f"  tila::u32 {v} = 0;")
+        scratch_col = self.tmem_next
+        total_cols = self.tmem_next + self.tmem_scratch_need
         if self.uses_tmem:
-            out.append("  if (tid == 0) { tila::mbar_init(tila_mma_bar, 1); tila::mbar_fence_init(); tila_dead = 0; }")
+            if total_cols > 512:
+                self.fail(f"kernel needs {total_cols} tensor-memory columns (limit 512)")
+            self.tmem_cols = _pow2_at_least(max(32, total_cols))
+        if self.uses_tmem or self._need_barrier_init:
+            inits = " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem + {o}), 1);"
+                             for o in self._need_barrier_init)
+            out.append(f"  if (tid == 0) {{ tila::mbar_init(tila_mma_bar, 1); {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
+            for tm in self.tensor_maps:
+                out.append(f"  if (tid == 0) tila::tma_prefetch_desc(&{tm['param']});")
+        if self.uses_tmem:
             out.append(f"  if (tid < 32) tila::tmem_alloc(tila_tmem_slot, {self.tmem_cols});")
             out.append("  tila::tc_fence_before();")
             out.append("  __syncthreads();")
             out.append("  tila::tc_fence_after();")
             out.append("  const tila::u32 tila_tmem = *tila_tmem_slot;")
+            out.append(f"  const tila::u32 tila_tmem_scratch_col = {scratch_col}; (void)tila_tmem_scratch_col;")
+        elif self._need_barrier_init:
+            out.append("  __syncthreads();")
         out.append("  do {")
         # the planned smem regions were allocated relative to offset 0 of the plan;
         # shift them past the head
@@ -1645,7 +1609,8 @@ class KernelEmitter:
             max_ctas = max(1, 512 // self.tmem_cols)
             floor_bytes = 233472 // (max_ctas + 1) - 1024 + 1
             smem = max(smem, floor_bytes)
-        return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols)
+        return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols,
+                          tensor_maps=list(self.tensor_maps))
 
 
 class _BroadcastView(Layout):
