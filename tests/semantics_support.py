@@ -1,0 +1,137 @@
+"""Small Tila programs that pin down TIR semantics, generated per dtype.
+
+Tila reads a kernel's source with ``inspect.getsource``, so each program is
+written to a module file and imported.  Used by the GPU semantics tests (B200
+against the interpreter) and by the CPU code-generation tests.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import sys
+from pathlib import Path
+
+import tila_b200  # noqa: F401  (installs the backend, makes `tila` importable)
+
+_CACHE = {}
+
+
+def load_source(directory: Path, name: str, source: str):
+    key = (name, source)
+    if key in _CACHE:
+        return _CACHE[key]
+    directory.mkdir(parents=True, exist_ok=True)
+    path = directory / f"{name}.py"
+    path.write_text(source)
+    spec = importlib.util.spec_from_file_location(name, path)
+    module = importlib.util.module_from_spec(spec)
+    sys.modules[name] = module
+    spec.loader.exec_module(module)
+    _CACHE[key] = module.kernel
+    return module.kernel
+
+
+def dot_program(directory, acc="f16"):
+    """out = f32(dot(a, b, acc=c)) on 16x32 @ 32x16 tiles; with an f16
+    accumulator the dot result is rounded to f16 before the widening cast."""
+    return load_source(directory, f"sem_dot_{acc}", f'''import tila as ti
+
+@ti.jit
+def kernel(a: ti.Buffer[ti.f16, (16, 32), ti.ReadOnly],
+           b: ti.Buffer[ti.f16, (32, 16), ti.ReadOnly],
+           c: ti.Buffer[ti.{acc}, (16, 16), ti.ReadOnly],
+           out: ti.Buffer[ti.f32, (16, 16), ti.WriteOnly]):
+    r = ti.arange(0, 16)
+    kk = ti.arange(0, 32)
+    lhs = ti.load(a, (r[:, None], kk[None, :]))
+    rhs = ti.load(b, (kk[:, None], r[None, :]))
+    init = ti.load(c, (r[:, None], r[None, :]))
+    ti.store(out, (r[:, None], r[None, :]), ti.cast[ti.f32](ti.dot(lhs, rhs, acc=init)))
+''')
+
+
+UNARY = {"copy": "v", "exp": "ti.exp(v)", "exp2": "ti.exp2(v)", "neg": "-v",
+         "add1": "v + 1", "exp_widen": "ti.cast[ti.f32](ti.exp(v))",
+         "exp2_widen": "ti.cast[ti.f32](ti.exp2(v))"}
+
+
+def unary_program(directory, dtype, op, out_dtype=None, cast_to=None):
+    """Element-wise program over a length-N vector in 8-wide programs."""
+    out_dtype = out_dtype or dtype
+    expr = f"ti.cast[ti.{cast_to}](v)" if cast_to else UNARY[op]
+    name = f"sem_un_{dtype}_{op}_{out_dtype}_{cast_to}"
+    return load_source(directory, name, f'''import tila as ti
+N = ti.Dim("N")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.{dtype}, (N,), ti.ReadOnly],
+           out: ti.Buffer[ti.{out_dtype}, (N,), ti.WriteOnly]):
+    i = ti.program_id(0) * 8 + ti.arange(0, 8)
+    ok = i < N
+    v = ti.load(x, i, mask=ok)
+    ti.store(out, i, {expr}, mask=ok)
+''')
+
+
+def binary_program(directory, dtype, op):
+    name = f"sem_bin_{dtype}_{op.replace('/', 'div').replace('%', 'mod').replace('*', 'mul').replace('+', 'add').replace('-', 'sub').replace('<', 'shl').replace('>', 'shr').replace('&', 'and').replace('|', 'or').replace('^', 'xor')}"
+    return load_source(directory, name, f'''import tila as ti
+N = ti.Dim("N")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.{dtype}, (N,), ti.ReadOnly],
+           y: ti.Buffer[ti.{dtype}, (N,), ti.ReadOnly],
+           out: ti.Buffer[ti.{dtype}, (N,), ti.WriteOnly]):
+    i = ti.program_id(0) * 32 + ti.arange(0, 32)
+    ok = i < N
+    a = ti.load(x, i, mask=ok)
+    b = ti.load(y, i, mask=ok)
+    ti.store(out, i, a {op} b, mask=ok)
+''')
+
+
+def reduce_program(directory, dtype, op, axis):
+    """Reduce an (R, 64) tile along ``axis`` (rows of 8 x 64 per program)."""
+    name = f"sem_red_{dtype}_{op}_{axis}"
+    if axis == 1:
+        body = f'''    t = ti.load(x, (r[:, None], c[None, :]), mask=(r[:, None] < M) & (c[None, :] < N))
+    red = ti.{op}(t, 1)
+    ti.store(out, (r,), red, mask=r < M)'''
+        out_shape = "(M,)"
+    else:
+        body = f'''    t = ti.load(x, (r[:, None], c[None, :]), mask=(r[:, None] < M) & (c[None, :] < N))
+    red = ti.{op}(t, 0)
+    ti.store(out, (pid, c), red, mask=c < N)'''
+        out_shape = "(G, N)"
+    return load_source(directory, name, f'''import tila as ti
+M = ti.Dim("M")
+N = ti.Dim("N")
+G = ti.Dim("G")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.{dtype}, (M, N), ti.ReadOnly],
+           out: ti.Buffer[ti.{dtype}, {out_shape}, ti.WriteOnly]):
+    pid = ti.program_id(0)
+    r = pid * 8 + ti.arange(0, 8)
+    c = ti.arange(0, 64)
+{body}
+''')
+
+
+def scalar_div_program(directory, dtype, op, lo, hi):
+    """x // d or x % d with a divisor the launch contract bounds away from 0
+    (Tila rejects a data-dependent divisor it cannot prove nonzero)."""
+    tag = "div" if op == "//" else "mod"
+    sign = "neg" if hi < 0 else "pos"
+    return load_source(directory, f"sem_sdiv_{dtype}_{tag}_{sign}", f'''import tila as ti
+N = ti.Dim("N")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.{dtype}, (N,), ti.ReadOnly],
+           out: ti.Buffer[ti.{dtype}, (N,), ti.WriteOnly],
+           d: ti.{dtype} | ti.Range[{lo}, {hi}]):
+    i = ti.program_id(0) * 32 + ti.arange(0, 32)
+    ok = i < N
+    a = ti.load(x, i, mask=ok)
+    ti.store(out, i, a {op} d, mask=ok)
+''')

@@ -73,3 +73,50 @@ def test_tmem_budget_and_occupancy():
     assert cols in (32, 64, 128, 256, 512)
     resident = 233472 // (spec.smem_bytes + 1024)
     assert resident * cols <= 512, "co-resident CTAs could exhaust tensor memory"
+
+
+# -- semantic programs of every dtype lower and compile -----------------------------
+
+def _dev_like(shape, dt):
+    import ml_dtypes  # noqa: F401
+    tmap = dict(f16=torch.float16, bf16=torch.bfloat16, f32=torch.float32, f64=torch.float64,
+                i8=torch.int8, i16=torch.int16, i32=torch.int32, i64=torch.int64, u8=torch.uint8,
+                u16=torch.uint16, u32=torch.uint32, u64=torch.uint64)
+    return torch.zeros(shape, dtype=tmap[dt])
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32", "f64"])
+def test_float_programs_compile(dt, tmp_path):
+    import semantics_support as S
+    for op in ("exp", "exp2", "neg"):
+        k = S.unary_program(tmp_path, dt, op)
+        gen(k, dict(x=_dev_like(40, dt), out=_dev_like(40, dt)))
+    for dst in ("f16", "bf16", "f32", "f64"):
+        k = S.unary_program(tmp_path, dt, "cast", dst, cast_to=dst)
+        gen(k, dict(x=_dev_like(40, dt), out=_dev_like(40, dst)))
+
+
+@pytest.mark.parametrize("dt", ["i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64"])
+def test_integer_programs_compile(dt, tmp_path):
+    import semantics_support as S
+    for op in ("+", "-", "*", "//", "%", "&", "|", "^"):
+        k = S.binary_program(tmp_path, dt, op)
+        gen(k, dict(x=_dev_like(100, dt), y=_dev_like(100, dt), out=_dev_like(100, dt)))
+
+
+@pytest.mark.parametrize("dt", ["f32", "i32"])
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_reduction_programs_compile(dt, op, axis, tmp_path):
+    import semantics_support as S
+    k = S.reduce_program(tmp_path, dt, op, axis)
+    out = _dev_like((24,), dt) if axis == 1 else _dev_like((3, 50), dt)
+    gen(k, dict(x=_dev_like((24, 50), dt), out=out), warps=8)
+
+
+@pytest.mark.parametrize("dt", ["i8", "i32", "u32"])
+def test_scalar_division_programs_compile(dt, tmp_path):
+    import semantics_support as S
+    for op in ("//", "%"):
+        k = S.scalar_div_program(tmp_path, dt, op, 1, 100)
+        gen(k, dict(x=_dev_like(64, dt), out=_dev_like(64, dt)))

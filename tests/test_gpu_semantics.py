@@ -1,0 +1,217 @@
+"""TIR semantics on B200 against the interpreter: dot accumulator rounding,
+transcendental tolerance classes, the float cast matrix, wrapping integer
+arithmetic with floor division, and NaN-propagating reductions.
+
+Known answers and bounds follow the reference's GPU suites
+(tests/test_m3_capabilities.py:15-30, tests/gpu_matrix_gaps.py:82-111,
+tests/gpu_capabilities.py:34-75, tests/gpu_semantics.py).
+"""
+
+from pathlib import Path
+
+import ml_dtypes
+import numpy as np
+import pytest
+import torch
+
+import tila_b200
+import semantics_support as S
+
+pytestmark = pytest.mark.gpu
+
+NP = dict(f16=np.float16, bf16=ml_dtypes.bfloat16, f32=np.float32, f64=np.float64,
+          i8=np.int8, i16=np.int16, i32=np.int32, i64=np.int64,
+          u8=np.uint8, u16=np.uint16, u32=np.uint32, u64=np.uint64)
+TORCH = dict(f16=torch.float16, bf16=torch.bfloat16, f32=torch.float32, f64=torch.float64,
+             i8=torch.int8, i16=torch.int16, i32=torch.int32, i64=torch.int64,
+             u8=torch.uint8, u16=torch.uint16, u32=torch.uint32, u64=torch.uint64)
+KDIR = Path(__file__).resolve().parent / ".kernels"
+
+
+def up(x, dt):
+    if dt == "bf16":
+        return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16).cuda()
+    if x.flags.c_contiguous:
+        return torch.from_numpy(x).cuda()
+    return torch.from_numpy(np.ascontiguousarray(x.T)).cuda().T
+
+
+def down(t):
+    if t.dtype == torch.bfloat16:
+        return t.cpu().view(torch.int16).numpy().view(ml_dtypes.bfloat16)
+    return t.cpu().numpy()
+
+
+def both(kernel, grid, inputs, dts, out_shape, out_dt, warps=4):
+    cpu = np.zeros(out_shape, NP[out_dt])
+    gpu = torch.zeros(out_shape, dtype=TORCH[out_dt], device="cuda")
+    launch = kernel[grid].with_options(num_warps=warps)
+    launch(*inputs, cpu)
+    launch(*(up(x, d) for x, d in zip(inputs, dts)), gpu)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    return cpu, down(gpu)
+
+
+@pytest.mark.parametrize("acc", ["f16", "f32"])
+@pytest.mark.parametrize("case", ["rounding", "random"])
+@pytest.mark.parametrize("strided", [False, True])
+@pytest.mark.parametrize("warps", [4, 8])
+def test_dot_accumulator(acc, case, strided, warps):
+    kernel = S.dot_program(KDIR, acc)
+    rng = np.random.default_rng(306)
+    a = rng.normal(size=(16, 32)).astype(np.float16)
+    b = rng.normal(size=(32, 16)).astype(np.float16)
+    c = rng.normal(size=(16, 16)).astype(NP[acc])
+    if case == "rounding":
+        a[:] = 0
+        b[:] = 0
+        a[:, 0] = 1
+        b[0, :] = np.resize(np.array([2**-11, 3 * 2**-11, -2**-12, 2**-10], np.float16), 16)
+        c[:] = 1
+    if strided:
+        a, b, c = [np.ascontiguousarray(v.T).T for v in (a, b, c)]
+    ref = a.astype(np.float64) @ b.astype(np.float64) + c.astype(np.float64)
+    bound = 33 * np.finfo(np.float32).eps * (np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+                                             + np.abs(c.astype(np.float64)))
+    if acc == "f16":
+        bound += 2**-11 * (np.abs(ref) + bound) + 2**-24
+    cpu, gpu = both(kernel, (1,), [a, b, c], ["f16", "f16", acc], (16, 16), "f32", warps)
+    for out in (cpu, gpu):
+        assert np.all(np.abs(out - ref) <= bound)
+        if case == "rounding":
+            np.testing.assert_array_equal(out, ref.astype(NP[acc]).astype(np.float32))
+        if acc == "f16":
+            np.testing.assert_array_equal(out, out.astype(np.float16).astype(np.float32))
+
+
+SPECIALS = [-4, -1, -0.0, 0.0, 0.125, 0.5, 1, 4, -np.inf, np.inf, np.nan]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32", "f64"])
+@pytest.mark.parametrize("op", ["exp", "exp2"])
+def test_exponentials(dtype, op):
+    kernel = S.unary_program(KDIR, dtype, op)
+    x = np.array(SPECIALS, dtype=NP[dtype])
+    cpu, gpu = both(kernel, (2,), [x], [dtype], x.shape, dtype)
+    ref = getattr(np, op)(x.astype(np.float64))
+    tol = dict(f16=2**-9, bf16=2**-6, f32=2e-6, f64=2e-14)[dtype]
+    for out in (cpu, gpu):
+        np.testing.assert_allclose(out.astype(np.float64), ref, rtol=tol, atol=0, equal_nan=True)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("op", ["exp_widen", "exp2_widen"])
+def test_narrow_exp_rounds_before_widening(dtype, op):
+    kernel = S.unary_program(KDIR, dtype, op, out_dtype="f32")
+    x = np.array([.125, .25, .5, .75, 1, 1.25, 1.5, 2], dtype=NP[dtype])
+    cpu, gpu = both(kernel, (1,), [x], [dtype], (8,), "f32")
+    fn = np.exp if op == "exp_widen" else np.exp2
+    ref = fn(x.astype(np.float32)).astype(NP[dtype]).astype(np.float32)
+    np.testing.assert_array_equal(cpu, ref)
+    np.testing.assert_array_equal(gpu, ref)
+
+
+@pytest.mark.parametrize("src", ["f16", "bf16", "f32", "f64"])
+@pytest.mark.parametrize("dst", ["f16", "bf16", "f32", "f64"])
+def test_float_cast_matrix(src, dst):
+    kernel = S.unary_program(KDIR, src, "cast", dst, cast_to=dst)
+    x = np.array([-np.inf, -3.5, -0.0, 0.0, .125, 1, 1.00390625, 1.00048828125, 65504, np.inf, np.nan],
+                 dtype=NP[src])
+    cpu, gpu = both(kernel, (2,), [x], [src], x.shape, dst)
+    ref = x.astype(NP[dst])
+    for out in (cpu, gpu):
+        np.testing.assert_equal(out.astype(np.float64), ref.astype(np.float64))
+        np.testing.assert_array_equal(np.signbit(out[2:4]), [True, False])
+
+
+INTS = ["i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64"]
+
+
+@pytest.mark.parametrize("dtype", INTS)
+def test_integer_add_wraps(dtype):
+    kernel = S.unary_program(KDIR, dtype, "add1")
+    info = np.iinfo(NP[dtype])
+    x = np.array([info.min, info.min + 1, -1 if info.min < 0 else 1, 0, 1, info.max - 1, info.max,
+                  7, 100], dtype=NP[dtype])
+    bits = info.bits
+    exp = [(int(v) + 1) % (1 << bits) for v in x]
+    if info.min < 0:
+        exp = [v - (1 << bits) if v >= 1 << (bits - 1) else v for v in exp]
+    exp = np.array(exp, dtype=NP[dtype])
+    if dtype == "i64":
+        # the interpreter's own i64 wrap overflows under NumPy 2.x
+        # (numeric.py:56-63); check the GPU against the exact expectation
+        gpu = torch.zeros(x.shape, dtype=torch.int64, device="cuda")
+        kernel[(2,)](up(x, dtype), gpu)
+        np.testing.assert_array_equal(down(gpu), exp)
+        return
+    cpu, gpu = both(kernel, (2,), [x], [dtype], x.shape, dtype)
+    np.testing.assert_array_equal(cpu, exp)
+    np.testing.assert_array_equal(gpu, exp)
+
+
+@pytest.mark.parametrize("dtype", ["i8", "i32", "u16", "u32"])
+@pytest.mark.parametrize("op", ["+", "-", "*", "&", "|", "^"])
+def test_integer_binary_bit_exact(dtype, op):
+    kernel = S.binary_program(KDIR, dtype, op)
+    info = np.iinfo(NP[dtype])
+    rng = np.random.default_rng(307)
+    n = 100
+    x = rng.integers(info.min, info.max, size=n, dtype=NP[dtype], endpoint=True)
+    y = rng.integers(info.min, info.max, size=n, dtype=NP[dtype], endpoint=True)
+    cpu, gpu = both(kernel, (4,), [x, y], [dtype, dtype], (n,), dtype)
+    np.testing.assert_array_equal(gpu, cpu)
+
+
+@pytest.mark.parametrize("dtype", ["i8", "i16", "i32", "u16", "u32"])
+@pytest.mark.parametrize("op", ["//", "%"])
+@pytest.mark.parametrize("sign", [1, -1])
+def test_floor_division_by_scalar(dtype, op, sign):
+    info = np.iinfo(NP[dtype])
+    if sign < 0 and info.min == 0:
+        pytest.skip("unsigned divisors are positive")
+    lo, hi = (1, 100) if sign > 0 else (-100, -1)
+    kernel = S.scalar_div_program(KDIR, dtype, op, lo, hi)
+    rng = np.random.default_rng(309)
+    x = rng.integers(info.min, info.max, size=64, dtype=NP[dtype], endpoint=True)
+    x[:3] = [info.min, info.max, 0]
+    for d in ((7, 1, 64) if sign > 0 else (-7, -1, -64)):
+        c = np.zeros_like(x)
+        g = torch.zeros(x.shape, dtype=TORCH[dtype], device="cuda")
+        kernel[(2,)](x, c, d)
+        kernel[(2,)](up(x, dtype), g, d)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(down(g), c)
+        # Python floor semantics, MIN // -1 wrapping to MIN
+        py = [(int(v) // d if op == "//" else int(v) % d) for v in x]
+        bits = info.bits
+        py = [((v % (1 << bits)) - (1 << bits)) if info.min < 0 and (v % (1 << bits)) >= 1 << (bits - 1)
+              else v % (1 << bits) for v in py]
+        np.testing.assert_array_equal(c, np.array(py, dtype=NP[dtype]))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "i32"])
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_reductions(dtype, op, axis):
+    kernel = S.reduce_program(KDIR, dtype, op, axis)
+    rng = np.random.default_rng(308)
+    m, n = 24, 50
+    if dtype == "f32":
+        x = rng.normal(size=(m, n)).astype(np.float32)
+        x[3, 7] = np.nan
+        x[10, 2] = np.inf
+        x[11, :] = -0.0
+    else:
+        x = rng.integers(-2**31, 2**31 - 1, size=(m, n), dtype=np.int32)
+    out_shape = (m,) if axis == 1 else (m // 8, n)
+    cpu, gpu = both(kernel, (m // 8,), [x], [dtype], out_shape, dtype)
+    if dtype == "f32":
+        if op == "max":
+            np.testing.assert_array_equal(gpu, cpu)       # max is exact, NaN propagates
+        else:
+            np.testing.assert_allclose(gpu, cpu, rtol=1e-5, atol=1e-5, equal_nan=True)
+        assert np.isnan(gpu.reshape(-1)).any()
+    else:
+        np.testing.assert_array_equal(gpu, cpu)           # wrapping integer sum / max
