@@ -105,6 +105,24 @@ int tila_encode_tensor_map(void *tensor_map_out, int dtype, int rank,
                            const uint64_t *strides_bytes, const uint32_t *box,
                            int swizzle, char *log, size_t log_cap);
 
+/* Capacity of the static scratch used by tila_launch_noalloc. */
+#define TILA_NOALLOC_SCRATCH_BYTES 256
+
+/* No counterpart in the reference (its launches allocate through PyTorch).
+ * Same as tila_launch for callers that cannot allocate device memory - code
+ * recording a CUDA graph, hosts whose own pool owns all device memory, loops
+ * that cannot afford cudaMalloc's synchronisation.  args[scratch_arg] (the
+ * kernel's scratch pointer, normally the error word) is replaced by the
+ * address of a file-scope device array of TILA_NOALLOC_SCRATCH_BYTES bytes;
+ * larger scratch_bytes are rejected with TILA_ERR_ARGUMENT.  The first call
+ * on a device looks up that address (issue it before any stream capture).
+ * The array is shared by every call and keeps the previous contents: the
+ * first scratch_bytes are cleared on cfg->stream before the launch, and calls
+ * that overlap on the GPU race on it.  Allocates nothing. */
+int tila_launch_noalloc(void *kernel, const tila_launch_config *cfg, void **args,
+                        int scratch_arg, uint32_t scratch_bytes, char *log,
+                        size_t log_cap);
+
 /* Number of SMs and opt-in shared memory per block of the current device. */
 int tila_device_info(int *sm_count, int *max_smem_optin, int *cc_major,
                      int *cc_minor, char *log, size_t log_cap);

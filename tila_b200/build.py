@@ -25,14 +25,17 @@ CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 
 def build_library(verbose=False) -> Path:
+    """nvcc build of the C-ABI library: the launcher (host C++) and the
+    no-allocation entry point (a .cu with a device array, sm_100a)."""
     out = PKG / "libtila_b200.so"
-    src = PKG / "csrc" / "launcher.cpp"
+    srcs = [PKG / "csrc" / "launcher.cpp", PKG / "csrc" / "noalloc.cu"]
     hdr = ROOT / "include" / "tila_b200.h"
-    if out.exists() and out.stat().st_mtime > max(src.stat().st_mtime, hdr.stat().st_mtime):
+    if out.exists() and out.stat().st_mtime > max([p.stat().st_mtime for p in srcs] + [hdr.stat().st_mtime]):
         return out
-    cmd = ["g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-Wall", f"-I{CUDA / 'include'}",
-           str(src), f"-L{CUDA / 'lib64'}", "-lnvrtc", "-ldl",
-           f"-Wl,-rpath,{CUDA / 'lib64'}", "-o", str(out) + ".tmp"]
+    cmd = [str(CUDA / "bin" / "nvcc"), "-std=c++17", "-O2", "-shared", "-Xcompiler", "-fPIC",
+           "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", f"-I{CUDA / 'include'}",
+           *[str(p) for p in srcs], f"-L{CUDA / 'lib64'}", "-lnvrtc", "-ldl",
+           "-Xlinker", f"-rpath,{CUDA / 'lib64'}", "-o", str(out) + ".tmp"]
     subprocess.run(cmd, check=True, capture_output=not verbose)
     os.replace(str(out) + ".tmp", out)
     return out

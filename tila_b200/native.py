@@ -36,8 +36,11 @@ EXPORTED_SYMBOLS = (
     "tila_nvrtc_compile", "tila_nvrtc_version", "tila_free_buffer", "tila_init",
     "tila_library_load", "tila_library_unload", "tila_kernel_get",
     "tila_kernel_attrs_get", "tila_launch", "tila_encode_tensor_map",
-    "tila_device_info", "tila_status_string",
+    "tila_device_info", "tila_status_string", "tila_launch_noalloc",
 )
+
+#: Capacity of the static scratch behind tila_launch_noalloc (include/tila_b200.h).
+NOALLOC_SCRATCH_BYTES = 256
 
 
 class NativeError(RuntimeError):
@@ -109,6 +112,9 @@ def library() -> ctypes.CDLL:
                                                ctypes.POINTER(ctypes.c_uint32), c_int,
                                                c_char_p, c_size_t]
         lib.tila_device_info.argtypes = [ctypes.POINTER(c_int)] * 4 + [c_char_p, c_size_t]
+        lib.tila_launch_noalloc.argtypes = [c_void_p, ctypes.POINTER(LaunchConfig),
+                                            ctypes.POINTER(c_void_p), c_int, ctypes.c_uint32,
+                                            c_char_p, c_size_t]
         lib.tila_status_string.argtypes = [c_int]
         lib.tila_status_string.restype = c_char_p
         _lib = lib
@@ -242,6 +248,26 @@ class Kernel:
         log = ctypes.create_string_buffer(1024)
         _check(library().tila_launch(self.handle, ctypes.byref(cfg), ptrs, log, len(log)),
                f"launch of {self.name}", log)
+
+    def launch_noalloc(self, grid, block, args, scratch_arg, scratch_bytes, smem_bytes=0,
+                       stream=0):
+        """Launch through tila_launch_noalloc: argument ``scratch_arg`` (the
+        kernel's scratch pointer) is replaced by the library's static device
+        scratch, so this call allocates no device memory.  Returns the C status."""
+        cfg = LaunchConfig()
+        for i in range(3):
+            cfg.grid[i] = grid[i]
+            cfg.block[i] = block[i]
+            cfg.cluster[i] = 1
+        cfg.smem_bytes = smem_bytes
+        cfg.stream = stream
+        ptrs = (ctypes.c_void_p * max(1, len(args)))(
+            *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
+        log = ctypes.create_string_buffer(1024)
+        status = library().tila_launch_noalloc(self.handle, ctypes.byref(cfg), ptrs, scratch_arg,
+                                               scratch_bytes, log, len(log))
+        self.last_log = log.value.decode(errors="replace")
+        return status
 
 
 # CUtensorMapDataType / CUtensorMapSwizzle numbering (cuda.h).
