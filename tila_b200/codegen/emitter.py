@@ -43,7 +43,7 @@ from .._reference import tila
 from . import dtypes as DT
 from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_predicate,
                       source_slot_map)
-from .mma import MmaMixin
+from .mma import AsyncLoopMixin, MmaMixin
 
 T_ = tila.tir
 TY = tila.types
@@ -162,7 +162,7 @@ class _Smem:
 # the emitter
 # ---------------------------------------------------------------------------
 
-class KernelEmitter(MmaMixin):
+class KernelEmitter(AsyncLoopMixin, MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
@@ -189,6 +189,7 @@ class KernelEmitter(MmaMixin):
         self.buffer_params = {b.name: b for b in tk.buffers}
         self.ptr_params = {p.name: p for p in tk.ptr_params}
         self.dot_rows = set()
+        self.actx = None
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -437,6 +438,8 @@ class KernelEmitter(MmaMixin):
     # -- TMEM --------------------------------------------------------------
 
     def tmem_to_reg(self, v: Val) -> Val:
+        if getattr(v, "pending", None) and self.actx is not None:
+            self.emit_acc_wait(v.pending, release=True)
         layout = TmemRows(tuple(v.shape), self.T)
         name = self.fresh("acc")
         n = layout.nreg
@@ -807,8 +810,8 @@ class KernelEmitter(MmaMixin):
                 c = self._owner_cond(lay, r)
                 self.emit(f"if ({c}) {part} = {fold(part, conv(f'{v.name}[{r}]'))};")
         else:
-            self.emit("#pragma unroll")
-            self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) {part} = {fold(part, conv(f'{v.name}[r]'))};")
+            # balanced tree inside the thread (short dependency chains)
+            self.emit(f"{part} = {_tree_fold([conv(f'{v.name}[{r}]') for r in range(lay.nreg)], fold)};")
             if own is not None:
                 self.emit(f"if (!({own})) {part} = {self._identity(op, acc_dt)};")
         return Val("scalar", acc_dt, expr=self._cta_allreduce(part, op, acc_dt))
@@ -872,10 +875,7 @@ class KernelEmitter(MmaMixin):
         self.emit(f"{ct} {name}[{n}];")
         own = owner_predicate(lay)
         for k, g in enumerate(outs):
-            terms = ident
-            for r in g:
-                terms = fold(terms, conv(f"{v.name}[{r}]"))
-            self.emit(f"{name}[{k}] = {terms};")
+            self.emit(f"{name}[{k}] = {_tree_fold([conv(f'{v.name}[{r}]') for r in g], fold)};")
         if own is not None and own != "PER_SLOT":
             self.emit(f"if (!({own})) {{")
             self.emit(f"  #pragma unroll")
@@ -1297,6 +1297,18 @@ class KernelEmitter(MmaMixin):
 
     def s_TAssign(self, s):
         v = None
+        actx = self.actx
+        if actx is not None and s.name in actx.loads:
+            v = self.load_smem_val(actx, s.name)
+            v.smem_name = s.name
+            self.env[s.name] = v
+            return
+        if actx is not None and s.name in actx.accs:
+            if s.value is actx.accs[s.name]["dot"]:
+                self.env[s.name] = self.emit_async_acc_dot(s.value, s.name)
+                return
+            if self.tmem_update_in_place(s.name, s.value):
+                return
         if isinstance(s.value, T_.TLoad):
             v = self.try_tma_load(s.value, assigned_name=s.name)
         if v is None:
@@ -1381,6 +1393,11 @@ class KernelEmitter(MmaMixin):
         self._loopvars[s.var] = min(sdiv, _pow2_div(abs(stepv)))
         if self.try_contraction_loop(s, start, end, stepv, carried):
             return
+        actx = None
+        if self.actx is None:
+            actx = self.try_async_loop_setup(s, start, end, stepv, carried)
+            if actx is not None:
+                carried = [n for n in carried if n not in actx.accs]
         loop_end_vals = None
         # two dry runs reach the fixpoint of the carried layouts
         pre = {n: self.env[n] for n in carried}
@@ -1414,6 +1431,8 @@ class KernelEmitter(MmaMixin):
         self.emit("}")
         for n, st in storage.items():
             self.env[n] = st
+        if actx is not None:
+            self.finish_async_loop(actx)
         self.env.pop(s.var, None)
 
     # -- merge points (loops and runtime ifs) ------------------------------------
@@ -1645,6 +1664,17 @@ class _BroadcastView(Layout):
             if n == 1:
                 out[..., i] = np.where(coords[..., i] >= 0, 0, -1)
         return out, np.zeros_like(owner)
+
+
+def _tree_fold(terms, fold):
+    """Pairwise combination of ``terms`` (depth log2(n))."""
+    terms = list(terms)
+    while len(terms) > 1:
+        nxt = [fold(terms[i], terms[i + 1]) for i in range(0, len(terms) - 1, 2)]
+        if len(terms) % 2:
+            nxt.append(terms[-1])
+        terms = nxt
+    return terms[0]
 
 
 def _affine_map(m):

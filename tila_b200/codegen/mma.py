@@ -207,6 +207,8 @@ class MmaMixin:
         return col
 
     def e_TDot(self, x):
+        if self.actx is not None:
+            self.wait_all_accs(release=True)
         dt, shape, _ = self.vt_info(x.vt)
         a = self.value(x.a)
         b = self.value(x.b)
@@ -282,6 +284,8 @@ class MmaMixin:
         self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
         self.emit("tila_mma_phase ^= 1u;")
         self.emit("tila::tc_fence_after();")
+        if self.actx is not None:
+            self.release_after_sync_dot([a, b])
         from .emitter import Val
         res = Val("tmem", D.f32, (M, N), tmem_col=col)
         reg = self.tmem_to_reg(res)
@@ -475,3 +479,347 @@ class MmaMixin:
     def _scalar(self, dt, expr):
         from .emitter import Val
         return Val("scalar", dt, expr=expr)
+
+
+# ---------------------------------------------------------------------------
+# asynchronous accumulator loops
+# ---------------------------------------------------------------------------
+
+@dataclass
+class AsyncCtx:
+    """Code-generation state of one asynchronous accumulator loop."""
+    loop: object
+    var: str
+    stepv: int
+    end: str
+    loads: dict          # name -> dict(plan, node, base, bar, phase, flag)
+    accs: dict           # name -> dict(col, N, bar, phase, pend, releases)
+    p_col: str = "tila_tmem_scratch_col"
+
+
+class AsyncLoopMixin:
+
+    def try_async_loop_setup(self, s, start, end, stepv, carried):
+        from .pipeline import match_async_loop
+        if stepv <= 0:
+            return None
+
+        def is_tma(ld):
+            plan = self.tma_plan(ld)
+            return plan is not None and plan.outer_extent >= 64
+
+        def is_smem(name):
+            v = self.env.get(name)
+            return v is not None and v.kind == "smem"
+
+        def acc_ok(dot):
+            dt, shape, _ = self.vt_info(dot.vt)
+            return (dt.name == "f32" and len(shape) == 2 and shape[0] == 128 and
+                    shape[1] % 16 == 0 and 16 <= shape[1] <= 256)
+        al = match_async_loop(s, self.pdefs, is_tma, is_smem, carried, acc_ok)
+        if al is None:
+            return None
+        # B operands must be laid out for an N that the instruction accepts
+        for name, dot in al.accs.items():
+            _, (M, N), _ = self.vt_info(dot.vt)
+            bplan = self.tma_plan(al.loads[dot.b.name])
+            if bplan.shape[1] != N:
+                return None
+        self.uses_mma = True
+        self.uses_tmem = True
+        ctx = AsyncCtx(al, s.var, stepv, f"(tila::i64)({end.expr})", {}, {})
+        ctx.body = s.body
+        for name, ld in al.loads.items():
+            plan = self.tma_plan(ld)
+            size = plan.nbox * max(plan.outer_extent, 128) * 128
+            base = self.smem.alloc(size, 1024)
+            bar_off = self.smem.alloc(8, 8)
+            ctx.loads[name] = dict(plan=plan, node=ld, base=str(base),
+                                   bar=f"reinterpret_cast<tila::u64*>(tila_smem + {bar_off})",
+                                   bar_off=bar_off,
+                                   phase=self._tma_state_var(f"tila_ph_{bar_off}"),
+                                   flag=self._tma_state_var(f"tila_w_{bar_off}"))
+        for name, dot in al.accs.items():
+            _, (M, N), _ = self.vt_info(dot.vt)
+            col = self.tmem_alloc_cols(N)
+            bar_off = self.smem.alloc(8, 8)
+            releases = [op.name for op in (dot.a, dot.b)
+                        if isinstance(op, T_.TName) and op.name in al.loads]
+            ctx.accs[name] = dict(col=col, N=N, bar_off=bar_off,
+                                  bar=f"reinterpret_cast<tila::u64*>(tila_smem + {bar_off})",
+                                  phase=self._tma_state_var(f"tila_ph_{bar_off}"),
+                                  pend=self._tma_state_var(f"tila_p_{bar_off}"),
+                                  releases=releases, dot=dot)
+        # TS operands (register P) live in the dot scratch columns
+        for name, dot in al.accs.items():
+            if isinstance(dot.a, T_.TCast):
+                K = self.vt_info(dot.a.vt)[1][1]
+                self.tmem_scratch_need = max(self.tmem_scratch_need, K // 2)
+        # prologue: accumulators into TMEM, barriers, first copies
+        from .emitter import Val
+        for name, a in ctx.accs.items():
+            pre = self.env[name]
+            lay = TmemRows((128, a["N"]), self.T)
+            if pre.kind == "tmem":
+                pre = self.tmem_to_reg(pre)
+            if pre.dt.name != "f32":
+                pre = self.coerce(pre, D.f32)
+            if pre.kind == "scalar":
+                pre = self.materialize_elementwise(D.f32, (128, a["N"]), [pre], lambda e: e[0], layout=lay)
+            pre = self.materialize(pre, lay)
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {a['col']}"
+                      + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "")
+                      + f" + ((tid & 96u) << 16), {pre.name});")
+        self.emit(f"// asynchronous accumulator loop over {s.var}: TMEM accumulators "
+                  f"{', '.join(ctx.accs)}; copies one iteration ahead: {', '.join(ctx.loads)}")
+        inits = " ".join(f"tila::mbar_init({x['bar']}, 1);" for x in list(ctx.loads.values()) + list(ctx.accs.values()))
+        self.emit(f"if (tid == 0) {{ {inits} tila::mbar_fence_init(); }}")
+        for x in ctx.loads.values():
+            self.emit(f"{x['phase']} = 0u; {x['flag']} = 1u;")
+        for x in ctx.accs.values():
+            self.emit(f"{x['phase']} = 0u; {x['pend']} = 0u;")
+        self.emit("tila::tc_fence_before();")
+        self.emit("__syncthreads();")
+        self.emit("tila::tc_fence_after();")
+        self.emit(f"if ((tila::i64)({start.expr}) < {ctx.end}) {{")
+        self.indent += 1
+        self._emit_loop_copies(ctx, list(ctx.loads), f"(tila::i64)({start.expr})")
+        self.indent -= 1
+        self.emit("}")
+        for name, a in ctx.accs.items():
+            v = Val("tmem", D.f32, (128, a["N"]), tmem_col=str(a["col"]))
+            self.env[name] = v
+        self.actx = ctx
+        return ctx
+
+    def _functional_prefix(self, ctx, loop_value):
+        """Bind the loop variable to ``loop_value`` and evaluate the body's
+        pure index assignments: no loads, dots, reductions or transcendental
+        math, and reading only the loop variable, Consts, scalars, names set
+        before the loop and earlier pure assignments."""
+        from .emitter import Val
+        from .pipeline import _walk
+        assigned = {st.name for st in ctx.body if isinstance(st, T_.TAssign)}
+        pure_names = set()
+
+        def pure(node):
+            ok = [True]
+
+            def chk(n):
+                if isinstance(n, (T_.TLoad, T_.TDot, T_.TReduce, T_.TAtomicAdd)) or \
+                        (isinstance(n, T_.TUna) and n.op in ("exp", "exp2")):
+                    ok[0] = False
+                elif isinstance(n, T_.TName) and n.name != ctx.var and n.name in assigned \
+                        and n.name not in pure_names:
+                    ok[0] = False
+            _walk(node, chk)
+            return ok[0]
+        self.env[ctx.var] = Val("scalar", D.i32, expr=f"((tila::i32)({loop_value}))")
+        for st in ctx.body:
+            if isinstance(st, T_.TAssign) and st.name not in ctx.loads and st.name not in ctx.accs \
+                    and st.name not in pure_names and pure(st.value):
+                self.env[st.name] = self.value(st.value)
+                pure_names.add(st.name)
+
+    def _emit_loop_copies(self, ctx, names, iter_value):
+        """tid 0 issues the TMA copies of ``names`` for loop value ``iter_value``;
+        every thread marks them not yet waited for."""
+        if not names:
+            return
+        saved = dict(self.env)
+        self.emit("{")
+        self.indent += 1
+        lv = self.fresh(f"s_{ctx.var}")
+        self.emit(f"const tila::i32 {lv} = (tila::i32)({iter_value});")
+        self._functional_prefix(ctx, lv)
+        for n in names:
+            self.emit(f"{ctx.loads[n]['flag']} = 0u;")
+        self.emit("if (tid == 0) {")
+        self.indent += 1
+        for n in names:
+            x = ctx.loads[n]
+            coords = [self.value(c) for c in x["node"].coords]
+            self.emit(f"tila::mbar_arrive_expect_tx({x['bar']}, {x['plan'].bytes}u);")
+            self._emit_tma(x["plan"], self._tma_coords(x["plan"], coords), x["base"], x["bar"])
+        self.indent -= 1
+        self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+        self.env = saved
+
+    def load_smem_val(self, ctx, name):
+        x = ctx.loads[name]
+        dt, shape, _ = self.vt_info(x["node"].vt)
+        return self._smem_val(dt, shape, SmemOperand(x["plan"], x["base"], x["bar"], x["phase"], x["flag"]))
+
+    def emit_acc_wait(self, name, release=True):
+        ctx = self.actx
+        a = ctx.accs[name]
+        self.emit(f"if ({a['pend']}) {{")
+        self.indent += 1
+        self.emit(f"tila::mbar_wait({a['bar']}, {a['phase']}, tila_err, __LINE__, &tila_dead);")
+        self.emit(f"{a['phase']} ^= 1u; {a['pend']} = 0u;")
+        self.emit("tila::tc_fence_after();")
+        if release and a["releases"]:
+            # the MMA that read these buffers is done: copy the current iteration's tiles
+            cur = self.env[ctx.var].expr
+            self._emit_loop_copies(ctx, a["releases"], f"(tila::i64)({cur})")
+        self.indent -= 1
+        self.emit("}")
+
+    def wait_all_accs(self, release=True):
+        if self.actx is None:
+            return
+        for name in self.actx.accs:
+            self.emit_acc_wait(name, release)
+
+    def release_after_sync_dot(self, operands):
+        """A synchronous dot completed: copy the next iteration's tiles of its
+        in-loop TMA operands into the freed buffers."""
+        ctx = self.actx
+        if ctx is None:
+            return
+        names = [v.smem_name for v in operands if getattr(v, "smem_name", None) in ctx.loads]
+        if not names:
+            return
+        cur = self.env[ctx.var].expr
+        nxt = f"((tila::i64)({cur}) + {ctx.stepv})"
+        self.emit(f"if ({nxt} < {ctx.end}) {{")
+        self.indent += 1
+        self._emit_loop_copies(ctx, names, nxt)
+        self.indent -= 1
+        self.emit("}")
+
+    def emit_async_acc_dot(self, x, name):
+        """acc = dot(a, b, acc=acc) with acc in TMEM: issue and leave pending."""
+        from .emitter import Val
+        ctx = self.actx
+        a = ctx.accs[name]
+        N = a["N"]
+        # the previous accumulation and any TS operand reader must be finished
+        self.wait_all_accs(release=True)
+        acc = self.env[name]
+        lay = TmemRows((128, N), self.T)
+        if acc.kind != "tmem":
+            accv = acc if acc.dt.name == "f32" else self.coerce(acc, D.f32)
+            accv = self.materialize(accv, lay) if not (accv.kind == "reg" and accv.layout == lay) else accv
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {a['col']}"
+                      + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "")
+                      + f" + ((tid & 96u) << 16), {accv.name});")
+        bv = self.value(x.b)
+        K = bv.shape[0]
+        ts = isinstance(x.a, T_.TCast)
+        if ts:
+            pv = self.value(x.a)                 # f16-rounded register tile
+            play = TmemRows((128, K), self.T)
+            pv = self.materialize(pv, play) if not (pv.kind == "reg" and pv.layout == play) else pv
+            half = play.nreg // 2
+            self.emit("{")
+            self.indent += 1
+            self.emit(f"float pk[{half}];")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float((tila::u32)tila::f2h({pv.name}[2 * c])"
+                      f" | ((tila::u32)tila::f2h({pv.name}[2 * c + 1]) << 16));")
+            goff = f" + (tid >> 7) * {play.cpg // 2}" if play.groups > 1 else ""
+            self.emit(f"tila::tmem_store_row<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
+            self.indent -= 1
+            self.emit("}")
+            adesc = None
+        else:
+            av = self.value(x.a)
+            if av.kind != "smem":
+                self.fail("asynchronous dot needs its A operand in shared or tensor memory")
+        self.emit_smem_wait(bv)
+        if not ts:
+            self.emit_smem_wait(av)
+        self.emit("tila::fence_proxy_async_smem();")
+        self.emit("tila::tc_fence_before();")
+        self.emit("__syncthreads();")
+        self.emit("tila::tc_fence_after();")
+        b_mn = self._operand_desc(bv, "B", 0)[1]
+        self.emit("if (tid == 0) {")
+        self.indent += 1
+        for kk in range(K // 16):
+            db, _ = self._operand_desc(bv, "B", kk)
+            if ts:
+                idesc = f"tila::idesc_f16_f32(128, {N}, 0, {b_mn})"
+                self.emit(f"tila::mma_f16_ts(tila_tmem + {a['col']}, tila_tmem + {ctx.p_col} + {kk * 8}, {db}, {idesc}, 1u);")
+            else:
+                da, a_mn = self._operand_desc(av, "A", kk)
+                idesc = f"tila::idesc_f16_f32(128, {N}, {a_mn}, {b_mn})"
+                self.emit(f"tila::mma_f16_ss(tila_tmem + {a['col']}, {da}, {db}, {idesc}, 1u);")
+        self.emit(f"tila::mma_commit({a['bar']});")
+        self.indent -= 1
+        self.emit("}")
+        self.emit(f"{a['pend']} = 1u;")
+        v = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
+        v.pending = name
+        return v
+
+    def tmem_update_in_place(self, name, node):
+        """acc = acc <op> rowvec (or scalar): update the TMEM accumulator in
+        32-column chunks instead of materialising the whole tile."""
+        if not isinstance(node, T_.TBin) or node.op not in ("*", "+", "-", "/"):
+            return False
+        l, r = node.left, node.right
+        if isinstance(l, T_.TName) and l.name == name:
+            other_node, acc_left = r, True
+        elif isinstance(r, T_.TName) and r.name == name:
+            other_node, acc_left = l, False
+        else:
+            return False
+        a = self.actx.accs[name]
+        N = a["N"]
+        dt, shape, _ = self.vt_info(node.vt)
+        if dt.name != "f32" or tuple(shape) != (128, N):
+            return False
+        other = self.value(other_node)
+        if other.kind == "tmem" or other.kind == "smem":
+            return False
+        if other.shape and other.shape[-1] != 1:
+            return False
+        if other.dt.name != "f32":
+            other = self.coerce(other, D.f32)
+        lay = TmemRows((128, N), self.T)
+        if other.kind == "reg":
+            m = self.slot_map(other.layout, lay, (128, N))
+            if m is None:
+                other = self.convert(other, lay, (128, N))
+                m = self.slot_map(other.layout, lay, (128, N))
+            if len(set(m)) != 1:
+                return False
+            oexpr = f"{other.name}[{m[0]}]"
+        elif other.kind == "func":
+            oexpr = other.fn(("((tid & 127))", "0") if len(other.shape) == 2 else ("0",))
+        else:
+            oexpr = other.expr
+        mk = self._bin_maker(node.op, D.f32, D.f32)
+        self.wait_all_accs(release=True)
+        chunk = 32 if lay.cpg % 32 == 0 else 8
+        base = f"tila_tmem + {a['col']}" + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "") + " + ((tid & 96u) << 16)"
+        self.emit("{ // in-place TMEM update of " + name)
+        self.indent += 1
+        self.emit(f"const float o_ = {oexpr};")
+        self.emit(f"for (int ch = 0; ch < {lay.cpg}; ch += {chunk}) {{")
+        self.indent += 1
+        self.emit(f"float t_[{chunk}];")
+        self.emit(f"tila::tmem_load_row<{chunk}>({base} + ch, t_);")
+        self.emit("#pragma unroll")
+        e = mk(["t_[j]", "o_"] if acc_left else ["o_", "t_[j]"])
+        self.emit(f"for (int j = 0; j < {chunk}; ++j) t_[j] = {e};")
+        self.emit(f"tila::tmem_store_row<{chunk}>({base} + ch, t_);")
+        self.indent -= 1
+        self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+        from .emitter import Val
+        self.env[name] = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
+        return True
+
+    def finish_async_loop(self, ctx):
+        from .emitter import Val
+        for name in ctx.accs:
+            self.emit_acc_wait(name, release=False)
+        for name, a in ctx.accs.items():
+            self.env[name] = Val("tmem", D.f32, (128, a["N"]), tmem_col=str(a["col"]))
+        self.actx = None

@@ -405,3 +405,104 @@ def match_contraction_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried)
             if name in reads(s.value):
                 return None
     return ContractionLoop(dots, loads, functional)
+
+
+# ---------------------------------------------------------------------------
+# asynchronous accumulator loops (online-softmax attention and relatives)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class AsyncLoop:
+    """A loop whose carried accumulators stay in tensor memory.
+
+    ``accs``: accumulator name -> its ``acc = dot(x, y, acc=acc)`` node; the
+    dot runs asynchronously and is waited for lazily.  ``loads``: in-body
+    loads that feed only dots and are TMA-copyable; each is copied one
+    iteration ahead, as soon as the MMA that read it has completed.
+    """
+    accs: dict
+    loads: dict
+
+
+def _walk(node, fn):
+    fn(node)
+    if hasattr(node, "__dataclass_fields__"):
+        for f in node.__dataclass_fields__:
+            if f in ("vt", "definition", "effect"):
+                continue
+            x = getattr(node, f)
+            if isinstance(x, list):
+                for y in x:
+                    _walk(y, fn)
+            elif hasattr(x, "__dataclass_fields__"):
+                _walk(x, fn)
+
+
+def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_shape_ok):
+    body = loop.body
+    if not body or any(not isinstance(s, T_.TAssign) for s in body):
+        return None
+    assigned = {}
+    for s in body:
+        assigned.setdefault(s.name, []).append(s.value)
+    loads = {}
+    for name, vals in assigned.items():
+        if len(vals) == 1 and isinstance(vals[0], T_.TLoad) and is_tma_load(vals[0]):
+            loads[name] = vals[0]
+    # how every name is used inside the body
+    uses = {}
+
+    def record(parent):
+        if not hasattr(parent, "__dataclass_fields__"):
+            return
+        for f in parent.__dataclass_fields__:
+            if f in ("vt", "definition", "effect"):
+                continue
+            x = getattr(parent, f)
+            for y in (x if isinstance(x, list) else [x]):
+                if isinstance(y, T_.TName):
+                    uses.setdefault(y.name, []).append((type(parent).__name__, f))
+    for s in body:
+        _walk(s.value, record)
+    for name in list(loads):
+        if not uses.get(name) or any(p != "TDot" or f not in ("a", "b") for p, f in uses[name]):
+            del loads[name]
+    accs = {}
+    for s in body:
+        v = s.value
+        if isinstance(v, T_.TDot) and isinstance(v.acc, T_.TName) and v.acc.name == s.name:
+            if s.name not in carried or not acc_shape_ok(v):
+                return None
+            if not (isinstance(v.b, T_.TName) and v.b.name in loads):
+                return None
+            a = v.a
+            ok_a = (isinstance(a, T_.TName) and (a.name in loads or is_smem_name(a.name))) or \
+                (isinstance(a, T_.TCast) and a.dtype.name == "f16" and isinstance(a.operand, T_.TName)
+                 and a.operand.name not in loads)
+            if not ok_a or s.name in accs:
+                return None
+            accs[s.name] = v
+    if not accs:
+        return None
+    # accumulators: besides their dot, only element-wise updates that read them
+    for name in accs:
+        for val in assigned[name]:
+            if isinstance(val, T_.TDot):
+                continue
+            if not isinstance(val, (T_.TBin, T_.TUna, T_.TWhere, T_.TCast)):
+                return None
+        for p, f in uses.get(name, []):
+            if p == "TDot" and f != "acc":
+                return None
+    # the other dots of the body: synchronous, operands in shared memory
+    for s in body:
+        def check(node):
+            if isinstance(node, T_.TDot) and not (isinstance(node.acc, T_.TName) and node.acc.name in accs):
+                for op in (node.a, node.b):
+                    if not (isinstance(op, T_.TName) and (op.name in loads or is_smem_name(op.name))):
+                        raise ValueError
+        try:
+            _walk(s.value, check)
+        except ValueError:
+            return None
+    return AsyncLoop(accs, loads)
