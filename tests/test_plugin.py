@@ -60,3 +60,12 @@ def test_non_sm100_device_is_rejected():
     with pytest.raises(ti.errors.TilaError) as exc:
         plugin.resolve_b200(FakeTorch, Dev())
     assert exc.value.code == "TILA-TARGET-007"
+
+
+def test_resource_failures_produce_the_reference_artifact(tmp_path, monkeypatch):
+    from tila_b200 import backend
+    monkeypatch.setenv("TILA_BACKEND_ARTIFACTS", str(tmp_path))
+    err = backend._failure(RuntimeError("threads"), "resources", "// src", {"kernel": "k"},
+                           resource=("threads", 2048, 1024))
+    assert err.code == "TILA-TARGET-011"
+    assert err.backend_artifact and (tmp_path / err.backend_artifact).exists()

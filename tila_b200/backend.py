@@ -18,8 +18,12 @@ import threading
 from contextlib import contextmanager
 from dataclasses import dataclass, asdict
 
+import importlib
+
 from ._reference import tila
 from . import native
+
+_tila_backend = importlib.import_module("tila.backend")
 from .codegen.emitter import BufferInfo, CodegenError, KernelEmitter
 
 TilaError = tila.errors.TilaError
@@ -180,9 +184,9 @@ def _failure(exc, phase, source, context, resource=None):
             pass
         r = _Res(str(exc))
         r.name, r.required, r.limit = resource
-        return tila.backend.failure(r, phase="resources", source=source, source_map={},
+        return _tila_backend.failure(r, phase="resources", source=source, source_map={},
                                     context=context, resource=True)
-    return tila.backend.failure(exc, phase=phase, source=source, source_map={}, context=context)
+    return _tila_backend.failure(exc, phase=phase, source=source, source_map={}, context=context)
 
 
 def preflight(entry: Compiled, context) -> dict:
@@ -226,7 +230,7 @@ def _tensor_map(t, info):
     return tm
 
 
-def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word):
+def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word, launch_grid):
     args = []
     for kind, name, ct in entry.spec.params:
         if kind in ("buffer", "ptr"):
@@ -287,7 +291,7 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
             launch_grid[ax] = hi - lo
             pid_off[ax] = lo
         err = _error_word(device)
-        args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err)
+        args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err, launch_grid)
         stream = torch.cuda.current_stream(device).cuda_stream
         record = LaunchRecord(entry, tuple(launch_grid), args, device)
         jf._b200_last_launch = record

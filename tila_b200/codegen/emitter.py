@@ -190,6 +190,7 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         self.ptr_params = {p.name: p for p in tk.ptr_params}
         self.dot_rows = set()
         self.actx = None
+        self._guard_mode = None
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -223,6 +224,40 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         if isinstance(vt, TY.ConstT):
             return vt.dtype, (), False
         self.fail(f"unsupported value type {vt!r}")
+
+    SMALL_PROGRAM_TILE = 2048
+
+    def _small_program(self):
+        """Programs without tensor-core work whose tiles have at most 2048
+        elements run with 64 threads: more programs resident per SM and
+        shorter CTA-wide reductions (measured best for row reductions)."""
+        if self.dot_rows or self.T != 128:
+            return False
+        ok = [True]
+
+        def visit(node):
+            if isinstance(node, (T_.TDot, T_.TAtomicAdd)):
+                ok[0] = False
+            vt = getattr(node, "vt", None)
+            if isinstance(vt, (TY.BlockT, TY.MaskT)):
+                try:
+                    n = int(np.prod(self.dims(vt)))
+                except Exception:
+                    ok[0] = False
+                    return
+                if n > self.SMALL_PROGRAM_TILE:
+                    ok[0] = False
+            if dataclasses.is_dataclass(node):
+                for f in dataclasses.fields(node):
+                    if f.name in ("vt", "definition", "effect"):
+                        continue
+                    v = getattr(node, f.name)
+                    for x in (v if isinstance(v, list) else [v]):
+                        if dataclasses.is_dataclass(x):
+                            visit(x)
+        for st in self.tk.body:
+            visit(st)
+        return ok[0]
 
     def _scan_dots(self, stmts):
         """Row counts of dot results: 2-D tiles with that many rows default to
@@ -620,6 +655,9 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
             fn = "exp" if op == "exp" else "exp2"
             if dt.name == "f64":
                 mk = lambda e: f"{fn}((double)({e[0]}))"
+            elif op == "exp2":
+                # ex2.approx.f32: relative error <= 2^-22.5, subnormals kept
+                mk = lambda e: DT.round_to(dt, f"tila::exp2_fast((float)({e[0]}))")
             else:
                 mk = lambda e: DT.round_to(dt, f"{fn}f((float)({e[0]}))")
             if v.kind == "scalar":
@@ -673,6 +711,14 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
             return self.combine(D.bool_, shape, [l, r], mk)
         l = self.coerce(l, odt)
         r = self.coerce(r, odt)
+        mode = getattr(self, "_guard_mode", None)
+        if mode and op in ("<", "<=") and shape and r.kind == "scalar" and l.kind == "func":
+            g = self._bound_guard(x, l, r, op, shape)
+            if g is not None:
+                if mode == "collect":
+                    self._guards.append(g)
+                elif g in self._guard_set:
+                    return Val("func", D.bool_, tuple(shape), fn=lambda idx: "true")
         mk = self._bin_maker(op, odt, dt)
         return self.combine(dt, shape, [l, r], mk)
 
@@ -1425,8 +1471,11 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         for n, st in storage.items():
             self.env[n] = st
         self.env[s.var] = Val("scalar", D.i32, expr=lv)
-        self.stmts(s.body)
-        self._assign_merged(storage)
+        if actx is not None:
+            self._emit_versioned_body(s.body, storage)
+        else:
+            self.stmts(s.body)
+            self._assign_merged(storage)
         self.indent -= 1
         self.emit("}")
         for n, st in storage.items():
@@ -1434,6 +1483,57 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         if actx is not None:
             self.finish_async_loop(actx)
         self.env.pop(s.var, None)
+
+    # -- loop-body versioning on tile bound checks ---------------------------------
+
+    def _emit_versioned_body(self, body, storage):
+        """Emit the loop body twice: a general version and one in which every
+        bound comparison ``uniform + arange < uniform`` of the body is known
+        to hold on the whole tile, selected by one uniform guard per
+        iteration (interior tiles skip their mask arithmetic)."""
+        env0, cc0 = dict(self.env), dict(self.conv_cache)
+        outer = self.lines
+        self.lines = []
+        self._guard_mode, self._guards = "collect", []
+        self.stmts(body)
+        self._assign_merged(storage)
+        general = self.lines
+        guards = list(dict.fromkeys(self._guards))
+        if not guards:
+            self._guard_mode = None
+            self.lines = outer + general
+            return
+        self.env, self.conv_cache = dict(env0), dict(cc0)
+        self.lines = []
+        self._guard_mode, self._guard_set = "fast", set(guards)
+        self.stmts(body)
+        self._assign_merged(storage)
+        fast = self.lines
+        self._guard_mode = None
+        self.lines = outer
+        self.env, self.conv_cache = env0, cc0
+        self.emit(f"if ({' && '.join(guards)}) {{  // every tile bound check holds")
+        self.lines.extend(fast)
+        self.emit("} else {")
+        self.lines.extend(general)
+        self.emit("}")
+
+    def _bound_guard(self, x, l, r, op, shape):
+        """Uniform condition under which ``l op r`` is true on the whole tile
+        (l = uniform + arange along one dim, r uniform), or None."""
+        from .pipeline import tile_affinity
+        uni = self._uniform_names()
+        if tile_affinity(x.right, self.pdefs, self.consts, uni) != ():
+            return None
+        aff = tile_affinity(x.left, self.pdefs, self.consts, uni)
+        if aff is None or sorted(aff) != sorted((1,) + (0,) * (len(aff) - 1)):
+            return None
+        dim = aff.index(1)
+        if len(l.shape) != len(aff) or l.kind != "func":
+            return None
+        extent = l.shape[dim]
+        base = l.fn(("0",) * len(l.shape))
+        return f"((tila::i64)({base}) + {extent - 1} {op} (tila::i64)({r.expr}))"
 
     # -- merge points (loops and runtime ifs) ------------------------------------
 
@@ -1539,6 +1639,8 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         self._phase_vars = []
         self.tmem_scratch_need = 0
         self._init_mma()
+        if self._small_program():
+            self.T = 64
         tk = self.tk
         params = []
         sig = []

@@ -615,11 +615,13 @@ class AsyncLoopMixin:
             _walk(node, chk)
             return ok[0]
         self.env[ctx.var] = Val("scalar", D.i32, expr=f"((tila::i32)({loop_value}))")
+        saved_mode, self._guard_mode = self._guard_mode, None
         for st in ctx.body:
             if isinstance(st, T_.TAssign) and st.name not in ctx.loads and st.name not in ctx.accs \
                     and st.name not in pure_names and pure(st.value):
                 self.env[st.name] = self.value(st.value)
                 pure_names.add(st.name)
+        self._guard_mode = saved_mode
 
     def _emit_loop_copies(self, ctx, names, iter_value):
         """tid 0 issues the TMA copies of ``names`` for loop value ``iter_value``;
@@ -710,7 +712,10 @@ class AsyncLoopMixin:
         K = bv.shape[0]
         ts = isinstance(x.a, T_.TCast)
         if ts:
-            pv = self.value(x.a)                 # f16-rounded register tile
+            # cast[f16](R): round and pack pairs straight from R (one cvt per pair)
+            pv = self.value(x.a.operand)
+            if pv.dt.name not in ("f32", "f16"):
+                pv = self.coerce(pv, D.f32)
             play = TmemRows((128, K), self.T)
             pv = self.materialize(pv, play) if not (pv.kind == "reg" and pv.layout == play) else pv
             half = play.nreg // 2
@@ -718,8 +723,7 @@ class AsyncLoopMixin:
             self.indent += 1
             self.emit(f"float pk[{half}];")
             self.emit("#pragma unroll")
-            self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float((tila::u32)tila::f2h({pv.name}[2 * c])"
-                      f" | ((tila::u32)tila::f2h({pv.name}[2 * c + 1]) << 16));")
+            self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float(tila::pack_f16x2({pv.name}[2 * c], {pv.name}[2 * c + 1]));")
             goff = f" + (tid >> 7) * {play.cpg // 2}" if play.groups > 1 else ""
             self.emit(f"tila::tmem_store_row<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
             self.indent -= 1

@@ -84,6 +84,21 @@ __device__ __forceinline__ u16 d2bf(double d) {
   }
   return f2bf(f);
 }
+// Two f32 -> one f16x2 word (lo in bits 0..15), each rounded to nearest even.
+__device__ __forceinline__ u32 pack_f16x2(float lo, float hi) {
+  u32 r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x with the hardware approximation: maximum relative error 2^-22.5,
+// subnormal results supported, exp2(-inf) = +0, exp2(+inf) = +inf, NaN -> NaN.
+__device__ __forceinline__ float exp2_fast(float x) {
+  float r;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Round an f32 to the nearest f16 / bf16 value and widen back (the register
 // representation of f16/bf16 tiles is an f32 holding a representable value).
 __device__ __forceinline__ float round_f16(float f) { return h2f(f2h(f)); }
