@@ -37,10 +37,11 @@ def test_softmax_reductions():
 def test_matmul_uses_tma_ring_and_tcgen05():
     t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
     spec = gen(W.tiled_matmul, t, BM=128, BN=128, BK=64)
-    assert "pipelined contraction loop" in spec.source
-    assert "tma_load_2d" in spec.source and "mma_f16_ss" in spec.source
+    # a 2 x 2 block of programs per CTA sharing A and B tiles, N = 256 MMAs
+    assert "2x2 programs per CTA" in spec.source and spec.fuse == {0: 2, 1: 2}
+    assert "tma_load_2d" in spec.source and "idesc_f16_f32(128, 256" in spec.source
     assert len(spec.tensor_maps) == 2
-    assert spec.smem_bytes <= 110 * 1024      # two CTAs per SM
+    assert spec.tmem_cols == 512 and spec.smem_bytes <= 227 * 1024
 
 
 def test_matmul_strided_falls_back_to_register_staging():

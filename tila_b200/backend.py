@@ -253,6 +253,8 @@ def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word
             args.append(ctypes.c_int32(grid[name]))
         elif kind == "pid_off":
             args.append(ctypes.c_int32(pid_off[name]))
+        elif kind == "launch":
+            args.append(ctypes.c_int32(launch_grid[name]))
         elif kind == "err":
             args.append(ctypes.c_uint64(err_word.data_ptr()))
         elif kind == "tensormap":
@@ -293,7 +295,10 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
         err = _error_word(device)
         args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err, launch_grid)
         stream = torch.cuda.current_stream(device).cuda_stream
-        record = LaunchRecord(entry, tuple(launch_grid), args, device)
+        cuda_grid = list(launch_grid)
+        for ax, f in entry.spec.fuse.items():        # CTAs that run blocks of programs
+            cuda_grid[ax] = -(-cuda_grid[ax] // f)
+        record = LaunchRecord(entry, tuple(cuda_grid), args, device, tensors)
         jf._b200_last_launch = record
         try:
             record.launch(stream)
@@ -309,8 +314,11 @@ class LaunchRecord:
     skips Tila's host-side contract checks, so benchmarks can time the kernel
     alone; the tensors it points at must stay alive and unchanged in shape."""
 
-    def __init__(self, entry, grid, args, device):
+    def __init__(self, entry, grid, args, device, tensors=None):
         self.entry, self.grid, self.args, self.device = entry, grid, args, device
+        # the packed arguments are raw device addresses: hold the tensors so
+        # that a replay never touches memory returned to the allocator
+        self.tensors = dict(tensors or {})
 
     def launch(self, stream=None):
         if stream is None:

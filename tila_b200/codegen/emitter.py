@@ -43,6 +43,7 @@ from .._reference import tila
 from . import dtypes as DT
 from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_predicate,
                       source_slot_map)
+from .fused import FusedContractionMixin
 from .mma import AsyncLoopMixin, MmaMixin
 
 T_ = tila.tir
@@ -114,6 +115,7 @@ class KernelSpec:
     tensor_maps: list = field(default_factory=list)
     persistent: bool = False
     grid_override: object = None
+    fuse: dict = field(default_factory=dict)   # {grid axis: programs per CTA along it}
 
 
 # ---------------------------------------------------------------------------
@@ -162,7 +164,7 @@ class _Smem:
 # the emitter
 # ---------------------------------------------------------------------------
 
-class KernelEmitter(AsyncLoopMixin, MmaMixin):
+class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
@@ -191,6 +193,8 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         self.dot_rows = set()
         self.actx = None
         self._guard_mode = None
+        self._pid_expr = {}          # program-id expressions of the program being emitted
+        self.fuse = None             # {axis: programs per CTA} when CTAs run program blocks
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -537,7 +541,7 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         return m(x)
 
     def e_TPid(self, x):
-        return Val("scalar", D.i32, expr=f"pid_{x.axis}")
+        return Val("scalar", D.i32, expr=self._pid_expr.get(x.axis, f"pid_{x.axis}"))
 
     def e_TNumPrograms(self, x):
         return Val("scalar", D.i32, expr=f"nprog_{x.axis}")
@@ -1668,8 +1672,12 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
         params.append(("err", None, "ptr"))
         self.lines = []
         self.indent = 2
-        self.stmts(tk.body)
+        if not self.try_fused_kernel():
+            self.stmts(tk.body)
         body = self.lines
+        for ax in sorted(self.fuse or {}):
+            sig.append(f"tila::i32 launch_{ax}")
+            params.append(("launch", ax, "i32"))
         for tm in self.tensor_maps:
             sig.append(f"const __grid_constant__ tila::TensorMap {tm['param']}")
             params.append(("tensormap", tm["param"], tm))
@@ -1731,7 +1739,7 @@ class KernelEmitter(AsyncLoopMixin, MmaMixin):
             floor_bytes = 233472 // (max_ctas + 1) - 1024 + 1
             smem = max(smem, floor_bytes)
         return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols,
-                          tensor_maps=list(self.tensor_maps))
+                          tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
 
 
 class _BroadcastView(Layout):

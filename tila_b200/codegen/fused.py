@@ -1,0 +1,242 @@
+"""CTA coarsening of contraction kernels: one CTA runs a block of programs.
+
+Tila programs are independent instances of the kernel body, so a CTA may run
+several of them.  For kernels of the form
+
+    <index math>;  for k: acc = dot(load_a, load_b, acc=acc);  <epilogue>
+
+where the A tile depends on one program axis and the B tile on another
+(matmul: A on the row-tile axis, B on the column-tile axis), running a 2 x 2
+block of programs in one CTA loads every A tile once for the two programs
+that share it and every B tile once for the two programs that share it.
+That halves the L2 -> shared-memory operand traffic, which is what bounds a
+128 x 128 tile on B200, and lets two adjacent MN-major B tiles form one
+N = 256 MMA.  Results are those of the individual programs: each program's
+accumulator lives in its own 128 TMEM columns and its epilogue runs with its
+own ``program_id`` values; programs beyond the launched grid store nothing.
+"""
+
+from __future__ import annotations
+
+from .._reference import tila
+from .layouts import TmemRows
+from .pipeline import _walk, canon, match_contraction_loop
+
+T_ = tila.tir
+D = tila.dtypes
+
+FUSE = 2     # programs per CTA along each of the two fused axes
+
+
+def _pure_index(node):
+    ok = [True]
+
+    def chk(n):
+        if isinstance(n, (T_.TLoad, T_.TDot, T_.TReduce, T_.TAtomicAdd)) or \
+                (isinstance(n, T_.TUna) and n.op in ("exp", "exp2")):
+            ok[0] = False
+    _walk(node, chk)
+    return ok[0]
+
+
+def _pid_axes(text):
+    return {ax for ax in range(3) if f"pid{ax}" in text}
+
+
+class FusedContractionMixin:
+
+    def try_fused_kernel(self):
+        """Emit the whole kernel body as a 2 x 2 block of programs per CTA
+        when the kernel is a single pipelined contraction; False otherwise."""
+        body = self.tk.body
+        loops = [i for i, s in enumerate(body) if isinstance(s, T_.TFor)]
+        if len(loops) != 1:
+            return False
+        li = loops[0]
+        loop, prefix, suffix = body[li], body[:li], body[li + 1:]
+        if any(not isinstance(s, T_.TAssign) or not _pure_index(s.value) for s in prefix):
+            return False
+        for s in suffix:
+            bad = [isinstance(s, (T_.TFor, T_.TIf, T_.TReturn))]
+
+            def chk(n):
+                if isinstance(n, (T_.TDot, T_.TFor, T_.TAtomicAdd, T_.TAtomicStmt)):
+                    bad[0] = True
+            _walk(s, chk)
+            if bad[0]:
+                return False
+        for part in (loop.start, loop.end, loop.step):
+            if part is not None and _pid_axes(canon(part, self.pdefs)):
+                return False
+        # bind the prefix once to check that the loop is a plain contraction
+        saved_env, saved_lines = dict(self.env), self.lines
+        self.lines = []
+        for s in prefix:
+            self.s_TAssign(s)
+        self._loopvars[loop.var] = 1
+        carried = sorted(n for n in {s.name for s in loop.body if isinstance(s, T_.TAssign)}
+                         if n in self.env)
+        cl = match_contraction_loop(loop, self.pdefs, lambda ld: self.tma_plan(ld) is not None,
+                                    lambda n: False, carried)
+        self.env, self.lines = saved_env, saved_lines
+        self._loopvars.pop(loop.var, None)
+        if cl is None or len(cl.dots) != 1:
+            return False
+        d = cl.dots[0]
+        if d.a_name not in cl.loads or d.b_name not in cl.loads:
+            return False
+        dt, (M, N), _ = self.vt_info(d.dot.vt)
+        pa, pb = self.tma_plan(cl.loads[d.a_name]), self.tma_plan(cl.loads[d.b_name])
+        if M != 128 or N != 128 or dt.name != "f32" or pa.shape[0] != 128 or pb.shape[1] != 128:
+            return False
+        if any(p.outer_extent > 256 for p in (pa, pb)):
+            return False
+        ya = set().union(*[_pid_axes(canon(c, self.pdefs)) for c in cl.loads[d.a_name].coords])
+        xb = set().union(*[_pid_axes(canon(c, self.pdefs)) for c in cl.loads[d.b_name].coords])
+        if len(ya) != 1 or len(xb) != 1 or ya == xb:
+            return False
+        ay, ax = ya.pop(), xb.pop()
+        if ay == 2 or ax == 2:
+            return False
+        self._emit_fused(prefix, loop, suffix, cl, d, ay, ax, pa, pb, N)
+        return True
+
+    def _emit_fused(self, prefix, loop, suffix, cl, d, ay, ax, pa, pb, N):
+        from .emitter import Val
+        fy = fx = FUSE
+        self.fuse = {ay: fy, ax: fx}
+        self.uses_mma = True
+        self.uses_tmem = True
+        inst = [(i, j) for i in range(fy) for j in range(fx)]
+        for ax_, f in ((ay, fy), (ax, fx)):
+            blk = "xyz"[ax_]
+            for k in range(f):
+                self.emit(f"const tila::i32 pid_{ax_}_{k} = (tila::i32)(blockIdx.{blk} * {f} + {k} + pid_off_{ax_});")
+                self.emit(f"const bool live_{ax_}_{k} = (tila::i32)(blockIdx.{blk} * {f} + {k}) < launch_{ax_};")
+        envs = {}
+        base_env = dict(self.env)
+        for (i, j) in inst:
+            self.env = dict(base_env)
+            self._pid_expr = {ay: f"pid_{ay}_{i}", ax: f"pid_{ax}_{j}"}
+            for s in prefix:
+                self.s_TAssign(s)
+            envs[(i, j)] = dict(self.env)
+        self._pid_expr = {}
+        self.env = dict(envs[(0, 0)])
+        start = self.value(loop.start) if loop.start is not None else Val("scalar", D.i64, expr="0", const=0)
+        end = self.value(loop.end)
+        stepv = int(self.value(loop.step).const)
+        # shared-memory ring: A_0..A_{fy-1} then B_0..B_{fx-1} (B tiles adjacent)
+        a_bytes = (pa.nbox * pa.box_bytes + 1023) // 1024 * 1024
+        b_bytes = (pb.nbox * pb.box_bytes + 1023) // 1024 * 1024
+        stage = fy * a_bytes + fx * b_bytes
+        tx = fy * pa.bytes + fx * pb.bytes
+        S = max(2, min(6, (200 * 1024) // stage))
+        ring = self.smem.alloc(S * stage, 1024)
+        bars = self.smem.alloc(8 * (2 * S + 1), 8)
+        full = lambda e: f"reinterpret_cast<tila::u64*>(tila_smem + {bars} + 8 * ({e}))"
+        empty = lambda e: f"reinterpret_cast<tila::u64*>(tila_smem + {bars} + 8 * ({S} + ({e})))"
+        accbar = f"reinterpret_cast<tila::u64*>(tila_smem + {bars + 16 * S})"
+        cols = {(i, j): self.tmem_alloc_cols(N) for (i, j) in inst}
+        lay = TmemRows((128, N), self.T)
+        for (i, j) in inst:
+            self.env = dict(envs[(i, j)])
+            pre = self.env[d.acc]
+            if pre.dt.name != "f32":
+                pre = self.coerce(pre, D.f32)
+            if pre.kind == "scalar":
+                pre = self.materialize_elementwise(D.f32, (128, N), [pre], lambda e: e[0], layout=lay)
+            pre = self.materialize(pre, lay)
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {cols[(i, j)]} + ((tid & 96u) << 16), {pre.name});")
+        self.emit(f"{{ // {fy}x{fx} programs per CTA: {S}-stage TMA ring, tcgen05.mma into TMEM")
+        self.indent += 1
+        self.emit(f"const tila::i64 cl_start = (tila::i64)({start.expr});")
+        self.emit(f"const tila::i64 cl_end = (tila::i64)({end.expr});")
+        self.emit(f"const tila::i64 cl_n = cl_end > cl_start ? (cl_end - cl_start + {stepv - 1}) / {stepv} : 0;")
+        self.emit("if (tid == 0) {")
+        self.emit(f"  for (int i = 0; i < {2 * S + 1}; ++i) tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem + {bars} + 8 * i), 1);")
+        self.emit("  tila::mbar_fence_init();")
+        self.emit("}")
+        self.emit("tila::tc_fence_before();")
+        self.emit("__syncthreads();")
+        self.emit("tila::tc_fence_after();")
+        self.emit("if (tid == 0) {")
+        self.indent += 1
+
+        def issue(jexpr, st):
+            self.emit("{")
+            self.indent += 1
+            lv = self.fresh(f"s_{loop.var}")
+            self.emit(f"const tila::i32 {lv} = (tila::i32)(cl_start + ({jexpr}) * {stepv});")
+            self.emit(f"tila::mbar_arrive_expect_tx({full(st)}, {tx}u);")
+            for role, plan, nm, count, offset in (("A", pa, d.a_name, fy, 0), ("B", pb, d.b_name, fx, fy * a_bytes)):
+                for k in range(count):
+                    self.env = dict(envs[(k, 0)] if role == "A" else envs[(0, k)])
+                    self.env[loop.var] = Val("scalar", D.i32, expr=lv)
+                    for s2 in cl.functional:
+                        self.s_TAssign(s2)
+                    coords = [self.value(c) for c in cl.loads[nm].coords]
+                    size = a_bytes if role == "A" else b_bytes
+                    self._emit_tma(plan, self._tma_coords(plan, coords),
+                                   f"{ring} + ({st}) * {stage} + {offset + k * size}", full(st))
+            self.indent -= 1
+            self.emit("}")
+
+        self.emit(f"for (tila::i64 j = 0; j < cl_n && j < {S - 1}; ++j) {{")
+        self.indent += 1
+        issue("j", "j")
+        self.indent -= 1
+        self.emit("}")
+        self.emit("for (tila::i64 i = 0; i < cl_n; ++i) {")
+        self.indent += 1
+        self.emit(f"const int st = (int)(i % {S});")
+        self.emit(f"tila::mbar_wait({full('st')}, (tila::u32)((i / {S}) & 1), tila_err, __LINE__, &tila_dead);")
+        self.emit("tila::tc_fence_after();")
+        # adjacent MN-major B tiles form one operand of N = fx * 128
+        merged = pb.inner == 1 and b_bytes == pb.nbox * pb.box_bytes
+        K = pa.shape[1]
+        for i in range(fy):
+            a_val = self._smem_val(D.f16, pa.shape, self._smem_op(pa, f"{ring} + st * {stage} + {i * a_bytes}"))
+            targets = [(0, fx)] if merged else [(j, 1) for j in range(fx)]
+            for j0, nb in targets:
+                b_val = self._smem_val(D.f16, (pb.shape[0], 128 * nb),
+                                       self._smem_op(pb, f"{ring} + st * {stage} + {fy * a_bytes + j0 * b_bytes}"))
+                for kk in range(K // 16):
+                    da, a_mn = self._operand_desc(a_val, "A", kk)
+                    db, b_mn = self._operand_desc(b_val, "B", kk)
+                    idesc = f"tila::idesc_f16_f32(128, {128 * nb}, {a_mn}, {b_mn})"
+                    self.emit(f"tila::mma_f16_ss(tila_tmem + {cols[(i, j0)]}, {da}, {db}, {idesc}, 1u);")
+        self.emit(f"tila::mma_commit({empty('st')});")
+        self.emit(f"const tila::i64 j = i + {S - 1};")
+        self.emit("if (j < cl_n) {")
+        self.indent += 1
+        self.emit(f"const int sj = (int)(j % {S});")
+        self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
+        issue("j", "sj")
+        self.indent -= 1
+        self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+        self.emit(f"tila::mma_commit({accbar});")
+        self.indent -= 1
+        self.emit("}")
+        self.emit(f"tila::mbar_wait({accbar}, 0u, tila_err, __LINE__, &tila_dead);")
+        self.emit("tila::tc_fence_after();")
+        self.indent -= 1
+        self.emit("}")
+        # epilogues, one program at a time (uniform branches: `live` depends on blockIdx)
+        for (i, j) in inst:
+            self.env = dict(envs[(i, j)])
+            self._pid_expr = {ay: f"pid_{ay}_{i}", ax: f"pid_{ax}_{j}"}
+            self.env[d.acc] = Val("tmem", D.f32, (128, N), tmem_col=str(cols[(i, j)]))
+            self.emit(f"if (live_{ay}_{i} && live_{ax}_{j}) {{")
+            self.indent += 1
+            self.conv_cache = {}
+            self.stmts(suffix)
+            self.indent -= 1
+            self.emit("}")
+        self._pid_expr = {}
+
+    def _smem_op(self, plan, base):
+        from .mma import SmemOperand
+        return SmemOperand(plan, base)
