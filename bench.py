@@ -159,9 +159,8 @@ class Case:
         return max(1, min(16, -(-2 * L2_BYTES // max(1, bytes_per_set))))
 
     def _shard(self, total):
-        lo = total * self.rank // self.world
-        hi = total * (self.rank + 1) // self.world
-        return lo, hi
+        from tila_b200.multigpu import shard_range
+        return shard_range(total, self.world, self.rank)
 
     # -- add --
     def _setup_add(self):
@@ -435,18 +434,16 @@ W_ROOF = {"add": "hbm", "softmax": "hbm", "matmul": "tensor", "unfused_attention
 
 
 def _gather(out, case, world, rank, device):
+    """NCCL all-gather of the output rows each rank computed (timed on the
+    device, max over ranks)."""
     import torch
     import torch.distributed as dist
-    ax = case.axis if not getattr(case, "multi_shard", None) else 0
-    lead = out.shape[0]
-    per = lead // world
-    shard = out[rank * per:(rank + 1) * per].contiguous()
-    bufs = [torch.empty_like(shard) for _ in range(world)]
+    from tila_b200.multigpu import gather_leading
     dist.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    dist.all_gather(bufs, shard)
+    gather_leading(out, world, rank)
     e1.record()
     torch.cuda.synchronize(device)
     t = torch.tensor([e0.elapsed_time(e1)], device=device)

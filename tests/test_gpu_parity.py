@@ -152,3 +152,29 @@ def test_unfused_attention(l, d, blk):
     # scores against the f64 product (f16 inputs are exact in f32 products)
     s_ref = np.asarray(q, np.float64) @ np.asarray(k, np.float64).swapaxes(-1, -2) * scale
     assert restate.rel_frobenius(s.cpu().numpy(), s_ref) <= 1e-5
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_program_range_shards_reproduce_the_full_launch(world):
+    """Each rank's share of the grid (run here one after another on one GPU)
+    writes exactly the rows the full launch writes."""
+    from tila_b200.multigpu import shard
+    x = torch.from_numpy(W.softmax_inputs(300, 1000, seed=13)).cuda()
+    full = torch.zeros_like(x)
+    W.row_softmax[(300,)](x, full, BN=1024)
+    parts = torch.full_like(x, float("nan"))
+    for rank in range(world):
+        with shard(0, 300, world, rank):
+            W.row_softmax[(300,)](x, parts, BN=1024)
+    _no_device_errors()
+    assert torch.equal(parts, full)
+    a, b = W.matmul_inputs(384, 256, 128, seed=14)
+    ag, bg = _cuda(a), _cuda(b)
+    c_full = torch.zeros((384, 256), device="cuda")
+    W.tiled_matmul[(3, 2)](ag, bg, c_full, BM=128, BN=128, BK=64)
+    c_part = torch.full_like(c_full, float("nan"))
+    for rank in range(world):
+        with shard(0, 3, world, rank):
+            W.tiled_matmul[(3, 2)](ag, bg, c_part, BM=128, BN=128, BK=64)
+    _no_device_errors()
+    assert torch.equal(c_part, c_full)

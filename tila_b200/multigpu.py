@@ -1,0 +1,59 @@
+"""Multi-GPU launches: split a kernel's program grid across GPUs.
+
+Programs of a Tila kernel are independent, so a launch shards by giving
+each rank (one process per GPU) a contiguous range of ``program_id`` values
+along one grid axis.  Every rank runs the full launch contract and proofs on
+the full grid (``kernel[grid](...)`` unchanged) while only its programs
+execute; ``program_id`` and ``num_programs`` keep their global values.  The
+rows of the output that a rank's programs wrote are then gathered with NCCL
+over NVLink (``torch.distributed``), the only collective on this path.
+"""
+
+from __future__ import annotations
+
+from contextlib import contextmanager
+
+from .backend import program_range
+
+
+def shard_range(total: int, world: int, rank: int):
+    """Contiguous [lo, hi) share of ``total`` programs for ``rank``; the
+    first ``total % world`` ranks get one extra program."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(int(total), world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return lo, hi
+
+
+@contextmanager
+def shard(axis: int, total: int, world: int, rank: int):
+    """Inside the block, B200 launches run only this rank's programs along
+    ``axis`` (of ``total`` programs)."""
+    lo, hi = shard_range(total, world, rank)
+    with program_range(axis, lo, hi):
+        yield lo, hi
+
+
+def gather_leading(out, world: int, rank: int, group=None):
+    """All-gather the leading-dimension shards of ``out`` in place.
+
+    Rank r owns rows ``shard_range(out.shape[0], world, r)`` of ``out``; after
+    the call every rank holds the full tensor.  Shards may differ in size by
+    one row; they are padded to the largest shard for the collective.
+    """
+    import torch
+    import torch.distributed as dist
+    n = out.shape[0]
+    ranges = [shard_range(n, world, r) for r in range(world)]
+    width = max(hi - lo for lo, hi in ranges)
+    lo, hi = ranges[rank]
+    send = torch.zeros((width,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
+    send[: hi - lo] = out[lo:hi]
+    recv = [torch.empty_like(send) for _ in range(world)]
+    dist.all_gather(recv, send, group=group)
+    for r, (a, b) in enumerate(ranges):
+        if r != rank:
+            out[a:b] = recv[r][: b - a]
+    return out
