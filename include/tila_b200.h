@@ -34,6 +34,14 @@ enum {
   TILA_ERR_NO_CONTEXT = -7       /* no current CUDA context on the calling thread */
 };
 
+/* tila_launch_config.flags */
+/* The kernel may be scheduled before the previous kernel in the stream has
+ * finished (programmatic dependent launch): its CTAs become resident while the
+ * previous grid drains and wait (griddepcontrol.wait) before their first
+ * global-memory access.  Every kernel this backend generates performs that
+ * wait; kernels from other sources must not be launched with this flag. */
+#define TILA_LAUNCH_OVERLAP_PREVIOUS 1u
+
 /* Launch geometry.  grid/block/cluster as in cuLaunchKernelEx; cluster all
  * ones (or zeros) means no cluster.  stream is a CUstream (0 = legacy). */
 typedef struct tila_launch_config {
@@ -42,6 +50,8 @@ typedef struct tila_launch_config {
   uint32_t cluster[3];
   uint32_t smem_bytes;
   uint64_t stream;
+  uint32_t flags;      /* TILA_LAUNCH_* bits */
+  uint32_t reserved;   /* must be 0 */
 } tila_launch_config;
 
 /* Compiled resource usage of one kernel (backend.py:77-86 reports the same

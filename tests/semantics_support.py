@@ -135,3 +135,27 @@ def kernel(x: ti.Buffer[ti.{dtype}, (N,), ti.ReadOnly],
     a = ti.load(x, i, mask=ok)
     ti.store(out, i, a {op} d, mask=ok)
 ''')
+
+
+def uniform_div_program(directory, kind):
+    """x / d where every element of a program divides by the same value: a
+    scalar parameter, or the sum of a row of ``y`` (one value per program)."""
+    if kind == "scalar":
+        params = "d: ti.f32"
+        divisor = "d"
+    else:
+        params = "y: ti.Buffer[ti.f32, (G, 256), ti.ReadOnly]"
+        divisor = "ti.sum(ti.load(y, (pid, ti.arange(0, 256))), 0)"
+    return load_source(directory, f"sem_udiv_{kind}", f'''import tila as ti
+N = ti.Dim("N")
+G = ti.Dim("G")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.f32, (N,), ti.ReadOnly],
+           out: ti.Buffer[ti.f32, (N,), ti.WriteOnly],
+           {params}):
+    pid = ti.program_id(0)
+    i = pid * 1024 + ti.arange(0, 1024)
+    ok = i < N
+    ti.store(out, i, ti.load(x, i, mask=ok) / {divisor}, mask=ok)
+''')

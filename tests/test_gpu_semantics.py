@@ -215,3 +215,79 @@ def test_reductions(dtype, op, axis):
         assert np.isnan(gpu.reshape(-1)).any()
     else:
         np.testing.assert_array_equal(gpu, cpu)           # wrapping integer sum / max
+
+
+def _division_cases(rng, n):
+    """Dividends over every exponent and sign, plus zeros, subnormals,
+    infinities, NaN and the ends of the range."""
+    bits = rng.integers(0, 2**32, size=n, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32).copy()
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 1.1754942e-38,
+                        1.1754944e-38, 3.4028235e38, -3.4028235e38, 1.0, -1.0, 2.0**-60,
+                        2.0**60, np.nextafter(np.float32(2.0**60), np.float32(0)),
+                        np.nextafter(np.float32(2.0**-60), np.float32(0))], dtype=np.float32)
+    x[: special.size] = special
+    # dense band of ordinary values (the common case, all on the fast path)
+    x[special.size: n // 2] = rng.normal(0.0, 1.0, n // 2 - special.size).astype(np.float32)
+    return x
+
+
+DIVISORS = [3.0, -7.25, 1.0 / 3.0, 0.1, 1e-30, 1e30, 2.0**-60, 2.0**60, 2.0**-61, 1.5 * 2.0**59,
+            1e-40, 0.0, -0.0, float("inf"), float("nan"), 1.0, 65504.0, 6.1e-05]
+
+
+def _same_bits(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    nan = np.isnan(a)
+    assert np.array_equal(nan, np.isnan(b))
+    np.testing.assert_array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", ["scalar", "reduced"])
+def test_division_by_uniform_divisor_is_ieee(kind):
+    """A divisor shared by a whole program (a scalar, or a row reduction
+    broadcast) takes the reciprocal-and-correct path; every quotient must
+    still be the IEEE f32 quotient, bit for bit, as NumPy computes it."""
+    kernel = S.uniform_div_program(KDIR, kind)
+    rng = np.random.default_rng(311)
+    n = 1024 * len(DIVISORS)
+    x = _division_cases(rng, n)
+    out = torch.zeros(n, device="cuda")
+    if kind == "scalar":
+        for j, d in enumerate(DIVISORS):
+            blk = x[j * 1024:(j + 1) * 1024].copy()
+            g = torch.zeros(1024, device="cuda")
+            kernel[(1,)](up(blk, "f32"), g, float(d))
+            torch.cuda.synchronize()
+            with np.errstate(all="ignore"):
+                _same_bits(down(g), blk / np.float32(d))
+    else:
+        y = np.zeros((len(DIVISORS), 256), np.float32)
+        y[:, 0] = np.array(DIVISORS, np.float32)
+        cpu = np.zeros(n, np.float32)
+        with np.errstate(all="ignore"):
+            kernel[(len(DIVISORS),)](x, cpu, y)
+        kernel[(len(DIVISORS),)](up(x, "f32"), out, up(y, "f32"))
+        torch.cuda.synchronize()
+        _same_bits(down(out), cpu)
+        with np.errstate(all="ignore"):
+            _same_bits(cpu, x / np.repeat(y.sum(1, dtype=np.float32), 1024))
+    assert tila_b200.read_device_errors() == 0
+
+
+def test_division_by_uniform_divisor_many_pairs():
+    """Ten million random (dividend, divisor) pairs in the fast range against
+    NumPy's IEEE quotients."""
+    kernel = S.uniform_div_program(KDIR, "reduced")
+    rng = np.random.default_rng(312)
+    g = 8192
+    n = 1024 * g
+    e = rng.integers(-59, 59, size=n)
+    x = (rng.uniform(1.0, 2.0, n) * np.exp2(e)).astype(np.float32) * rng.choice([-1, 1], n).astype(np.float32)
+    d = (rng.uniform(1.0, 2.0, g) * np.exp2(rng.integers(-59, 59, size=g))).astype(np.float32)
+    y = np.zeros((g, 256), np.float32)
+    y[:, 0] = d
+    out = torch.zeros(n, device="cuda")
+    kernel[(g,)](up(x, "f32"), out, up(y, "f32"))
+    torch.cuda.synchronize()
+    _same_bits(down(out), x / np.repeat(d, 1024))

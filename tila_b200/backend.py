@@ -309,6 +309,15 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
             raise _failure(exc, "launch", entry.spec.source, context) from exc
 
 
+def launch_flags() -> int:
+    """Launch flags of generated kernels.  Every generated kernel waits for
+    the previous grid in its stream before touching global memory, so it is
+    launched to overlap that grid's tail (TILA_B200_OVERLAP=0 turns it off)."""
+    if os.environ.get("TILA_B200_OVERLAP", "1") == "0":
+        return 0
+    return native.LAUNCH_OVERLAP_PREVIOUS
+
+
 class LaunchRecord:
     """One prepared launch (kernel, geometry, packed arguments).  Re-issuing it
     skips Tila's host-side contract checks, so benchmarks can time the kernel
@@ -325,7 +334,8 @@ class LaunchRecord:
             import torch
             stream = torch.cuda.current_stream(self.device).cuda_stream
         self.entry.kernel.launch(self.grid, (self.entry.spec.threads, 1, 1), self.args,
-                                 smem_bytes=self.entry.spec.smem_bytes, stream=stream)
+                                 smem_bytes=self.entry.spec.smem_bytes, stream=stream,
+                                 flags=launch_flags())
 
     @property
     def kernel_name(self):

@@ -33,6 +33,8 @@ into the TMEM-row layout.
 
 from __future__ import annotations
 
+import re
+
 import dataclasses
 import math
 from dataclasses import dataclass, field
@@ -379,16 +381,45 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         name = self.fresh(base)
         self.emit(f"{DT.ctype(dt)} {name}[{layout.nreg}];")
         if straight:
-            for r in range(layout.nreg):
-                exprs = [self.elem(v, layout, r, m) for v, m in zip(ops, maps)]
-                self.emit(f"{name}[{r}] = {make_expr(exprs)};")
+            rows = [[self.elem(v, layout, r, m) for v, m in zip(ops, maps)]
+                    for r in range(layout.nreg)]
+            if isinstance(make_expr, _UniformDivisor) and len({e[1] for e in rows}) == 1:
+                self._uniform_division(name, [(str(r), e[0]) for r, e in enumerate(rows)], rows[0][1])
+            else:
+                for r, exprs in enumerate(rows):
+                    self.emit(f"{name}[{r}] = {make_expr(exprs)};")
+        else:
+            exprs = [self.elem(v, layout, "r") for v in ops]
+            if isinstance(make_expr, _UniformDivisor) and not re.search(r"\br\b", exprs[1]):
+                self._uniform_division(name, None, exprs[1], exprs[0], layout.nreg)
+            else:
+                self.emit("#pragma unroll")
+                self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+                self.emit(f"  {name}[r] = {make_expr(exprs)};")
+                self.emit("}")
+        return Val("reg", dt, tuple(shape), name=name, layout=layout)
+
+    def _uniform_division(self, name, rows, divisor, dividend=None, nreg=None):
+        """f32 quotients by a divisor shared by all of this thread's elements:
+        one reciprocal (tila::udiv_prepare), Markstein-corrected quotients,
+        and an IEEE recomputation if any dividend leaves the exact range."""
+        ud = self.fresh("ud")
+        self.emit(f"const tila::UDiv {ud} = tila::udiv_prepare({divisor});")
+        self.emit(f"tila::u32 {ud}_hi = 0u, {ud}_lo = 0xffffffffu;")
+        if rows is not None:
+            for r, a in rows:
+                self.emit(f"{name}[{r}] = tila::udiv_fast(({a}), {ud}, {ud}_hi, {ud}_lo);")
         else:
             self.emit("#pragma unroll")
-            self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
-            exprs = [self.elem(v, layout, "r") for v in ops]
-            self.emit(f"  {name}[r] = {make_expr(exprs)};")
-            self.emit("}")
-        return Val("reg", dt, tuple(shape), name=name, layout=layout)
+            self.emit(f"for (int r = 0; r < {nreg}; ++r) {name}[r] = "
+                      f"tila::udiv_fast(({dividend}), {ud}, {ud}_hi, {ud}_lo);")
+        self.emit(f"if (!tila::udiv_all_fast({ud}, {ud}_hi, {ud}_lo)) {{")
+        if rows is not None:
+            for r, a in rows:
+                self.emit(f"  {name}[{r}] = (({a}) / ({divisor}));")
+        else:
+            self.emit(f"  for (int r = 0; r < {nreg}; ++r) {name}[r] = (({dividend}) / ({divisor}));")
+        self.emit("}")
 
     def materialize(self, v: Val, layout=None) -> Val:
         if v.kind == "reg" and (layout is None or v.layout == layout):
@@ -743,6 +774,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 return lambda e: f"((bool)(({e[0]}) {op} ({e[1]})))"
             self.fail(f"operator {op} on masks")
         if DT.is_float(odt):
+            if op == "/" and odt.name == "f32" and rdt.name == "f32":
+                return _UniformDivisor()
             if op in ("+", "-", "*", "/"):
                 return lambda e: DT.round_to(rdt, f"(({e[0]}) {op} ({e[1]}))")
             if op == "//":
@@ -1088,7 +1121,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if not shape:
             return self._scalar_load(x.buffer, coords, mask, other, dt)
         layout = self.default_layout(shape, dt)
-        return self._tile_load(x.buffer, list(x.coords), coords, mask, other, dt, shape, layout)
+        return self._tile_load(x.buffer, list(x.coords), coords, mask, other, dt, shape, layout,
+                               mask_node=x.mask)
 
     def _scalar_load(self, buffer, coords, mask, other, dt):
         name = self.fresh("ld")
@@ -1102,7 +1136,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit(f"const {DT.ctype(dt)} {name} = {load};")
         return Val("scalar", dt, expr=name)
 
-    def _tile_load(self, buffer, coord_nodes, coords, mask, other, dt, shape, layout):
+    def _tile_load(self, buffer, coord_nodes, coords, mask, other, dt, shape, layout, mask_node=None):
         ops = list(coords) + ([mask] if mask is not None else []) + ([other] if other is not None else [])
         ops, maps, straight = self.prepare_operands(ops, layout, shape)
         nc = len(coords)
@@ -1138,7 +1172,13 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             off = self.address_terms(buffer, coords, layout, "r0", cm)
             self.emit(f"const tila::i64 off = {off};")
             lane_cond = cond_at("r")
-            if lane_cond is not None:
+            interval = lane_cond is not None and (mask is None or self._interval_mask(mask_node))
+            if interval:
+                # the group's lanes where the mask holds are consecutive:
+                # the first and the last lane decide the whole group
+                self.emit(f"bool all; {{ int r = r0; const bool a_ = {lane_cond}; "
+                          f"r = r0 + {width - 1}; all = a_ && ({lane_cond}); }}")
+            elif lane_cond is not None:
                 self.emit(f"bool m[{width}];")
                 self.emit("bool all = true;")
                 self.emit("#pragma unroll")
@@ -1157,7 +1197,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit("    const int r = r0 + j;")
             offr = self.address_terms(buffer, coords, layout, "r", cm)
             fill = self.elem(other, layout, "r") if other is not None else fill0
-            mcond = "m[j]" if lane_cond is not None else "true"
+            mcond = (f"({lane_cond})" if interval else "m[j]") if lane_cond is not None else "true"
             self.emit(f"    {name}[r] = {mcond} ? {DT.load_conv(dt, f'p_{buffer}[{offr}]')} : {fill};")
             self.emit("  }")
             self.emit("}")
@@ -1235,7 +1275,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.indent += 1
             self.emit(f"const int r0 = g * {width};")
             self.emit(f"const tila::i64 off = {self.address_terms(s.buffer, coords, layout, 'r0', cm)};")
-            if mask is not None:
+            interval = mask is not None and self._interval_mask(s.mask)
+            if interval:
+                mexpr = self.elem(mask, layout, "r")
+                self.emit(f"bool all; {{ int r = r0; const bool a_ = {mexpr}; "
+                          f"r = r0 + {width - 1}; all = a_ && ({mexpr}); }}")
+            elif mask is not None:
                 self.emit(f"bool m[{width}];")
                 self.emit("bool all = true;")
                 self.emit("#pragma unroll")
@@ -1254,7 +1299,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit(f"  for (int j = 0; j < {width}; ++j) {{")
             self.emit("    const int r = r0 + j;")
             offr = self.address_terms(s.buffer, coords, layout, "r", cm)
-            mcond = "m[j]" if mask is not None else "true"
+            mcond = (f"({self.elem(mask, layout, 'r')})" if interval else "m[j]") if mask is not None else "true"
             self.emit(f"    if ({mcond}) p_{s.buffer}[{offr}] = {DT.store_conv(dt, self.elem(value, layout, 'r'))};")
             self.emit("  }")
             self.emit("}")
@@ -1522,6 +1567,39 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self.lines.extend(general)
         self.emit("}")
 
+    def _interval_mask(self, node, depth=0):
+        """True when the lanes of any run of consecutive elements along the
+        last tile dim on which mask ``node`` holds are themselves consecutive
+        (a conjunction of bounds on coordinates that step by 0 or +1 along
+        that dim).  Then a vector group is fully inside iff its first and last
+        lanes are."""
+        from .pipeline import tile_affinity
+        if node is None or depth > 16:
+            return False
+        node = self.pdefs.resolve(node)
+        if isinstance(node, T_.TLit):
+            return True
+        if isinstance(node, T_.TBin):
+            if node.op in ("&", "and"):
+                return (self._interval_mask(node.left, depth + 1)
+                        and self._interval_mask(node.right, depth + 1))
+            if node.op in ("<", "<=", ">", ">=", "=="):
+                uni = self._uniform_names()
+                la = tile_affinity(node.left, self.pdefs, self.consts, uni)
+                ra = tile_affinity(node.right, self.pdefs, self.consts, uni)
+                if la is None or ra is None:
+                    return False
+                if la == () and ra == ():
+                    return True
+                var = la if ra == () else ra if la == () else None
+                return var is not None and var[-1] in (0, 1)
+            return False
+        if isinstance(node, T_.TExpand):
+            if node.axis == 1:           # m[:, None]: constant along the last dim
+                return True
+            return self._interval_mask(node.operand, depth + 1)
+        return False
+
     def _bound_guard(self, x, l, r, op, shape):
         """Uniform condition under which ``l op r`` is true on the whole tile
         (l = uniform + arange along one dim, r uniform), or None."""
@@ -1712,6 +1790,10 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append(f"  if (tid == 0) {{ tila::mbar_init(tila_mma_bar, 1); {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
             for tm in self.tensor_maps:
                 out.append(f"  if (tid == 0) tila::tma_prefetch_desc(&{tm['param']});")
+        # everything above touches only shared memory and kernel parameters;
+        # global memory (and tensor memory) only after the previous grid ends
+        out.append("  tila::grid_dep_wait();")
+        out.append("  tila::grid_dep_release();")
         if self.uses_tmem:
             out.append(f"  if (tid < 32) tila::tmem_alloc(tila_tmem_slot, {self.tmem_cols});")
             out.append("  tila::tc_fence_before();")
@@ -1740,6 +1822,17 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             smem = max(smem, floor_bytes)
         return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
+
+
+class _UniformDivisor:
+    """Expression maker of an f32 division (IEEE).  When a register tile is
+    materialised and every element of a thread divides by the same value (a
+    scalar, or a row value broadcast along the thread's elements), the
+    emitter replaces it with the shared-reciprocal path
+    (``KernelEmitter._uniform_division``), which yields the same quotients."""
+
+    def __call__(self, e):
+        return f"(({e[0]}) / ({e[1]}))"
 
 
 class _BroadcastView(Layout):

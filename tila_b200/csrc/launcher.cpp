@@ -279,6 +279,10 @@ int tila_launch(void *kernel, const tila_launch_config *cfg, void **args,
   if (kernel == nullptr || cfg == nullptr) return TILA_ERR_ARGUMENT;
   for (int i = 0; i < 3; ++i)
     if (cfg->block[i] == 0) return TILA_ERR_ARGUMENT;
+  if ((cfg->flags & ~TILA_LAUNCH_OVERLAP_PREVIOUS) != 0 || cfg->reserved != 0) {
+    put_log(log, log_cap, "tila_launch: unknown flag bits");
+    return TILA_ERR_ARGUMENT;
+  }
   int st = ensure_driver(log, log_cap);
   if (st != TILA_OK) return st;
   if (cfg->grid[0] == 0 || cfg->grid[1] == 0 || cfg->grid[2] == 0) return TILA_OK;
@@ -314,18 +318,25 @@ int tila_launch(void *kernel, const tila_launch_config *cfg, void **args,
   lc.blockDimZ = cfg->block[2];
   lc.sharedMemBytes = cfg->smem_bytes;
   lc.hStream = reinterpret_cast<CUstream>(static_cast<uintptr_t>(cfg->stream));
-  CUlaunchAttribute attr[1];
+  CUlaunchAttribute attr[2];
+  unsigned nattr = 0;
   unsigned cx = cfg->cluster[0] ? cfg->cluster[0] : 1;
   unsigned cy = cfg->cluster[1] ? cfg->cluster[1] : 1;
   unsigned cz = cfg->cluster[2] ? cfg->cluster[2] : 1;
   if (cx * cy * cz > 1) {
-    attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    attr[0].value.clusterDim.x = cx;
-    attr[0].value.clusterDim.y = cy;
-    attr[0].value.clusterDim.z = cz;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
+    attr[nattr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr[nattr].value.clusterDim.x = cx;
+    attr[nattr].value.clusterDim.y = cy;
+    attr[nattr].value.clusterDim.z = cz;
+    ++nattr;
   }
+  if (cfg->flags & TILA_LAUNCH_OVERLAP_PREVIOUS) {
+    attr[nattr].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attr[nattr].value.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  lc.attrs = nattr ? attr : nullptr;
+  lc.numAttrs = nattr;
   // A CUkernel is accepted wherever a CUfunction is expected; the driver
   // resolves it for the current context.
   CUresult r = g_drv.LaunchKernelEx(&lc, reinterpret_cast<CUfunction>(k), args, nullptr);

@@ -99,6 +99,57 @@ __device__ __forceinline__ float exp2_fast(float x) {
   return r;
 }
 
+// Division by a divisor shared by many dividends (a row sum broadcast along
+// a row, a scalar parameter): the IEEE f32 quotient a / b, bit for bit, with
+// the reciprocal computed once per divisor.
+// Method: residual correction after P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
+// 1990 (Markstein's theorem: if q is a faithful approximation of a/b and y
+// approximates 1/b with relative error below 2^-24, then r = a - b*q is exact
+// and RN(q + r*y) = RN(a/b), barring underflow and overflow).  q0 = RN(a*y)
+// with y = RN(1/b) can be off by up to 1.5 ulp (e.g. 1.5 / 1.9999999), so a
+// first correction makes it faithful (its error is then below 0.5 ulp plus
+// 2^-45 relative) and the second one rounds correctly.  The quotient of the
+// magnitudes is computed and the sign attached afterwards, which keeps signed
+// zeros exact.  Magnitudes in [2^-60, 2^60) for both operands (and zero for
+// the dividend) keep every intermediate normal and finite; udiv_fast records
+// the dividends' range so that a thread whose dividends leave it (subnormals,
+// infinities, extreme exponents) recomputes its quotients with IEEE division.
+struct UDiv {
+  float babs;   // |b|
+  float y;      // RN(1/|b|)
+  u32 sbits;    // sign bit of b
+  bool ok;      // 2^-60 <= |b| < 2^60
+};
+__device__ __forceinline__ UDiv udiv_prepare(float b) {
+  UDiv d;
+  const u32 ub = __float_as_uint(b);
+  d.babs = fabsf(b);
+  d.y = __frcp_rn(d.babs);
+  d.sbits = ub & 0x80000000u;
+  d.ok = ((ub & 0x7fffffffu) - 0x21800000u) < (0x5d800000u - 0x21800000u);
+  return d;
+}
+// Quotient for one dividend (valid when udiv_all_fast holds at the end);
+// updates the range record: hi = max of 2|a| bits, lo = min of (2|a| bits) - 1
+// (a zero dividend maps to 0 and 0xffffffff and so changes neither).
+__device__ __forceinline__ float udiv_fast(float a, const UDiv &d, u32 &hi, u32 &lo) {
+  const u32 ua = __float_as_uint(a);
+  const u32 u2 = ua + ua;
+  hi = max(hi, u2);
+  lo = min(lo, u2 - 1u);
+  const float aa = fabsf(a);
+  float q = __fmul_rn(aa, d.y);
+  float r = __fmaf_rn(-d.babs, q, aa);
+  q = __fmaf_rn(r, d.y, q);
+  r = __fmaf_rn(-d.babs, q, aa);
+  q = __fmaf_rn(r, d.y, q);
+  return __uint_as_float(__float_as_uint(q) | ((ua ^ d.sbits) & 0x80000000u));
+}
+__device__ __forceinline__ bool udiv_all_fast(const UDiv &d, u32 hi, u32 lo) {
+  return d.ok && hi < 0xbb000000u && lo >= 0x42ffffffu;   // 2|a| bits in [2^-60, 2^60)
+}
+
 // Round an f32 to the nearest f16 / bf16 value and widen back (the register
 // representation of f16/bf16 tiles is an f32 holding a representable value).
 __device__ __forceinline__ float round_f16(float f) { return h2f(f2h(f)); }
@@ -265,6 +316,20 @@ __device__ __forceinline__ bool mbar_try_wait(u64 *bar, u32 parity) {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
+}
+
+// Programmatic dependent launch.  A kernel launched with the overlap flag may
+// be resident before the previous grid in its stream has finished;
+// grid_dep_wait blocks until that grid has completed and its memory writes are
+// visible, and must precede every global-memory access.  grid_dep_release
+// lets the next grid in the stream be scheduled once every CTA of this grid
+// has executed it (it does not make this grid's results visible early: the
+// dependent's own wait still covers them).  Without the flag both are no-ops.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ u64 globaltimer_ns() {

@@ -55,7 +55,12 @@ class NativeError(RuntimeError):
 class LaunchConfig(ctypes.Structure):
     _fields_ = [("grid", ctypes.c_uint32 * 3), ("block", ctypes.c_uint32 * 3),
                 ("cluster", ctypes.c_uint32 * 3), ("smem_bytes", ctypes.c_uint32),
-                ("stream", ctypes.c_uint64)]
+                ("stream", ctypes.c_uint64), ("flags", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
+
+
+# tila_launch_config.flags
+LAUNCH_OVERLAP_PREVIOUS = 1
 
 
 class KernelAttrs(ctypes.Structure):
@@ -234,8 +239,10 @@ class Kernel:
                f"attributes of {self.name}", log)
         return {f: getattr(a, f) for f, _ in KernelAttrs._fields_}
 
-    def launch(self, grid, block, args, smem_bytes=0, stream=0, cluster=(1, 1, 1)):
-        """Launch with ``args``: a sequence of ctypes objects, one per parameter."""
+    def launch(self, grid, block, args, smem_bytes=0, stream=0, cluster=(1, 1, 1), flags=0):
+        """Launch with ``args``: a sequence of ctypes objects, one per parameter.
+        ``flags``: LAUNCH_* bits (LAUNCH_OVERLAP_PREVIOUS only for kernels that
+        wait on the previous grid before touching global memory)."""
         cfg = LaunchConfig()
         for i in range(3):
             cfg.grid[i] = grid[i]
@@ -243,6 +250,7 @@ class Kernel:
             cfg.cluster[i] = cluster[i]
         cfg.smem_bytes = smem_bytes
         cfg.stream = stream
+        cfg.flags = flags
         ptrs = (ctypes.c_void_p * max(1, len(args)))(
             *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
         log = ctypes.create_string_buffer(1024)
@@ -250,7 +258,7 @@ class Kernel:
                f"launch of {self.name}", log)
 
     def launch_noalloc(self, grid, block, args, scratch_arg, scratch_bytes, smem_bytes=0,
-                       stream=0):
+                       stream=0, flags=0):
         """Launch through tila_launch_noalloc: argument ``scratch_arg`` (the
         kernel's scratch pointer) is replaced by the library's static device
         scratch, so this call allocates no device memory.  Returns the C status."""
@@ -261,6 +269,7 @@ class Kernel:
             cfg.cluster[i] = 1
         cfg.smem_bytes = smem_bytes
         cfg.stream = stream
+        cfg.flags = flags
         ptrs = (ctypes.c_void_p * max(1, len(args)))(
             *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
         log = ctypes.create_string_buffer(1024)
