@@ -15,7 +15,7 @@ f16 = torch.float16
 
 def gen(jf, tensors, warps=4, **consts):
     spec = KernelEmitter(jf.tk, consts, binding_facts(jf.tk, tensors), num_warps=warps).generate()
-    native.compile_cubin(spec.source, spec.name)
+    native.compile_spec(spec)
     return spec
 
 

@@ -165,7 +165,7 @@ def compile_kernel(jf, consts, facts, num_warps, context=None) -> Compiled:
                         Loc(exc.line),
                         fixes=["restructure the kernel, or run it on CPU arrays (interpreter)"]) from exc
     try:
-        cubin = native.compile_cubin(spec.source, spec.name)
+        cubin = native.compile_spec(spec)
         lib = native.Library(cubin)
         kern = lib.kernel(spec.name)
     except native.NativeError as exc:

@@ -98,7 +98,7 @@ def warm_cubins():
     for jf, tensors, consts in cases:
         facts = binding_facts(jf.tk, tensors)
         spec = KernelEmitter(jf.tk, consts, facts, num_warps=4).generate()
-        native.compile_cubin(spec.source, spec.name)
+        native.compile_spec(spec)
         names.append(spec.name)
     return names
 

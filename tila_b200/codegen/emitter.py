@@ -118,6 +118,10 @@ class KernelSpec:
     persistent: bool = False
     grid_override: object = None
     fuse: dict = field(default_factory=dict)   # {grid axis: programs per CTA along it}
+    # compile with multiply-add contraction (tensor-core kernels, whose results
+    # are compared within a tolerance; kernels without a dot keep every f32
+    # multiply and add separately rounded, like NumPy)
+    fp_contract: bool = False
 
 
 # ---------------------------------------------------------------------------
@@ -197,6 +201,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._guard_mode = None
         self._pid_expr = {}          # program-id expressions of the program being emitted
         self.fuse = None             # {axis: programs per CTA} when CTAs run program blocks
+        self._wg_candidate = False   # an asynchronous loop allows two programs per CTA
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -692,7 +697,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 mk = lambda e: f"{fn}((double)({e[0]}))"
             elif op == "exp2":
                 # ex2.approx.f32: relative error <= 2^-22.5, subnormals kept
-                mk = lambda e: DT.round_to(dt, f"tila::exp2_fast((float)({e[0]}))")
+                # (tensor-core kernels flush subnormal results; see tila_exp2_f32)
+                mk = lambda e: DT.round_to(dt, f"tila_exp2_f32((float)({e[0]}))")
             else:
                 mk = lambda e: DT.round_to(dt, f"{fn}f((float)({e[0]}))")
             if v.kind == "scalar":
@@ -1753,23 +1759,56 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if not self.try_fused_kernel():
             self.stmts(tk.body)
         body = self.lines
+        # shared-memory plan and tensor-memory columns of one program
+        scratch_off = (self.smem.top + 127) // 128 * 128
+        scratch_col = self.tmem_next
+        total_cols = self.tmem_next + self.tmem_scratch_need
+        if self.uses_tmem:
+            if total_cols > 512:
+                self.fail(f"kernel needs {total_cols} tensor-memory columns (limit 512)")
+            self.tmem_cols = _pow2_at_least(max(32, total_cols))
+        per_prog = -(-(scratch_off + self.smem.scratch) // 1024) * 1024
+        # two programs of axis 0 per CTA, one per warpgroup (see _pingpong_ok)
+        wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
+              and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448)
+        if wg:
+            self.fuse = {0: 2}
         for ax in sorted(self.fuse or {}):
             sig.append(f"tila::i32 launch_{ax}")
             params.append(("launch", ax, "i32"))
         for tm in self.tensor_maps:
             sig.append(f"const __grid_constant__ tila::TensorMap {tm['param']}")
             params.append(("tensormap", tm["param"], tm))
+        threads = 2 * self.T if wg else self.T
+        cta_cols = 2 * self.tmem_cols if wg else self.tmem_cols
         out = ['#include "tila_tile.cuh"', ""]
-        out.append(f'extern "C" __global__ void __launch_bounds__({self.T}) {self.entry}(')
+        # f32 exp2: tensor-core kernels (compared within a tolerance, compiled
+        # with multiply-add contraction) use the flush-to-zero form, which
+        # returns 0 instead of a subnormal below 2^-126 and the same values
+        # elsewhere; all other kernels keep subnormal results.
+        out.append("#define tila_exp2_f32 tila::" + ("exp2_ftz" if self.uses_mma else "exp2_fast"))
+        out.append("")
+        out.append(f'extern "C" __global__ void __launch_bounds__({threads}) {self.entry}(')
         out.append(",\n".join("    " + x for x in sig) + ") {")
-        out.append("  extern __shared__ __align__(1024) unsigned char tila_smem[];")
-        out.append("  const int tid = threadIdx.x;")
-        out.append("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x + pid_off_0);")
+        if wg:
+            out.append("  extern __shared__ __align__(1024) unsigned char tila_smem_all[];")
+            out.append("  // two programs of grid axis 0 per CTA: warpgroup w runs program 2*blockIdx.x + w")
+            out.append("  const int tila_wg = threadIdx.x >> 7;")
+            out.append("  const int tid = threadIdx.x & 127;")
+            out.append(f"  unsigned char* const tila_smem = tila_smem_all + tila_wg * {per_prog};")
+            out.append("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + tila_wg + pid_off_0);")
+            out.append("  const bool tila_live = (tila::i32)(blockIdx.x * 2 + tila_wg) < launch_0;")
+            out.append("  const bool tila_partner_live = (tila::i32)(blockIdx.x * 2 + (tila_wg ^ 1)) < launch_0;")
+            out.append(f"  tila::u64* const tila_tok = reinterpret_cast<tila::u64*>(tila_smem_all + {2 * per_prog});")
+            out.append("  tila::u32 tila_tok_ph = 0, tila_tok_n = 0;")
+            out.append("  (void)tila_partner_live; (void)tila_tok; (void)tila_tok_ph; (void)tila_tok_n;")
+        else:
+            out.append("  extern __shared__ __align__(1024) unsigned char tila_smem[];")
+            out.append("  const int tid = threadIdx.x;")
+            out.append("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x + pid_off_0);")
         out.append("  const tila::i32 pid_1 = (tila::i32)(blockIdx.y + pid_off_1);")
         out.append("  const tila::i32 pid_2 = (tila::i32)(blockIdx.z + pid_off_2);")
         # fixed shared-memory head: mbarrier, tmem slot, dead flag; scratch follows the plan
-        scratch_off = (self.smem.top + 127) // 128 * 128
-        # the planned regions start after the head
         out.append(f"  tila::u64* tila_mma_bar = reinterpret_cast<tila::u64*>(tila_smem);")
         out.append(f"  tila::u32* tila_tmem_slot = reinterpret_cast<tila::u32*>(tila_smem + 8);")
         out.append(f"  volatile int& tila_dead = *reinterpret_cast<volatile int*>(tila_smem + 12);")
@@ -1778,49 +1817,65 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         out.append("  tila::u32 tila_mma_phase = 0; (void)tila_mma_phase;")
         for v in self._phase_vars:
             out.append(f"  tila::u32 {v} = 0;")
-        scratch_col = self.tmem_next
-        total_cols = self.tmem_next + self.tmem_scratch_need
-        if self.uses_tmem:
-            if total_cols > 512:
-                self.fail(f"kernel needs {total_cols} tensor-memory columns (limit 512)")
-            self.tmem_cols = _pow2_at_least(max(32, total_cols))
         if self.uses_tmem or self._need_barrier_init:
             inits = " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem + {o}), 1);"
                              for o in self._need_barrier_init)
             out.append(f"  if (tid == 0) {{ tila::mbar_init(tila_mma_bar, 1); {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
             for tm in self.tensor_maps:
                 out.append(f"  if (tid == 0) tila::tma_prefetch_desc(&{tm['param']});")
+        if wg:
+            out.append("  if (threadIdx.x == 0) { tila::mbar_init(&tila_tok[0], 128); "
+                       "tila::mbar_init(&tila_tok[1], 128); tila::mbar_fence_init(); }")
         # everything above touches only shared memory and kernel parameters;
         # global memory (and tensor memory) only after the previous grid ends
         out.append("  tila::grid_dep_wait();")
         out.append("  tila::grid_dep_release();")
         if self.uses_tmem:
-            out.append(f"  if (tid < 32) tila::tmem_alloc(tila_tmem_slot, {self.tmem_cols});")
+            out.append(f"  if (threadIdx.x < 32) tila::tmem_alloc("
+                       + ("reinterpret_cast<tila::u32*>(tila_smem_all + 8)" if wg else "tila_tmem_slot")
+                       + f", {cta_cols});")
             out.append("  tila::tc_fence_before();")
             out.append("  __syncthreads();")
             out.append("  tila::tc_fence_after();")
-            out.append("  const tila::u32 tila_tmem = *tila_tmem_slot;")
+            if wg:
+                out.append(f"  const tila::u32 tila_tmem = *reinterpret_cast<tila::u32*>(tila_smem_all + 8) "
+                           f"+ (tila::u32)(tila_wg * {self.tmem_cols});")
+            else:
+                out.append("  const tila::u32 tila_tmem = *tila_tmem_slot;")
             out.append(f"  const tila::u32 tila_tmem_scratch_col = {scratch_col}; (void)tila_tmem_scratch_col;")
         elif self._need_barrier_init:
             out.append("  __syncthreads();")
         out.append("  do {")
-        # the planned smem regions were allocated relative to offset 0 of the plan;
-        # shift them past the head
-        out.extend(body)
+        if wg:
+            from .mma import WG_ACQUIRE, WG_RELEASE
+            acquire = ("if (tila_partner_live && (tila_wg == 1 || tila_tok_n > 0)) { "
+                       "tila::mbar_wait(&tila_tok[tila_wg], tila_tok_ph, tila_err, __LINE__, &tila_dead); "
+                       "tila_tok_ph ^= 1u; } ++tila_tok_n;")
+            release = "if (tila_partner_live) tila::mbar_arrive(&tila_tok[tila_wg ^ 1]);"
+            out.append("    if (!tila_live) break;")
+            for line in body:
+                line = line.replace("__syncthreads();", "tila::wg_sync(tila_wg);")
+                line = line.replace(WG_ACQUIRE, acquire).replace(WG_RELEASE, release)
+                out.append(line)
+        else:
+            from .mma import WG_ACQUIRE, WG_RELEASE
+            out.extend(l for l in body if l.strip() not in (WG_ACQUIRE, WG_RELEASE))
         out.append("  } while (0);")
         if self.uses_tmem:
             out.append("  tila::tc_fence_before();")
             out.append("  __syncthreads();")
-            out.append(f"  if (tid < 32) tila::tmem_dealloc(tila_tmem, {self.tmem_cols});")
+            out.append(f"  if (threadIdx.x < 32) tila::tmem_dealloc(tila_tmem, {cta_cols});")
         out.append("}")
         src = "\n".join(out) + "\n"
-        smem = scratch_off + self.smem.scratch
+        smem = 2 * per_prog + 64 if wg else scratch_off + self.smem.scratch
         if self.uses_tmem:
             # keep (resident CTAs) x (TMEM columns) within the SM's 512 columns
-            max_ctas = max(1, 512 // self.tmem_cols)
+            max_ctas = max(1, 512 // cta_cols)
             floor_bytes = 233472 // (max_ctas + 1) - 1024 + 1
             smem = max(smem, floor_bytes)
-        return KernelSpec(self.entry, src, self.T, smem, params, tmem_cols=self.tmem_cols,
+        self.tmem_cols = cta_cols
+        return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma,
+                          tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
 
 

@@ -207,9 +207,20 @@ class MmaMixin:
         return col
 
     def e_TDot(self, x):
-        if self.actx is not None:
-            self.wait_all_accs(release=True)
         dt, shape, _ = self.vt_info(x.vt)
+        ctx = self.actx
+        # In an asynchronous loop whose synchronous dot reads two TMA tiles,
+        # that dot's MMAs for the next iteration are issued right behind the
+        # accumulating dot (see emit_async_acc_dot); tila_s_pre records it.
+        hoist = (ctx is not None and getattr(ctx, "pingpong", False) and x.acc is None
+                 and isinstance(x.a, T_.TName) and isinstance(x.b, T_.TName)
+                 and getattr(self.env.get(x.a.name), "kind", None) == "smem"
+                 and getattr(self.env.get(x.b.name), "kind", None) == "smem")
+        if hoist:
+            self.emit(f"if (!{self._s_pre_var()}) {{")
+            self.indent += 1
+        if ctx is not None:
+            self.wait_all_accs(release=True)
         a = self.value(x.a)
         b = self.value(x.b)
         acc = self.value(x.acc) if x.acc is not None else None
@@ -268,6 +279,8 @@ class MmaMixin:
         self.emit("tila::tc_fence_before();")
         self.emit("__syncthreads();")
         self.emit("tila::tc_fence_after();")
+        issue_at = len(self.lines)
+        issue_indent = self.indent
         self.emit("if (tid == 0) {")
         self.indent += 1
         a_mn = descs["A"](0)[1]
@@ -281,10 +294,24 @@ class MmaMixin:
         self.emit("tila::mma_commit(tila_mma_bar);")
         self.indent -= 1
         self.emit("}")
+        if hoist:
+            pad = "  " * issue_indent
+            ctx.s_issue = [l[len(pad):] if l.startswith(pad) else l.lstrip() for l in self.lines[issue_at:]]
+            ctx.s_operands = [v for v in (a, b) if v.kind == "smem"]
+            self.indent -= 1
+            self.emit("}")
+            self.emit(f"{self._s_pre_var()} = 0u;")
         self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
         self.emit("tila_mma_phase ^= 1u;")
         self.emit("tila::tc_fence_after();")
-        if self.actx is not None:
+        if ctx is not None:
+            if hoist:
+                # MMAs complete in issue order: the accumulating dot issued
+                # before this one is done too (its buffers can be refilled)
+                self.wait_all_accs(release=True)
+            if getattr(ctx, "pingpong", False):
+                # start of the CUDA-core phase of the iteration (see WG_ACQUIRE)
+                self.emit(WG_ACQUIRE)
             self.release_after_sync_dot([a, b])
         from .emitter import Val
         res = Val("tmem", D.f32, (M, N), tmem_col=col)
@@ -485,6 +512,14 @@ class MmaMixin:
 # asynchronous accumulator loops
 # ---------------------------------------------------------------------------
 
+# Placeholders for the warpgroup hand-off of an asynchronous accumulator loop
+# (filled in, or dropped, when the kernel is assembled): a warpgroup acquires
+# the CUDA-core phase of its iteration once its synchronous dot has completed
+# and releases it when it issues the accumulating dot.
+WG_ACQUIRE = "/*@wg_acquire*/"
+WG_RELEASE = "/*@wg_release*/"
+
+
 @dataclass
 class AsyncCtx:
     """Code-generation state of one asynchronous accumulator loop."""
@@ -589,8 +624,53 @@ class AsyncLoopMixin:
         for name, a in ctx.accs.items():
             v = Val("tmem", D.f32, (128, a["N"]), tmem_col=str(a["col"]))
             self.env[name] = v
+        ctx.pingpong = self._pingpong_ok(s, start, al)
+        if ctx.pingpong:
+            self._wg_candidate = True
         self.actx = ctx
         return ctx
+
+    def _pingpong_ok(self, s, start, al):
+        """Two programs of grid axis 0 may share a CTA, one per warpgroup,
+        handing the CUDA-core phase of each iteration back and forth, when
+        both are sure to run the same iterations: the loop is a top-level
+        statement of a kernel without early returns, its bounds do not depend
+        on program_id(0), and each iteration has exactly one synchronous and
+        one accumulating dot."""
+        from .pipeline import _walk
+        if self.T != 128 or id(s) not in {id(st) for st in self.tk.body}:
+            return False
+        has_return = [False]
+        for st in self.tk.body:
+            _walk(st, lambda n: has_return.__setitem__(0, has_return[0] or isinstance(n, T_.TReturn)))
+        if has_return[0] or len(al.accs) != 1:
+            return False
+        for node in (s.start, s.end, s.step):
+            if node is not None and not self._pid0_free(node):
+                return False
+        dots = []
+        for st in s.body:
+            _walk(st, lambda n: dots.append(n) if isinstance(n, T_.TDot) else None)
+        acc_dots = {id(d) for d in al.accs.values()}
+        return len(dots) == 2 and sum(1 for d in dots if id(d) not in acc_dots) == 1
+
+    def _pid0_free(self, node, depth=0):
+        """``node`` provably has the same value in every program of grid axis 0."""
+        from .pipeline import _walk
+        if depth > 32:
+            return False
+        ok = [True]
+        uni = set(self.scalar_params)
+
+        def chk(n):
+            if isinstance(n, T_.TPid) and n.axis == 0:
+                ok[0] = False
+            elif isinstance(n, T_.TName) and n.name not in uni and n.name not in self.consts:
+                d = self.pdefs.resolve(n)
+                if d is n or not self._pid0_free(d, depth + 1):
+                    ok[0] = False
+        _walk(node, chk)
+        return ok[0]
 
     def _functional_prefix(self, ctx, loop_value):
         """Bind the loop variable to ``loop_value`` and evaluate the body's
@@ -740,6 +820,8 @@ class AsyncLoopMixin:
         self.emit("tila::tc_fence_before();")
         self.emit("__syncthreads();")
         self.emit("tila::tc_fence_after();")
+        if getattr(ctx, "pingpong", False):
+            self.emit(WG_RELEASE)
         b_mn = self._operand_desc(bv, "B", 0)[1]
         self.emit("if (tid == 0) {")
         self.indent += 1
@@ -756,9 +838,28 @@ class AsyncLoopMixin:
         self.indent -= 1
         self.emit("}")
         self.emit(f"{a['pend']} = 1u;")
+        if getattr(ctx, "s_issue", None):
+            # issue the next iteration's synchronous dot now: the tensor pipe
+            # executes it right after this accumulation (in issue order; it
+            # overwrites the TMEM columns this accumulation reads only after
+            # that MMA has consumed them)
+            cur = self.env[ctx.var].expr
+            nxt = f"((tila::i64)({cur}) + {ctx.stepv})"
+            self.emit(f"if ({nxt} < {ctx.end}) {{")
+            self.indent += 1
+            for op in ctx.s_operands:
+                self.emit_smem_wait(op)
+            for line in ctx.s_issue:
+                self.emit(line)
+            self.emit(f"{self._s_pre_var()} = 1u;")
+            self.indent -= 1
+            self.emit("}")
         v = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
         v.pending = name
         return v
+
+    def _s_pre_var(self):
+        return self._tma_state_var("tila_s_pre")
 
     def tmem_update_in_place(self, name, node):
         """acc = acc <op> rowvec (or scalar): update the TMEM accumulator in

@@ -99,6 +99,14 @@ __device__ __forceinline__ float exp2_fast(float x) {
   return r;
 }
 
+// 2^x for arguments >= -126 (normal results): the flush-to-zero form, equal
+// to exp2_fast there.
+__device__ __forceinline__ float exp2_ftz(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Division by a divisor shared by many dividends (a row sum broadcast along
 // a row, a scalar parameter): the IEEE f32 quotient a / b, bit for bit, with
 // the reciprocal computed once per divisor.
@@ -330,6 +338,12 @@ __device__ __forceinline__ void grid_dep_wait() {
 }
 __device__ __forceinline__ void grid_dep_release() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Barrier of one 128-thread warpgroup (named barrier 1 + wg) in kernels that
+// run one program per warpgroup.
+__device__ __forceinline__ void wg_sync(int wg) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
 }
 
 __device__ __forceinline__ u64 globaltimer_ns() {

@@ -139,15 +139,23 @@ def nvrtc_version() -> int:
     return v.value
 
 
-def default_options(extra=()) -> list[str]:
+def default_options(extra=(), fp_contract=False) -> list[str]:
     """NVRTC options of every generated kernel.
 
     ``--fmad=false`` keeps each f32 add and multiply separately rounded, which
     is what NumPy (the interpreter's arithmetic) does; divisions and square
-    roots stay IEEE (no fast-math).
+    roots stay IEEE (no fast-math).  ``fp_contract`` (tensor-core kernels,
+    compared within a tolerance) lets a*b+c contract into one FMA.
     """
-    return ["-arch=sm_100a", "--std=c++17", "--fmad=false", "-default-device",
+    fmad = "--fmad=true" if fp_contract else "--fmad=false"
+    return ["-arch=sm_100a", "--std=c++17", fmad, "-default-device",
             "-lineinfo", f"-I{TILE_INCLUDE_DIR}", "-DNDEBUG", *extra]
+
+
+def compile_spec(spec) -> bytes:
+    """Compile a generated kernel (``codegen.emitter.KernelSpec``)."""
+    return compile_cubin(spec.source, spec.name,
+                         default_options(fp_contract=getattr(spec, "fp_contract", False)))
 
 
 def _tile_headers_digest() -> str:
