@@ -259,8 +259,12 @@ class Case:
         self.out_index = 5
         self.units_per_rank = W.unfused_flops(bh1, l, d)
         self.bytes_per_rank = W.unfused_bytes(bh1, l, d)
+        # algorithmic bytes of each launch: scores (Q, K read, S written),
+        # softmax (S read, P written), P @ V (P, V read, O written)
+        self.kernel_units = [2 * bh1 * l * d * 2 + bh1 * l * l * 4, 2 * 4 * bh1 * l * l,
+                             bh1 * l * l * 4 + bh1 * l * d * 2 + bh1 * l * d * 4]
         self.dominant = 1
-        self.dominant_units = 2 * 4 * bh1 * l * l      # softmax kernel: S read + P write
+        self.dominant_units = self.kernel_units[1]
         self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
         self.dtype = "f16 in, f32 accumulate"
         self.config = {"workload": "unfused_attention", "batch": 8, "heads": 16, "seq": l,
@@ -378,21 +382,30 @@ def run_ours(args, world, rank, device, keys):
         ms_step = ms_total / K
         name, unit, scale = case.metric_unit
         value = case.units_per_rank * world / (ms_step * 1e-3) / scale
-        # dominant kernel: its own graph of K launches timed with events
+        # multi-launch steps: each kernel in its own graph of K launches,
+        # timed with events on the launching stream; the dominant kernel is
+        # the one that takes longest
         dom_ms = ms_step
+        per_kernel = []
         if len(case.launches) > 1:
-            g2 = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g2, stream=stream):
-                for i in range(K):
-                    case.records[i % len(case.records)][case.dominant].launch()
-            torch.cuda.synchronize(device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g2.replay()
-            e1.record()
-            torch.cuda.synchronize(device)
-            dom_ms = e0.elapsed_time(e1) / K
-            del g2
+            for j in range(len(case.launches)):
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2, stream=stream):
+                    for i in range(K):
+                        case.records[i % len(case.records)][j].launch()
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    g2.replay()
+                    e0.record(stream)
+                    g2.replay()
+                    e1.record(stream)
+                torch.cuda.synchronize(device)
+                per_kernel.append(e0.elapsed_time(e1) / K)
+                del g2
+            case.dominant = max(range(len(per_kernel)), key=lambda j: per_kernel[j])
+            case.dominant_units = case.kernel_units[case.dominant]
+            dom_ms = per_kernel[case.dominant]
         dom_kernel = case.records[0][case.dominant].kernel_name
         if W_ROOF.get(key, "hbm") == "hbm":
             achieved = case.dominant_units / (dom_ms * 1e-3) / 1e9
@@ -416,6 +429,11 @@ def run_ours(args, world, rank, device, keys):
                  "dtype": case.dtype}
         if key == "unfused_attention":
             entry["hbm_gbs"] = round(case.bytes_per_rank * world / (ms_step * 1e-3) / 1e9, 2)
+        if per_kernel:
+            entry["kernels"] = {case.records[0][j].kernel_name: {
+                "ms": round(per_kernel[j], 5),
+                "gbs": round(case.kernel_units[j] / (per_kernel[j] * 1e-3) / 1e9, 1)}
+                for j in range(len(per_kernel))}
         if gather_ms is not None:
             entry["gather_ms"] = round(gather_ms, 4)
         del graph

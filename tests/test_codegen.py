@@ -40,7 +40,7 @@ def test_matmul_uses_tma_ring_and_tcgen05():
     # a 2 x 2 block of programs per CTA sharing A and B tiles, N = 256 MMAs
     assert "2x2 programs per CTA" in spec.source and spec.fuse == {0: 2, 1: 2}
     assert "tma_load_2d" in spec.source and "idesc_f16_f32(128, 256" in spec.source
-    assert len(spec.tensor_maps) == 2
+    assert len(spec.tensor_maps) == 3          # A, B loads and the C store
     assert spec.tmem_cols == 512 and spec.smem_bytes <= 227 * 1024
 
 
@@ -140,3 +140,17 @@ def test_uniform_divisor_takes_reciprocal_path(tmp_path):
     k = S.binary_program(tmp_path, "f32", "/")
     src = gen(k, dict(x=torch.zeros(100), y=torch.zeros(100), out=torch.zeros(100))).source
     assert "udiv" not in src and " / " in src
+
+
+def test_f32_tile_epilogues_store_through_tma():
+    """128-row f32 results held one row per thread (scores, matmul, flash
+    attention) are written with TMA box stores from swizzled shared memory."""
+    t = dict(q=torch.zeros(2, 256, 64, dtype=f16), k=torch.zeros(2, 256, 64, dtype=f16),
+             s=torch.zeros(2, 256, 256))
+    src = gen(W.attention_scores, t, BM=128, BN=128, BD=64).source
+    assert "tila::tma_store_3d(" in src and "bulk_wait_read" in src
+    t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
+    assert "tila::tma_store_2d(" in gen(W.tiled_matmul, t, BM=128, BN=128, BK=64).source
+    # a column offset that is not a multiple of 4 elements keeps plain stores
+    t = dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000))
+    assert "tma_store" not in gen(W.row_softmax, t, BN=1024).source

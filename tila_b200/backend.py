@@ -126,7 +126,7 @@ def binding_facts(tk, tensors) -> dict:
         writable = access is not tila.types.READ_ONLY
         base_align = _pow2_div(t.data_ptr(), 256) if t.data_ptr() else 256
         esize = t.element_size()
-        tma_ok = (dt is not None and dt.name == "f16" and len(strides) >= 2 and strides[-1] == 1
+        tma_ok = (dt is not None and dt.name in ("f16", "f32") and len(strides) >= 2 and strides[-1] == 1
                   and base_align >= 16 and all((s * esize) % 16 == 0 and s > 0 for s in strides[:-1])
                   and all(0 < n < (1 << 31) for n in t.shape) and not is_ptr)
         out[p.name] = BufferInfo(

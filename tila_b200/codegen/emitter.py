@@ -97,7 +97,7 @@ class BufferInfo:
     base_align: int            # largest power of two (<= 256) dividing the base address
     writable: bool
     is_ptr: bool = False
-    tma_ok: bool = False       # f16, unit last stride, 16-byte aligned base and strides
+    tma_ok: bool = False       # f16/f32, unit last stride, 16-byte aligned base and strides
 
     def key(self):
         return (self.name, self.dtype.name, self.rank, self.unit_last, self.stride_div,
@@ -202,6 +202,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._pid_expr = {}          # program-id expressions of the program being emitted
         self.fuse = None             # {axis: programs per CTA} when CTAs run program blocks
         self._wg_candidate = False   # an asynchronous loop allows two programs per CTA
+        self._free_smem = []         # (offset, bytes) of buffers no longer in use
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -1249,6 +1250,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             return
         if value.kind == "tmem":
             value = self.tmem_to_reg(value)
+        if self._try_tma_store(s, coords, value, shape, dt):
+            return
         if value.kind == "reg" and tuple(value.shape) == tuple(shape):
             layout = value.layout
             if isinstance(layout, Derived) and not layout.reg_affine():
@@ -1335,6 +1338,75 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit("}")
         self.indent -= 1
         self.emit("}")
+
+    def _try_tma_store(self, s, coords, value, shape, dt):
+        """Store a 128-row f32 tile held in the tcgen05.ld register image
+        (thread = row) with TMA: the rows go to shared memory in the
+        SWIZZLE_128B box layout (conflict-free 16-byte writes), one thread
+        issues the box stores, and global memory receives whole lines instead
+        of 32 scattered 16-byte pieces per warp instruction."""
+        from .pipeline import plan_tma_store
+        if dt.name != "f32" or value.kind != "reg" or not isinstance(value.layout, TmemRows):
+            return False
+        lay = value.layout
+        if len(shape) != 2 or tuple(value.shape) != tuple(shape) or shape[0] != 128 \
+                or shape[1] % 32 or lay.cpg % 4 or self.T not in (128, 256):
+            return False
+        plan = plan_tma_store(s, tuple(shape), self.pdefs, self.consts, self._uniform_names(),
+                              self.buffer_params[s.buffer], self.buffers.get(s.buffer))
+        if plan is None or plan.inner != 1 or plan.rank not in (2, 3, 4):
+            return False
+        if any(c.kind not in ("scalar", "func") for c in coords):
+            return False
+        # the inner origin must be a multiple of 4 elements (16-byte TMA rule)
+        coef, div = self._affine_last(s.coords[plan.col_axis])
+        if coef != 1 or div % 4:
+            return False
+        size = plan.nbox * 128 * 128
+        base = self._store_staging(size)
+        if base is None:
+            return False
+        tm = self.tensor_map_param(plan)
+        origin = self._tma_coords(plan, coords)
+        col0 = "(tid >> 7) * %d + " % lay.cpg if lay.groups > 1 else ""
+        self.emit(f"{{ // TMA store of {s.buffer} ({shape[0]}x{shape[1]} f32) through shared memory")
+        self.indent += 1
+        self.emit("const int row_ = tid & 127;")
+        self.emit("#pragma unroll")
+        self.emit(f"for (int r = 0; r < {lay.nreg}; r += 4) {{")
+        self.emit(f"  const int c_ = {col0}r;")
+        self.emit(f"  *reinterpret_cast<float4*>(tila_smem + {base} + (c_ / 32) * 16384 + row_ * 128 + "
+                  f"((((c_ % 32) / 4) ^ (row_ & 7)) * 16)) = "
+                  f"make_float4({value.name}[r], {value.name}[r + 1], {value.name}[r + 2], {value.name}[r + 3]);")
+        self.emit("}")
+        self.emit("tila::fence_proxy_async_smem();")
+        self.emit("__syncthreads();")
+        self.emit("if (tid == 0) {")
+        self.indent += 1
+        for b in range(plan.nbox):
+            cs = list(origin)
+            if b:
+                cs[0] = f"({cs[0]} + {32 * b})"
+            self.emit(f"tila::tma_store_{plan.rank}d(&{tm}, tila_smem + {base} + {b * 16384}, {', '.join(cs)});")
+        self.emit("tila::bulk_commit();")
+        self.emit("tila::bulk_wait_read();")
+        self.indent -= 1
+        self.emit("}")
+        self.emit("__syncthreads();")
+        self.indent -= 1
+        self.emit("}")
+        return True
+
+    def _store_staging(self, size):
+        """Shared memory for a TMA store: a region freed by a finished
+        pipelined loop when one is large enough, else a new allocation
+        (None when that would not fit)."""
+        for off, n in self._free_smem:
+            if n >= size:
+                return off
+        if self.smem.top + size > 200 * 1024:
+            return None
+        return self.smem.alloc(size, 1024)
 
     def ptr_load(self, x, dt, shape):
         self.fail("Ptr-form loads are not supported by the B200 backend yet", x.line)

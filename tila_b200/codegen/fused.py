@@ -224,6 +224,8 @@ class FusedContractionMixin:
         self.emit("tila::tc_fence_after();")
         self.indent -= 1
         self.emit("}")
+        # every copy into the ring has been consumed by a completed MMA
+        self._free_smem.append((ring, S * stage))
         # epilogues, one program at a time (uniform branches: `live` depends on blockIdx)
         for (i, j) in inst:
             self.env = dict(envs[(i, j)])

@@ -102,7 +102,7 @@ class MmaMixin:
             self._tm_index[key] = name
             self.tensor_maps.append({"param": name, "buffer": plan.buffer,
                                      "box": list(plan.box_dims()), "swizzle": 128,
-                                     "dtype": "f16"})
+                                     "dtype": "f16" if plan.elem_bytes == 2 else "f32"})
         return self._tm_index[key]
 
     def _tma_coords(self, plan: TmaPlan, coords):
@@ -126,7 +126,7 @@ class MmaMixin:
         for b in range(plan.nbox):
             cs = list(coords_if)
             if b:
-                cs[0] = f"({cs[0]} + {64 * b})"
+                cs[0] = f"({cs[0]} + {plan.box_elems * b})"
             args = ", ".join(cs)
             self.emit(f"tila::tma_load_{rank}d(tila_smem + {dst} + {b * plan.box_bytes}, &{tm}, {bar}, {args});")
 
@@ -497,6 +497,8 @@ class MmaMixin:
         self.emit("tila::tc_fence_after();")
         self.indent -= 1
         self.emit("}")
+        # every copy into the ring has been consumed by a completed MMA
+        self._free_smem.append((ring, S * stage))
         from .emitter import Val
         for d in cl.dots:
             col, N = acc_cols[d.acc]
@@ -925,6 +927,13 @@ class AsyncLoopMixin:
         from .emitter import Val
         for name in ctx.accs:
             self.emit_acc_wait(name, release=False)
+        # all loop copies were consumed (the last iteration issues none)
+        spans = [(int(x["base"]), x["plan"].nbox * max(x["plan"].outer_extent, 128) * 128)
+                 for x in ctx.loads.values()]
+        if spans:
+            lo = min(b for b, _ in spans)
+            hi = max(b + n for b, n in spans)
+            self._free_smem.append((lo, hi - lo))
         for name, a in ctx.accs.items():
             self.env[name] = Val("tmem", D.f32, (128, a["N"]), tmem_col=str(a["col"]))
         self.actx = None

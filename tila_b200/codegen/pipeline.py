@@ -144,13 +144,14 @@ SWIZZLE_BYTES = 128          # 128-byte swizzle: inner box of 64 f16
 
 @dataclass
 class TmaPlan:
-    """A 2-D tile load performed as TMA box copies into shared memory.
+    """A 2-D tile copied between global and shared memory as TMA boxes.
 
     ``row_axis``/``col_axis``: buffer axes following tile dims 0 / 1.
     ``inner``: tile dim (0 or 1) lying along the buffer's contiguous axis.
-    The tile is copied as ``nbox`` boxes of 64 contiguous elements; box b
-    covers inner indices [64 b, 64 b + 64) and lands ``outer * 128`` bytes
-    after box b - 1 (the UMMA SWIZZLE_128B canonical layout).
+    The tile is copied as ``nbox`` boxes of 128 contiguous bytes (64 f16 or
+    32 f32 elements); box b covers inner indices [E b, E b + E) and lands
+    ``outer * 128`` bytes after box b - 1 (the UMMA SWIZZLE_128B canonical
+    layout for f16 operands).
     """
     buffer: str
     rank: int
@@ -170,8 +171,13 @@ class TmaPlan:
         return self.shape[self.inner]
 
     @property
+    def box_elems(self):
+        """Elements of the innermost box dim: 128 bytes (the swizzle span)."""
+        return 128 // self.elem_bytes
+
+    @property
     def nbox(self):
-        return self.inner_extent // 64
+        return self.inner_extent // self.box_elems
 
     @property
     def box_bytes(self):
@@ -186,7 +192,7 @@ class TmaPlan:
         dims = []
         for ax in reversed(range(self.rank)):
             if ax == self.rank - 1:
-                dims.append(64)
+                dims.append(self.box_elems)
             elif ax == self.row_axis:
                 dims.append(self.shape[0])
             elif ax == self.col_axis:
@@ -228,16 +234,31 @@ def _split_cmp(atom, defs):
     return None
 
 
-def plan_tma(load, dims, defs: Defs, consts, uniform_names, buffer_param, facts) -> TmaPlan | None:
-    """TMA plan for ``load`` (a TLoad with a 2-D f16 result), or None."""
+def plan_tma_store(store, dims, defs: Defs, consts, uniform_names, buffer_param, facts):
+    """TMA plan for a 2-D f32 tile ``store`` (TStore), or None: the same
+    conditions as a load (affine tile coordinates, mask = bounds of the
+    tiled coordinates), since a TMA store skips the box's out-of-bounds
+    elements exactly like the masked store."""
+    from types import SimpleNamespace
+    view = SimpleNamespace(buffer=store.buffer, ptr=None, coords=store.coords, other=None,
+                           mask=store.mask)
+    return plan_tma(view, dims, defs, consts, uniform_names, buffer_param, facts,
+                    dtypes=("f32",))
+
+
+def plan_tma(load, dims, defs: Defs, consts, uniform_names, buffer_param, facts,
+             dtypes=("f16",)) -> TmaPlan | None:
+    """TMA plan for ``load`` (a TLoad with a 2-D result of one of ``dtypes``), or None."""
     if load.buffer is None or load.ptr is not None:
         return None
     if facts is None or not getattr(facts, "tma_ok", False):
         return None
     if len(dims) != 2:
         return None
-    if buffer_param.vtype.elem.name != "f16":
+    ename = buffer_param.vtype.elem.name
+    if ename not in dtypes:
         return None
+    elem_bytes = 2 if ename == "f16" else 4
     R, C = dims
     rank = len(load.coords)
     rows = cols = None
@@ -264,7 +285,7 @@ def plan_tma(load, dims, defs: Defs, consts, uniform_names, buffer_param, facts)
         return None
     inner_extent = dims[inner]
     outer_extent = dims[1 - inner]
-    if inner_extent % 64 or outer_extent > 256 or outer_extent < 8:
+    if inner_extent % (128 // elem_bytes) or outer_extent > 256 or outer_extent < 8:
         return None
     # other must be zero (TMA fills out-of-bounds elements with zero)
     if load.other is not None:
@@ -300,7 +321,7 @@ def plan_tma(load, dims, defs: Defs, consts, uniform_names, buffer_param, facts)
             r = defs.resolve(right)
             if not (isinstance(r, T_.TName) and getattr(d, "name", None) == r.name):
                 return None
-    return TmaPlan(load.buffer, rank, (R, C), rows, cols, inner, tuple(load.coords))
+    return TmaPlan(load.buffer, rank, (R, C), rows, cols, inner, tuple(load.coords), elem_bytes)
 
 
 # ---------------------------------------------------------------------------

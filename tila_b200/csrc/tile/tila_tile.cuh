@@ -413,6 +413,33 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const TensorMap *map, u64
         "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
+// TMA tile stores (shared -> global).  Elements of the box outside the
+// tensor are not written.  The issuing thread groups its stores with
+// bulk_commit() and must call bulk_wait_read() before the shared-memory
+// source is overwritten or the CTA exits.  Coordinates must be >= 0.
+__device__ __forceinline__ void tma_store_2d(const TensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<u64>(map)), "r"(smem_u32(src)), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const TensorMap *map, const void *src, int x, int y,
+                                             int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<u64>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const TensorMap *map, const void *src, int x, int y,
+                                             int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+               ::"l"(reinterpret_cast<u64>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z),
+                 "r"(w) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory and the 5th-generation tensor core
 // ---------------------------------------------------------------------------
