@@ -81,15 +81,18 @@ class MmaMixin:
     def _uniform_names(self):
         return set(self.scalar_params) | set(self._loopvars)
 
-    def tma_plan(self, load):
-        key = id(load)
+    def tma_plan(self, load, cast=False):
+        """TMA plan of a tile load: f16 MMA operands, or with ``cast`` also
+        f32 tiles that are read into registers."""
+        key = (id(load), cast)
         if key in self.tma_plans:
             return self.tma_plans[key]
         plan = None
         if load.buffer is not None and load.buffer in self.buffer_params:
             dt, shape, _ = self.vt_info(load.vt)
             plan = plan_tma(load, shape, self.pdefs, self.consts, self._uniform_names(),
-                            self.buffer_params[load.buffer], self.buffers.get(load.buffer))
+                            self.buffer_params[load.buffer], self.buffers.get(load.buffer),
+                            dtypes=("f16", "f32") if cast else ("f16",))
         self.tma_plans[key] = plan
         return plan
 
@@ -322,6 +325,45 @@ class MmaMixin:
         self.emit("tila::tc_fence_before();")
         return reg
 
+    def smem_rows_to_reg(self, v, lay):
+        """Read a TMA-copied (SWIZZLE_128B) tile whose columns run along the
+        buffer's contiguous axis into the row-per-thread register image
+        ``lay`` (TmemRows): 16-byte shared loads, four lanes per bank group."""
+        from .emitter import Val
+        plan = v.smem.plan
+        if plan.inner != 1 or plan.shape[0] != 128 or not isinstance(lay, TmemRows):
+            self.fail("row read of a shared-memory tile needs 128 rows with contiguous columns")
+        self.emit_smem_wait(v)
+        name = self.fresh("sr")
+        eb = plan.elem_bytes
+        per = 16 // eb                    # elements per 16-byte chunk
+        be = plan.box_elems
+        col0 = f"(tid >> 7) * {lay.cpg} + " if lay.groups > 1 else ""
+        self.emit(f"float {name}[{lay.nreg}];")
+        self.emit("{")
+        self.indent += 1
+        self.emit("const int row_ = tid & 127;")
+        self.emit("#pragma unroll")
+        self.emit(f"for (int r = 0; r < {lay.nreg}; r += {per}) {{")
+        self.indent += 1
+        self.emit(f"const int c_ = {col0}r;")
+        addr = (f"tila_smem + {v.smem.base} + (c_ / {be}) * {plan.box_bytes} + row_ * 128 + "
+                f"((((c_ % {be}) / {per}) ^ (row_ & 7)) * 16)")
+        if eb == 4:
+            self.emit(f"const float4 q_ = *reinterpret_cast<const float4*>({addr});")
+            self.emit(f"{name}[r] = q_.x; {name}[r + 1] = q_.y; {name}[r + 2] = q_.z; {name}[r + 3] = q_.w;")
+        else:
+            self.emit(f"const uint4 q_ = *reinterpret_cast<const uint4*>({addr});")
+            self.emit("const tila::u32 w_[4] = {q_.x, q_.y, q_.z, q_.w};")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int j = 0; j < 4; ++j) {{ {name}[r + 2 * j] = tila::h2f((tila::u16)(w_[j] & 0xffffu)); "
+                      f"{name}[r + 2 * j + 1] = tila::h2f((tila::u16)(w_[j] >> 16)); }}")
+        self.indent -= 1
+        self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+        return Val("reg", v.dt, tuple(v.shape), name=name, layout=lay)
+
     def smem_to_reg(self, v):
         """Read a TMA-loaded (SWIZZLE_128B) tile from shared memory into registers."""
         plan = v.smem.plan
@@ -553,7 +595,10 @@ class AsyncLoopMixin:
             dt, shape, _ = self.vt_info(dot.vt)
             return (dt.name == "f32" and len(shape) == 2 and shape[0] == 128 and
                     shape[1] % 16 == 0 and 16 <= shape[1] <= 256)
-        al = match_async_loop(s, self.pdefs, is_tma, is_smem, carried, acc_ok)
+        def is_cast_tma(ld):
+            plan = self.tma_plan(ld, cast=True)
+            return plan is not None and plan.inner == 1 and plan.shape[0] == 128
+        al = match_async_loop(s, self.pdefs, is_tma, is_smem, carried, acc_ok, is_cast_tma)
         if al is None:
             return None
         # B operands must be laid out for an N that the instruction accepts
@@ -566,8 +611,9 @@ class AsyncLoopMixin:
         self.uses_tmem = True
         ctx = AsyncCtx(al, s.var, stepv, f"(tila::i64)({end.expr})", {}, {})
         ctx.body = s.body
+        ctx.cast_loads = set(al.cast_loads)
         for name, ld in al.loads.items():
-            plan = self.tma_plan(ld)
+            plan = self.tma_plan(ld, cast=name in al.cast_loads)
             size = plan.nbox * max(plan.outer_extent, 128) * 128
             base = self.smem.alloc(size, 1024)
             bar_off = self.smem.alloc(8, 8)
@@ -793,12 +839,16 @@ class AsyncLoopMixin:
         bv = self.value(x.b)
         K = bv.shape[0]
         ts = isinstance(x.a, T_.TCast)
+        cast_src = None
         if ts:
             # cast[f16](R): round and pack pairs straight from R (one cvt per pair)
             pv = self.value(x.a.operand)
+            play = TmemRows((128, K), self.T)
+            if pv.kind == "smem":
+                cast_src = getattr(pv, "smem_name", None)
+                pv = self.smem_rows_to_reg(pv, play)
             if pv.dt.name not in ("f32", "f16"):
                 pv = self.coerce(pv, D.f32)
-            play = TmemRows((128, K), self.T)
             pv = self.materialize(pv, play) if not (pv.kind == "reg" and pv.layout == play) else pv
             half = play.nreg // 2
             self.emit("{")
@@ -824,6 +874,15 @@ class AsyncLoopMixin:
         self.emit("tila::tc_fence_after();")
         if getattr(ctx, "pingpong", False):
             self.emit(WG_RELEASE)
+        if cast_src is not None and cast_src in ctx.cast_loads:
+            # every thread has read the tile into registers: copy the next one
+            cur = self.env[ctx.var].expr
+            nxt = f"((tila::i64)({cur}) + {ctx.stepv})"
+            self.emit(f"if ({nxt} < {ctx.end}) {{")
+            self.indent += 1
+            self._emit_loop_copies(ctx, [cast_src], nxt)
+            self.indent -= 1
+            self.emit("}")
         b_mn = self._operand_desc(bv, "B", 0)[1]
         self.emit("if (tid == 0) {")
         self.indent += 1

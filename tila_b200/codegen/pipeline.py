@@ -443,6 +443,10 @@ class AsyncLoop:
     """
     accs: dict
     loads: dict
+    # loads consumed only through cast[f16](...) as the A operand of an
+    # accumulating dot: copied by TMA, read into registers, re-copied as soon
+    # as every thread has read them
+    cast_loads: set = field(default_factory=set)
 
 
 def _walk(node, fn):
@@ -459,7 +463,8 @@ def _walk(node, fn):
                 _walk(x, fn)
 
 
-def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_shape_ok):
+def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_shape_ok,
+                     is_tma_cast_load=None):
     body = loop.body
     if not body or any(not isinstance(s, T_.TAssign) for s in body):
         return None
@@ -470,6 +475,13 @@ def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_s
     for name, vals in assigned.items():
         if len(vals) == 1 and isinstance(vals[0], T_.TLoad) and is_tma_load(vals[0]):
             loads[name] = vals[0]
+    # candidates read only through a cast feeding an accumulating dot's A
+    cast_cands = {}
+    if is_tma_cast_load is not None:
+        for name, vals in assigned.items():
+            if name not in loads and len(vals) == 1 and isinstance(vals[0], T_.TLoad) \
+                    and is_tma_cast_load(vals[0]):
+                cast_cands[name] = vals[0]
     # how every name is used inside the body
     uses = {}
 
@@ -488,6 +500,15 @@ def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_s
     for name in list(loads):
         if not uses.get(name) or any(p != "TDot" or f not in ("a", "b") for p, f in uses[name]):
             del loads[name]
+    cast_loads = set()
+    for s in body:
+        v = s.value
+        if isinstance(v, T_.TDot) and isinstance(v.acc, T_.TName) and v.acc.name == s.name \
+                and isinstance(v.a, T_.TCast) and isinstance(v.a.operand, T_.TName):
+            n = v.a.operand.name
+            if n in cast_cands and uses.get(n) == [("TCast", "operand")]:
+                loads[n] = cast_cands[n]
+                cast_loads.add(n)
     accs = {}
     for s in body:
         v = s.value
@@ -499,7 +520,7 @@ def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_s
             a = v.a
             ok_a = (isinstance(a, T_.TName) and (a.name in loads or is_smem_name(a.name))) or \
                 (isinstance(a, T_.TCast) and a.dtype.name == "f16" and isinstance(a.operand, T_.TName)
-                 and a.operand.name not in loads)
+                 and (a.operand.name not in loads or a.operand.name in cast_loads))
             if not ok_a or s.name in accs:
                 return None
             accs[s.name] = v
@@ -526,4 +547,4 @@ def match_async_loop(loop, defs: Defs, is_tma_load, is_smem_name, carried, acc_s
             _walk(s.value, check)
         except ValueError:
             return None
-    return AsyncLoop(accs, loads)
+    return AsyncLoop(accs, loads, cast_loads)
