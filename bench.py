@@ -413,7 +413,7 @@ def run_ours(args, world, rank, device, keys):
         else:
             achieved = case.dominant_units / (dom_ms * 1e-3) / 1e12
             peak, runit = peaks["bf16_tflops"], "TFLOP/s"
-        tr = traffic.get(dom_kernel)
+        tr = traffic.get(f"{dom_kernel}@{key}") or traffic.get(dom_kernel)
         roof = {"bound": W_ROOF.get(key, "hbm"), "kernel": dom_kernel, "achieved": round(achieved, 2),
                 "peak": peak, "unit": runit, "frac": round(achieved / peak, 4),
                 "traffic": tr.get("bytes_per_launch") if tr else None,
