@@ -492,10 +492,16 @@ def _e2e(case, args, world, rank, device):
     one()
     if world > 1:
         dist.barrier()
-    t0 = time.perf_counter()
+    # device time of the whole sequence (copies, Tila's host checks while the
+    # stream waits, the launch, the read-back), max over ranks
+    cur = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
     for _ in range(steps):
         one()
-    dt = (time.perf_counter() - t0) / steps
+    e1.record(cur)
+    torch.cuda.synchronize(device)
+    dt = e0.elapsed_time(e1) * 1e-3 / steps
     if world > 1:
         t = torch.tensor([dt], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
