@@ -457,6 +457,7 @@ def _gather(out, case, world, rank, device):
     import torch
     import torch.distributed as dist
     from tila_b200.multigpu import gather_leading
+    gather_leading(out, world, rank)        # first call sets up the communicator's buffers
     dist.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
