@@ -398,6 +398,17 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             exprs = [self.elem(v, layout, "r") for v in ops]
             if isinstance(make_expr, _UniformDivisor) and not re.search(r"\br\b", exprs[1]):
                 self._uniform_division(name, None, exprs[1], exprs[0], layout.nreg)
+            elif isinstance(make_expr, _PackedBin) and dt.name == "f32" and layout.nreg % 2 == 0 \
+                    and layout.nreg >= 4:
+                # two elements per f32x2 instruction
+                e0 = [self.elem(v, layout, "(r)") for v in ops]
+                e1 = [self.elem(v, layout, "(r + 1)") for v in ops]
+                args = ", ".join(f"tila::pk2({a}, {b})" for a, b in zip(e0, e1))
+                self.emit("#pragma unroll")
+                self.emit(f"for (int r = 0; r < {layout.nreg}; r += 2) {{")
+                self.emit(f"  const tila::u64 q_ = tila::{make_expr.fn}({args});")
+                self.emit(f"  {name}[r] = tila::lo2(q_); {name}[r + 1] = tila::hi2(q_);")
+                self.emit("}")
             else:
                 self.emit("#pragma unroll")
                 self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
@@ -415,6 +426,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if rows is not None:
             for r, a in rows:
                 self.emit(f"{name}[{r}] = tila::udiv_fast(({a}), {ud}, {ud}_hi, {ud}_lo);")
+        elif nreg % 2 == 0:
+            d0 = re.sub(r"\br\b", "(r)", dividend)
+            d1 = re.sub(r"\br\b", "(r + 1)", dividend)
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {nreg}; r += 2) "
+                      f"tila::udiv_fast2(({d0}), ({d1}), {ud}, {ud}_hi, {ud}_lo, {name}[r], {name}[r + 1]);")
         else:
             self.emit("#pragma unroll")
             self.emit(f"for (int r = 0; r < {nreg}; ++r) {name}[r] = "
@@ -783,6 +800,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if DT.is_float(odt):
             if op == "/" and odt.name == "f32" and rdt.name == "f32":
                 return _UniformDivisor()
+            if op in ("+", "-", "*") and odt.name == "f32" and rdt.name == "f32":
+                return _PackedBin(op)
             if op in ("+", "-", "*", "/"):
                 return lambda e: DT.round_to(rdt, f"(({e[0]}) {op} ({e[1]}))")
             if op == "//":
@@ -899,6 +918,15 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             for r in range(lay.nreg):
                 c = self._owner_cond(lay, r)
                 self.emit(f"if ({c}) {part} = {fold(part, conv(f'{v.name}[{r}]'))};")
+        elif op == "sum" and acc_dt.name == "f32" and lay.nreg % 2 == 0 and lay.nreg >= 8:
+            # two interleaved trees in the lanes of f32x2 additions
+            pairs = [f"tila::pk2({conv(f'{v.name}[{r}]')}, {conv(f'{v.name}[{r + 1}]')})"
+                     for r in range(0, lay.nreg, 2)]
+            t = self.fresh("ps")
+            self.emit(f"const tila::u64 {t} = {_tree_fold(pairs, lambda a, b: f'tila::add2({a}, {b})')};")
+            self.emit(f"{part} = ((tila::lo2({t})) + (tila::hi2({t})));")
+            if own is not None:
+                self.emit(f"if (!({own})) {part} = {self._identity(op, acc_dt)};")
         else:
             # balanced tree inside the thread (short dependency chains)
             self.emit(f"{part} = {_tree_fold([conv(f'{v.name}[{r}]') for r in range(lay.nreg)], fold)};")
@@ -1949,6 +1977,18 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma,
                           tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
+
+
+class _PackedBin:
+    """Expression maker of an f32 +, - or *; register tiles with an even
+    number of slots are materialised two elements per f32x2 instruction."""
+
+    def __init__(self, op):
+        self.op = op
+        self.fn = {"+": "add2", "-": "sub2", "*": "mul2"}[op]
+
+    def __call__(self, e):
+        return f"(({e[0]}) {self.op} ({e[1]}))"
 
 
 class _UniformDivisor:

@@ -971,8 +971,15 @@ class AsyncLoopMixin:
         self.emit(f"float t_[{chunk}];")
         self.emit(f"tila::tmem_load_row<{chunk}>({base} + ch, t_);")
         self.emit("#pragma unroll")
-        e = mk(["t_[j]", "o_"] if acc_left else ["o_", "t_[j]"])
-        self.emit(f"for (int j = 0; j < {chunk}; ++j) t_[j] = {e};")
+        if getattr(mk, "fn", None) and chunk % 2 == 0:
+            # two columns per f32x2 instruction
+            xt, xo = ("tila::pk2(t_[j], t_[j + 1])", "tila::pk2(o_, o_)")
+            args = f"{xt}, {xo}" if acc_left else f"{xo}, {xt}"
+            self.emit(f"for (int j = 0; j < {chunk}; j += 2) {{ const tila::u64 q_ = tila::{mk.fn}({args}); "
+                      f"t_[j] = tila::lo2(q_); t_[j + 1] = tila::hi2(q_); }}")
+        else:
+            e = mk(["t_[j]", "o_"] if acc_left else ["o_", "t_[j]"])
+            self.emit(f"for (int j = 0; j < {chunk}; ++j) t_[j] = {e};")
         self.emit(f"tila::tmem_store_row<{chunk}>({base} + ch, t_);")
         self.indent -= 1
         self.emit("}")
