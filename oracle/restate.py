@@ -55,11 +55,14 @@ def matmul_bound(a, b):
                                             np.abs(np.asarray(b, np.float64)))
 
 
-def attention_f64(q, k, v, scale=None):
-    """softmax(Q K^T * scale) V in f64 (tests/gpu_examples.py:67-73)."""
+def attention_f64(q, k, v, scale=None, causal=False):
+    """softmax(Q K^T * scale) V in f64, optionally with the causal mask
+    (tests/gpu_examples.py:67-73)."""
     q64, k64, v64 = (np.asarray(t, np.float64) for t in (q, k, v))
     scale = q.shape[-1] ** -0.5 if scale is None else scale
     s = q64 @ k64.swapaxes(-1, -2) * scale
+    if causal:
+        s = np.where(np.tril(np.ones(s.shape[-2:], bool)), s, -np.inf)
     p = np.exp(s - s.max(axis=-1, keepdims=True))
     p /= p.sum(axis=-1, keepdims=True)
     return p @ v64

@@ -1,0 +1,58 @@
+"""The B200 backend on the golden fixtures (the reference's example kernels'
+inputs and interpreter outputs, tests/golden/): the same programs launched on
+CUDA tensors, held to the reference suite's bars - add bit-exact, softmax
+rtol 1e-6, matmul K*eps_f32 elementwise, attention (causal and not) 2e-3."""
+
+import numpy as np
+import pytest
+import torch
+
+import tila_b200
+from tila_b200 import workloads as W
+from oracle import restate
+from test_oracle import CASES, load, our_program
+
+pytestmark = pytest.mark.gpu
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_golden_on_b200(case):
+    inputs, want, meta = load(case)
+    prog, consts = our_program(meta)
+    out = torch.zeros(want.shape, dtype=torch.float32, device="cuda")
+    prog[tuple(meta["grid"])](*(_cuda(a) for a in inputs), out, *meta["scalars"], **consts)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    got = out.cpu().numpy()
+    ex = meta["example"]
+    if ex.endswith("add_kernel.py"):
+        np.testing.assert_array_equal(got, want)
+    elif ex.endswith("softmax.py"):
+        np.testing.assert_allclose(got, want, rtol=1e-6, atol=0)
+    elif ex.endswith("matmul.py"):
+        a, b = inputs
+        assert np.all(np.abs(got - restate.matmul_f64(a, b)) <= restate.matmul_bound(a, b))
+        assert restate.rel_frobenius(got, want) <= 2e-3
+    else:
+        causal = ex.endswith("self_attention.py") or meta["consts"].get("CAUSAL", 0) == 1
+        ref = restate.attention_f64(*inputs, scale=meta["scalars"][0], causal=causal)
+        np.testing.assert_allclose(got, ref, rtol=2e-3, atol=2e-3)
+        assert restate.rel_frobenius(got, want) <= 2e-3
+
+
+@pytest.mark.parametrize("l,d", [(128, 64), (300, 64), (384, 128)])
+def test_causal_flash_attention_128_tiles(l, d):
+    """The two-stage causal kernel (stage loops whose trip count depends on
+    program_id(0): one program per CTA) at 128x128 tiles."""
+    q, k, v = W.attention_inputs(2, l, d, seed=17)
+    o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    W.flash_attention_causal[(-(-l // 128), 2)](_cuda(q), _cuda(k), _cuda(v), o, d ** -0.5,
+                                                BM=128, BN=128, BD=d)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    ref = restate.attention_f64(q, k, v, causal=True)
+    assert restate.rel_frobenius(o.cpu().numpy(), ref) <= 2e-3

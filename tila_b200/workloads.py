@@ -198,6 +198,109 @@ def flash_attention(
 
 
 # ---------------------------------------------------------------------------
+# causal variants (the adjacent kernels of the same examples: the CAUSAL=1
+# branch of examples/fused_attention.py:62-103 and examples/self_attention.py)
+# ---------------------------------------------------------------------------
+
+@ti.jit
+def flash_attention_causal(
+    q: ti.Buffer[ti.f16, (BH, L, BD), ti.ReadOnly],
+    k: ti.Buffer[ti.f16, (BH, L, BD), ti.ReadOnly],
+    v: ti.Buffer[ti.f16, (BH, L, BD), ti.ReadOnly],
+    o: ti.Buffer[ti.f32, (BH, L, BD), ti.WriteOnly],
+    sm_scale: ti.f32 | ti.Positive,
+    BM: ti.Const[int, ti.PowerOfTwo] = 64,
+    BN: ti.Const[int, ti.PowerOfTwo] = 64,
+    BD: ti.Const[int, ti.PowerOfTwo] = 64,
+):
+    # two stages: key blocks strictly below the diagonal band need no mask;
+    # the band [qb*BM, qb*BM + BM) applies the causal mask as an additive bias
+    qb = ti.program_id(0)
+    h = ti.program_id(1)
+    qi = qb * BM + ti.arange(0, BM)
+    kn = ti.arange(0, BN)
+    di = ti.arange(0, BD)
+    q_ok = qi < L
+    qt = ti.load(q, (h, qi[:, None], di[None, :]), mask=q_ok[:, None])
+    scale2 = sm_scale * LOG2E
+    m_run = ti.zeros((BM, 1), ti.f32) - 1.0e30
+    l_run = ti.zeros((BM, 1), ti.f32)
+    acc = ti.zeros((BM, BD), ti.f32)
+    for n0 in ti.range(0, qb * BM, BN):
+        ki = n0 + kn
+        k_ok = ki < L
+        kt = ti.load(k, (h, ki[None, :], di[:, None]), mask=k_ok[None, :])
+        sc = ti.dot(qt, kt) * scale2
+        m_blk = ti.max(sc, 1)[:, None]
+        m_new = ti.where(m_blk > m_run, m_blk, m_run)
+        corr = ti.exp2(m_run - m_new)
+        pr = ti.exp2(sc - m_new)
+        vt = ti.load(v, (h, ki[:, None], di[None, :]), mask=k_ok[:, None])
+        l_blk = ti.sum(pr, 1)
+        acc = acc * corr
+        acc = ti.dot(ti.cast[ti.f16](pr), vt, acc=acc)
+        l_run = l_run * corr + l_blk[:, None]
+        m_run = m_new
+    for n0 in ti.range(qb * BM, qb * BM + BM, BN):
+        ki = n0 + kn
+        k_ok = ki < L
+        keep = (qi[:, None] >= ki[None, :]) & k_ok[None, :]
+        kt = ti.load(k, (h, ki[None, :], di[:, None]), mask=k_ok[None, :])
+        sc = ti.dot(qt, kt) * scale2 + ti.where(keep, 0.0, -1.0e6)
+        m_blk = ti.max(sc, 1)[:, None]
+        m_new = ti.where(m_blk > m_run, m_blk, m_run)
+        corr = ti.exp2(m_run - m_new)
+        pr = ti.exp2(sc - m_new)
+        vt = ti.load(v, (h, ki[:, None], di[None, :]), mask=k_ok[:, None])
+        l_blk = ti.sum(pr, 1)
+        acc = acc * corr
+        acc = ti.dot(ti.cast[ti.f16](pr), vt, acc=acc)
+        l_run = l_run * corr + l_blk[:, None]
+        m_run = m_new
+    ti.store(o, (h, qi[:, None], di[None, :]), acc / l_run, mask=q_ok[:, None])
+
+
+@ti.jit
+def causal_self_attention(
+    q: ti.Buffer[ti.f16, (M, BD), ti.ReadOnly],
+    k: ti.Buffer[ti.f16, (N, BD), ti.ReadOnly],
+    v: ti.Buffer[ti.f16, (N, BD), ti.ReadOnly],
+    o: ti.Buffer[ti.f32, (M, BD), ti.WriteOnly],
+    scale: ti.f32 | ti.Positive,
+    BM: ti.Const[int, ti.PowerOfTwo] = 64,
+    BN: ti.Const[int, ti.PowerOfTwo] = 64,
+    BD: ti.Const[int, ti.PowerOfTwo] = 64,
+):
+    # one loop over every key block; masked scores are replaced (not biased)
+    # and exp runs in the natural base
+    qb = ti.program_id(0)
+    qi = qb * BM + ti.arange(0, BM)
+    kn = ti.arange(0, BN)
+    di = ti.arange(0, BD)
+    q_ok = qi < M
+    qt = ti.load(q, (qi[:, None], di[None, :]), mask=q_ok[:, None])
+    m_run = ti.zeros((BM, 1), ti.f32) - 1.0e30
+    l_run = ti.zeros((BM, 1), ti.f32)
+    acc = ti.zeros((BM, BD), ti.f32)
+    for n0 in ti.range(0, N, BN):
+        ki = n0 + kn
+        k_ok = ki < N
+        keep = (qi[:, None] >= ki[None, :]) & k_ok[None, :]
+        kt = ti.load(k, (ki[None, :], di[:, None]), mask=k_ok[None, :] & (di[:, None] >= 0))
+        sc = ti.where(keep, ti.dot(qt, kt) * scale, -1.0e30)
+        m_blk = ti.max(sc, 1)[:, None]
+        m_new = ti.where(m_blk > m_run, m_blk, m_run)
+        corr = ti.exp(m_run - m_new)
+        pr = ti.where(keep, ti.exp(sc - m_new), 0.0)
+        vt = ti.load(v, (ki[:, None], di[None, :]), mask=k_ok[:, None])
+        acc = acc * corr
+        l_run = l_run * corr + ti.sum(pr, 1)[:, None]
+        acc = ti.dot(ti.cast[ti.f16](pr), vt, acc=acc)
+        m_run = m_new
+    ti.store(o, (qi[:, None], di[None, :]), acc / l_run, mask=q_ok[:, None])
+
+
+# ---------------------------------------------------------------------------
 # configurations (the judged sizes) and their synthetic inputs
 # ---------------------------------------------------------------------------
 
