@@ -11,8 +11,10 @@ its algorithmic work (bytes or flops) for the roofline.
 The programs express the algorithms of the reference examples
 (examples/add_kernel.py:12-27, examples/softmax.py:14-29,
 examples/matmul.py:10-40, examples/fused_attention.py:104-126 for the
-non-causal loop); ``tests/test_workload_equivalence.py`` checks, on the
-interpreter, that they produce bit-identical results to those examples.
+non-causal loop; the causal variants follow examples/fused_attention.py:62-103
+and examples/self_attention.py); ``tests/test_oracle.py`` checks, on the
+interpreter, that they produce bit-identical results to those examples on the
+fixtures in ``tests/golden/``.
 """
 
 from __future__ import annotations
