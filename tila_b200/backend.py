@@ -165,7 +165,16 @@ def compile_kernel(jf, consts, facts, num_warps, context=None) -> Compiled:
                         Loc(exc.line),
                         fixes=["restructure the kernel, or run it on CPU arrays (interpreter)"]) from exc
     try:
-        cubin = native.compile_spec(spec)
+        try:
+            cubin = native.compile_spec(spec)
+        except native.NativeError as exc:
+            # a kernel whose loop bodies do not fit the register file once
+            # specialised for interior tiles is compiled with one body per loop
+            if "Register allocation failed" not in (exc.log or ""):
+                raise
+            spec = KernelEmitter(tk, consts, facts, num_warps=num_warps, debug=_debug(),
+                                 versioning=False).generate()
+            cubin = native.compile_spec(spec)
         lib = native.Library(cubin)
         kern = lib.kernel(spec.name)
     except native.NativeError as exc:

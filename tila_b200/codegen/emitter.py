@@ -174,8 +174,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
-                 entry_name=None, debug=False):
+                 entry_name=None, debug=False, versioning=True):
         self.tk = tk
+        self.versioning = versioning     # loop bodies specialised for interior tiles
         self.consts = dict(consts)
         self.buffers = buffers
         self.T = 32 * num_warps
@@ -1589,9 +1590,22 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.fail("loop step is zero", s.line)
         assigned = _stmt_names_assigned(s.body)
         carried = sorted(n for n in assigned if n in self.env and n != s.var)
+        # names first assigned inside the body are local to it (their C++
+        # variables live in the loop's scope): unbound after the loop
+        local = [n for n in assigned if n not in self.env and n != s.var]
         # the loop variable's divisibility (for vector alignment proofs)
         sdiv = _pow2_div(int(start.const)) if start.const is not None else 1
         self._loopvars[s.var] = min(sdiv, _pow2_div(abs(stepv)))
+        self.pdefs.scopes.append(self.pdefs.loop_locals(s.body))
+        try:
+            self._emit_for(s, start, end, stepv, carried)
+        finally:
+            self.pdefs.scopes.pop()
+        self.env.pop(s.var, None)
+        for n in local:
+            self.env.pop(n, None)
+
+    def _emit_for(self, s, start, end, stepv, carried):
         if self.try_contraction_loop(s, start, end, stepv, carried):
             return
         actx = None
@@ -1637,7 +1651,6 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.env[n] = st
         if actx is not None:
             self.finish_async_loop(actx)
-        self.env.pop(s.var, None)
 
     # -- loop-body versioning on tile bound checks ---------------------------------
 
@@ -1646,6 +1659,10 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         bound comparison ``uniform + arange < uniform`` of the body is known
         to hold on the whole tile, selected by one uniform guard per
         iteration (interior tiles skip their mask arithmetic)."""
+        if not self.versioning:
+            self.stmts(body)
+            self._assign_merged(storage)
+            return
         env0, cc0 = dict(self.env), dict(self.conv_cache)
         outer = self.lines
         self.lines = []

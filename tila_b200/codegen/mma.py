@@ -615,7 +615,7 @@ class AsyncLoopMixin:
         for name, ld in al.loads.items():
             plan = self.tma_plan(ld, cast=name in al.cast_loads)
             size = plan.nbox * max(plan.outer_extent, 128) * 128
-            base = self.smem.alloc(size, 1024)
+            base = self._reuse_smem(size)
             bar_off = self.smem.alloc(8, 8)
             ctx.loads[name] = dict(plan=plan, node=ld, base=str(base),
                                    bar=f"reinterpret_cast<tila::u64*>(tila_smem + {bar_off})",
@@ -677,6 +677,15 @@ class AsyncLoopMixin:
             self._wg_candidate = True
         self.actx = ctx
         return ctx
+
+    def _reuse_smem(self, size):
+        """1024-aligned shared memory for a loop buffer: part of a region a
+        finished pipelined loop released, else a new allocation."""
+        for i, (off, n) in enumerate(self._free_smem):
+            if n >= size:
+                self._free_smem[i] = (off + size, n - size)
+                return off
+        return self.smem.alloc(size, 1024)
 
     def _pingpong_ok(self, s, start, al):
         """Two programs of grid axis 0 may share a CTA, one per warpgroup,

@@ -37,6 +37,7 @@ class Defs:
     def __init__(self, body):
         self.defs = {}
         self.count = {}
+        self.scopes = []          # loop-local definitions of the bodies being emitted
         self._collect(body)
 
     def _collect(self, body):
@@ -53,10 +54,54 @@ class Defs:
 
     def resolve(self, node):
         seen = 0
-        while isinstance(node, T_.TName) and self.count.get(node.name) == 1 and seen < 64:
-            node = self.defs[node.name]
+        while isinstance(node, T_.TName) and seen < 64:
+            for scope in reversed(self.scopes):
+                if node.name in scope:
+                    node = scope[node.name]
+                    break
+            else:
+                if self.count.get(node.name) != 1:
+                    break
+                node = self.defs[node.name]
             seen += 1
         return node
+
+    @staticmethod
+    def loop_locals(body):
+        """Names assigned exactly once in ``body`` (a loop's statement list,
+        nested statements included) and never read in it before that
+        assignment: their value inside the body is that single definition
+        (names reused by another loop resolve per loop)."""
+        order = []
+
+        def flat(stmts):
+            for st in stmts:
+                order.append(st)
+                if isinstance(st, (T_.TIf, T_.TStaticIf)):
+                    flat(st.then_body)
+                    flat(st.else_body)
+                elif isinstance(st, T_.TFor):
+                    flat(st.body)
+        flat(body)
+        count = {}
+        for st in order:
+            if isinstance(st, T_.TAssign):
+                count[st.name] = count.get(st.name, 0) + 1
+        out, defined, read_early = {}, set(), set()
+        for st in order:
+            names = []
+            for fld in getattr(st, "__dataclass_fields__", {}):
+                if fld in ("vt", "definition", "effect", "body", "then_body", "else_body", "name"):
+                    continue
+                _walk(getattr(st, fld), lambda n: names.append(n.name) if isinstance(n, T_.TName) else None)
+            for n in names:
+                if n not in defined:
+                    read_early.add(n)
+            if isinstance(st, T_.TAssign):
+                defined.add(st.name)
+                if count[st.name] == 1 and st.name not in read_early:
+                    out[st.name] = st.value
+        return out
 
 
 def canon(node, defs: Defs, expand=None) -> str:
