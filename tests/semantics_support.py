@@ -159,3 +159,41 @@ def kernel(x: ti.Buffer[ti.f32, (N,), ti.ReadOnly],
     ok = i < N
     ti.store(out, i, ti.load(x, i, mask=ok) / {divisor}, mask=ok)
 ''')
+
+
+def atomic_program(directory, dtype="i32", kind="buffer"):
+    """Every lane adds ``values[i]`` to x[offset] (offset 0 for all lanes, or
+    its own lane) and stores the old value it saw; ``kind`` selects the
+    Buffer form (x, offset) or the Ptr form (x + offset)."""
+    annotation = (f"ti.Buffer[ti.{dtype}, (64,), ti.ReadWrite]" if kind == "buffer"
+                  else f"ti.RWPtr[ti.{dtype}, 64]")
+    target = "x, offset" if kind == "buffer" else "x + offset"
+    return load_source(directory, f"sem_atomic_{dtype}_{kind}", f'''import tila as ti
+
+@ti.jit
+def kernel(x: {annotation}, values: ti.Buffer[ti.{dtype}, (64,), ti.ReadOnly],
+           old: ti.Buffer[ti.{dtype}, (64,), ti.WriteOnly],
+           COUNT: ti.Const[int] = 64, COLLIDE: ti.Const[bool] = True):
+    i = ti.program_id(0) * 32 + ti.arange(0, 32)
+    if COLLIDE:
+        offset = i * 0
+    else:
+        offset = i
+    value = ti.load(values, i, mask=i < COUNT, other=0)
+    before = ti.atomic_add({target}, value, mask=i < COUNT)
+    ti.store(old, i, before, mask=i < 64)
+''')
+
+
+def ptr_copy_program(directory, dtype="f32"):
+    """out[i] = 2 * x[i] through Ptr parameters (x + i, out + i)."""
+    return load_source(directory, f"sem_ptr_copy_{dtype}", f'''import tila as ti
+N = ti.Dim("N")
+
+@ti.jit
+def kernel(x: ti.ReadPtr[ti.{dtype}, N], out: ti.WritePtr[ti.{dtype}, N]):
+    i = ti.program_id(0) * 64 + ti.arange(0, 64)
+    ok = i < N
+    v = ti.load(x + i, mask=ok, other=0)
+    ti.store(out + i, v + v, mask=ok)
+''')

@@ -154,3 +154,20 @@ def test_f32_tile_epilogues_store_through_tma():
     # a column offset that is not a multiple of 4 elements keeps plain stores
     t = dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000))
     assert "tma_store" not in gen(W.row_softmax, t, BN=1024).source
+
+
+@pytest.mark.parametrize("dt", ["i32", "u32", "f32"])
+@pytest.mark.parametrize("kind", ["buffer", "ptr"])
+def test_atomic_programs_compile(dt, kind, tmp_path):
+    import semantics_support as S
+    k = S.atomic_program(tmp_path, dt, kind)
+    t = dict(x=_dev_like(64, dt), values=_dev_like(64, dt), old=_dev_like(64, dt))
+    for collide in (True, False):
+        src = gen(k, t, COUNT=61, COLLIDE=collide).source
+        assert "atomicAdd(" in src
+
+
+def test_ptr_programs_compile(tmp_path):
+    import semantics_support as S
+    k = S.ptr_copy_program(tmp_path, "f32")
+    gen(k, dict(x=torch.zeros(100), out=torch.zeros(100)))

@@ -291,3 +291,68 @@ def test_division_by_uniform_divisor_many_pairs():
     kernel[(g,)](up(x, "f32"), out, up(y, "f32"))
     torch.cuda.synchronize()
     _same_bits(down(out), x / np.repeat(d, 1024))
+
+
+ATOMIC_NP = dict(i32=np.int32, u32=np.uint32, f32=np.float32)
+
+
+@pytest.mark.parametrize("dtype", ["i32", "u32", "f32"])
+@pytest.mark.parametrize("kind", ["buffer", "ptr"])
+@pytest.mark.parametrize("count", [0, 5, 61, 64])
+def test_atomic_tickets_and_tail(dtype, kind, count):
+    """All lanes add 1 to x[0]: the old values are the tickets 0..count-1 in
+    some order and the masked tail reads 0 (tests/gpu_atomic.py:23-40)."""
+    kernel = S.atomic_program(KDIR, dtype, kind)
+    npd = ATOMIC_NP[dtype]
+    values = np.ones(64, npd)
+    cpu, old_cpu = np.zeros(64, npd), np.zeros(64, npd)
+    kernel[(2,)](cpu, values, old_cpu, COUNT=count)
+    x = torch.zeros(64, dtype=TORCH[dtype], device="cuda")
+    old = torch.zeros(64, dtype=TORCH[dtype], device="cuda")
+    for _ in range(3):
+        x.zero_()
+        kernel[(2,)](x, up(values, dtype), old, COUNT=count)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(down(x), cpu)
+        tickets = down(old)
+        np.testing.assert_array_equal(np.sort(tickets[:count]), np.arange(count, dtype=npd))
+        np.testing.assert_array_equal(tickets[count:], 0)
+    assert tila_b200.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", ["i32", "u32", "f32"])
+@pytest.mark.parametrize("kind", ["buffer", "ptr"])
+def test_atomic_noncolliding(dtype, kind):
+    """Each lane updates its own element: the result and the old values are
+    deterministic and equal the interpreter's, wrapping at the integer ends."""
+    kernel = S.atomic_program(KDIR, dtype, kind)
+    npd = ATOMIC_NP[dtype]
+    initial = np.arange(64).astype(npd)
+    if dtype == "i32":
+        initial[1] = 2**31 - 1
+    if dtype == "u32":
+        initial[1] = 2**32 - 1
+    values = np.ones(64, npd)
+    cpu, old_cpu = initial.copy(), np.zeros(64, npd)
+    kernel[(2,)](cpu, values, old_cpu, COUNT=61, COLLIDE=False)
+    x = up(initial.copy(), dtype)
+    old = torch.zeros(64, dtype=TORCH[dtype], device="cuda")
+    kernel[(2,)](x, up(values, dtype), old, COUNT=61, COLLIDE=False)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(down(x), cpu)
+    np.testing.assert_array_equal(down(old), old_cpu)
+
+
+@pytest.mark.parametrize("n", [1, 64, 100, 1000])
+def test_ptr_form_load_store(n):
+    """Ptr parameters with element offsets (x + i) load and store like the
+    Buffer form, masked tail included."""
+    kernel = S.ptr_copy_program(KDIR, "f32")
+    x = np.random.default_rng(313).normal(size=n).astype(np.float32)
+    cpu = np.zeros(n, np.float32)
+    kernel[(-(-n // 64),)](x, cpu)
+    out = torch.zeros(n, device="cuda")
+    kernel[(-(-n // 64),)](up(x, "f32"), out)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(down(out), cpu)
+    np.testing.assert_array_equal(cpu, x + x)

@@ -1437,17 +1437,187 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             return None
         return self.smem.alloc(size, 1024)
 
-    def ptr_load(self, x, dt, shape):
-        self.fail("Ptr-form loads are not supported by the B200 backend yet", x.line)
-
-    def ptr_store(self, s):
-        self.fail("Ptr-form stores are not supported by the B200 backend yet", s.line)
+    # -- Ptr form (interp.py:357-384): a base pointer plus element offsets ------
 
     def e_TBufPtr(self, x):
-        self.fail("buffer pointers are not supported by the B200 backend yet", getattr(x, "line", 0))
+        src = self.ptr_params.get(x.buffer) or self.buffer_params[x.buffer]
+        return Val("ptr", src.vtype.elem, ptr=(x.buffer, None))
+
+    def e_TPAdd(self, x):
+        p = self.value(x.ptr)
+        if p.kind != "ptr":
+            self.fail("pointer arithmetic on a non-pointer value")
+        off = self.coerce(self.value(x.offset), D.i64)
+        name, cur = p.ptr
+        if cur is not None:
+            off = self.combine(D.i64, _broadcast_shapes([cur.shape, off.shape]), [cur, off],
+                               lambda e: f"tila::wadd<tila::i64>({e[0]}, {e[1]})")
+        return Val("ptr", p.dt, tuple(off.shape), ptr=(name, off))
+
+    def _ptr_target(self, ptr_node):
+        p = self.value(ptr_node)
+        if p.kind != "ptr":
+            self.fail("expected a pointer value")
+        name, off = p.ptr
+        if off is None:
+            off = Val("scalar", D.i64, expr="0", const=0)
+        return name, off
+
+    def ptr_load(self, x, dt, shape):
+        name, off = self._ptr_target(x.ptr)
+        mask = self.value(x.mask) if x.mask is not None else None
+        other = self.coerce(self.value(x.other), dt) if x.other is not None else None
+        fill0 = DT.literal(dt, 0)
+        if not shape:
+            fill = other.expr if other is not None else fill0
+            ld = DT.load_conv(dt, f"p_{name}[(tila::i64)({off.expr})]")
+            v = self.fresh("pl")
+            cond = f"({mask.expr})" if mask is not None else "true"
+            self.emit(f"const {DT.ctype(dt)} {v} = {cond} ? {ld} : {fill};")
+            return Val("scalar", dt, expr=v)
+        layout = self.default_layout(shape, dt)
+        ops = [off] + ([mask] if mask is not None else []) + ([other] if other is not None else [])
+        ops, maps, straight = self.prepare_operands(ops, layout, shape)
+        name_v = self.fresh("pl")
+        self.emit(f"{DT.ctype(dt)} {name_v}[{layout.nreg}];")
+        valid = layout.valid_expr()
+        rng = range(layout.nreg) if straight else ["r"]
+        if not straight:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+            self.indent += 1
+        for r in rng:
+            oe = self.elem(ops[0], layout, r, maps[0])
+            conds = [f"({valid})"] if valid is not None else []
+            if mask is not None:
+                conds.append(f"({self.elem(ops[1], layout, r, maps[1])})")
+            fill = self.elem(ops[-1], layout, r, maps[-1]) if other is not None else fill0
+            ld = DT.load_conv(dt, f"p_{name}[(tila::i64)({oe})]")
+            c = " && ".join(conds) if conds else "true"
+            self.emit(f"{name_v}[{r}] = ({c}) ? {ld} : {fill};")
+        if not straight:
+            self.indent -= 1
+            self.emit("}")
+        return Val("reg", dt, tuple(shape), name=name_v, layout=layout)
+
+    def ptr_store(self, s):
+        name, off = self._ptr_target(s.ptr)
+        dt = self.ptr_params[name].vtype.elem if name in self.ptr_params else \
+            self.buffer_params[name].vtype.elem
+        value = self.value(s.value)
+        value = self.coerce(value, dt) if value.dt.name != dt.name else value
+        mask = self.value(s.mask) if s.mask is not None else None
+        shapes = [off.shape, value.shape] + ([mask.shape] if mask is not None else [])
+        shape = _broadcast_shapes(shapes)
+        if not shape:
+            cond = "tid == 0" + (f" && ({mask.expr})" if mask is not None else "")
+            self.emit(f"if ({cond}) p_{name}[(tila::i64)({off.expr})] = {DT.store_conv(dt, value.expr)};")
+            return
+        if value.kind == "tmem":
+            value = self.tmem_to_reg(value)
+        layout = value.layout if value.kind == "reg" and tuple(value.shape) == tuple(shape) \
+            else self.default_layout(shape, dt)
+        ops = [off, value] + ([mask] if mask is not None else [])
+        ops, maps, straight = self.prepare_operands(ops, layout, shape)
+        own = owner_predicate(layout)
+        if own == "PER_SLOT":
+            straight = True
+        valid = layout.valid_expr()
+        self.emit("{")
+        self.indent += 1
+        if own is not None and own != "PER_SLOT":
+            self.emit(f"if ({own}) {{")
+            self.indent += 1
+        rng = range(layout.nreg) if straight else ["r"]
+        if not straight:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+            self.indent += 1
+        for r in rng:
+            conds = [f"({valid})"] if valid is not None else []
+            if own == "PER_SLOT":
+                conds.append(self._owner_cond(layout, r))
+            if mask is not None:
+                conds.append(f"({self.elem(ops[2], layout, r, maps[2])})")
+            oe = self.elem(ops[0], layout, r, maps[0])
+            ve = DT.store_conv(dt, self.elem(ops[1], layout, r, maps[1]))
+            c = f"if ({' && '.join(conds)}) " if conds else ""
+            self.emit(f"{c}p_{name}[(tila::i64)({oe})] = {ve};")
+        if not straight:
+            self.indent -= 1
+            self.emit("}")
+        if own is not None and own != "PER_SLOT":
+            self.indent -= 1
+            self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+
+    # -- atomic_add (relaxed, GPU scope; interp.py:334-356) -------------------
+
+    _ATOMIC_CT = {"i32": "int", "u32": "unsigned int", "f32": "float"}
 
     def e_TAtomicAdd(self, x):
-        self.fail("atomic_add is not supported by the B200 backend yet", x.line)
+        dt, shape, _ = self.vt_info(x.vt)
+        if dt.name not in self._ATOMIC_CT:
+            self.fail(f"atomic_add on {dt.name} is not supported (i32, u32, f32)", x.line)
+        ct = self._ATOMIC_CT[dt.name]
+        if x.buffer is not None:
+            coords = [self.value(c) for c in x.coords]
+            base = x.buffer
+        else:
+            base, off = self._ptr_target(x.ptr)
+            coords = [off]
+        value = self.coerce(self.value(x.value), dt)
+        mask = self.value(x.mask) if x.mask is not None else None
+        nc = len(coords)
+
+        def addr(exprs):
+            if x.buffer is not None:
+                terms = [f"(tila::i64)p_{base}_stride{i} * (tila::i64)({e})" for i, e in enumerate(exprs)]
+                return " + ".join(terms) or "0"
+            return f"(tila::i64)({exprs[0]})"
+        res = self.fresh("at")
+        if not shape:
+            # one thread performs the update; the old value is shared with all
+            self.smem.need_scratch(8)
+            cond = "tid == 0" + (f" && ({mask.expr})" if mask is not None else "")
+            self.emit(f"{DT.ctype(dt)} {res} = {DT.literal(dt, 0)};")
+            self.emit(f"if ({cond}) {res} = atomicAdd(reinterpret_cast<{ct}*>(p_{base} + "
+                      f"({addr([c.expr for c in coords])})), ({ct})({value.expr}));")
+            self.emit("__syncthreads();")
+            self.emit(f"if (tid == 0) *reinterpret_cast<{DT.ctype(dt)}*>(tila_scratch) = {res};")
+            self.emit("__syncthreads();")
+            self.emit(f"{res} = *reinterpret_cast<{DT.ctype(dt)}*>(tila_scratch);")
+            self.emit("__syncthreads();")
+            return Val("scalar", dt, expr=res)
+        layout = self.default_layout(shape, dt)
+        ops = list(coords) + [value] + ([mask] if mask is not None else [])
+        ops, maps, straight = self.prepare_operands(ops, layout, shape)
+        own = owner_predicate(layout)
+        if own == "PER_SLOT":
+            straight = True
+        valid = layout.valid_expr()
+        self.emit(f"{DT.ctype(dt)} {res}[{layout.nreg}];")
+        rng = range(layout.nreg) if straight else ["r"]
+        if not straight:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {layout.nreg}; ++r) {{")
+            self.indent += 1
+        for r in rng:
+            conds = [f"({valid})"] if valid is not None else []
+            if own is not None:
+                conds.append(self._owner_cond(layout, r) if own == "PER_SLOT" else f"({own})")
+            if mask is not None:
+                conds.append(f"({self.elem(ops[nc + 1], layout, r, maps[nc + 1])})")
+            a = addr([self.elem(ops[i], layout, r, maps[i]) for i in range(nc)])
+            v = self.elem(ops[nc], layout, r, maps[nc])
+            c = " && ".join(conds) if conds else "true"
+            self.emit(f"{res}[{r}] = ({c}) ? atomicAdd(reinterpret_cast<{ct}*>(p_{base} + ({a})), ({ct})({v})) "
+                      f": {DT.literal(dt, 0)};")
+        if not straight:
+            self.indent -= 1
+            self.emit("}")
+        return Val("reg", dt, tuple(shape), name=res, layout=layout)
 
     # -- dot (tcgen05): see mma.MmaMixin -----------------------------------
 
