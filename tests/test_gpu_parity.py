@@ -191,3 +191,41 @@ def test_program_range_shards_reproduce_the_full_launch(world):
             W.tiled_matmul[(3, 2)](ag, bg, c_part, BM=128, BN=128, BK=64)
     _no_device_errors()
     assert torch.equal(c_part, c_full)
+
+
+def test_repeated_signature_launches_skip_checks_and_use_new_buffers():
+    """A second launch with the same binding signature takes the cached path
+    (no re-checking) and reads and writes the new tensors; a different
+    signature (shape, aliasing) takes the full path again."""
+    from tila_b200 import plugin
+    n = 3000
+    xs = [torch.randn(n, device="cuda") for _ in range(3)]
+    ys = [torch.randn(n, device="cuda") for _ in range(3)]
+    outs = [torch.empty(n, device="cuda") for _ in range(3)]
+    grid = (ti.cdiv(n, 1024),)
+    W.vector_add[grid](xs[0], ys[0], outs[0], BLOCK=1024)
+    hits = plugin.fast_hits
+    for i in (1, 2):
+        W.vector_add[grid](xs[i], ys[i], outs[i], BLOCK=1024)
+    torch.cuda.synchronize()
+    assert plugin.fast_hits == hits + 2
+    for i in range(3):
+        assert torch.equal(outs[i], xs[i] + ys[i])
+    assert W.vector_add.last_backend_resources is not None
+    # a new shape and an aliased output are checked again
+    m = 2000
+    o2 = torch.empty(m, device="cuda")
+    W.vector_add[(ti.cdiv(m, 1024),)](xs[0][:m], ys[0][:m], o2, BLOCK=1024)
+    assert plugin.fast_hits == hits + 2
+    torch.cuda.synchronize()
+    assert torch.equal(o2, xs[0][:m] + ys[0][:m])
+    x_alias = xs[2].clone()
+    try:
+        W.vector_add[grid](x_alias, ys[2], x_alias, BLOCK=1024)
+    except ti.errors.TilaError:
+        pass                       # the checker may reject the aliasing: also not cached
+    else:
+        torch.cuda.synchronize()
+        assert torch.equal(x_alias, xs[2] + ys[2])
+    assert plugin.fast_hits == hits + 2
+    _no_device_errors()

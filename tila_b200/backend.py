@@ -277,14 +277,18 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
     """Compile (cached) and launch a checked kernel on the tensors' device."""
     import torch
     jf, tk = launcher.jf, launcher.jf.tk
+    # what the launch needs besides the tensors; a repeated launch with the
+    # same binding signature replays it (plugin.py, repeated-signature path)
+    launcher._b200_last_exec = (dict(tensors), scalar_vals, stride_vals, consts, grid)
     device = next(iter(tensors.values())).device
     facts = binding_facts(tk, tensors)
+    target = getattr(launcher, "target", None)
     context = {"kernel": tk.name, "tila_source": jf.tila_source,
                "source_file": jf.fn.__code__.co_filename,
                "source_start_line": jf.source_start_line, "consts": consts,
                "scalars": scalar_vals, "grid": grid, "num_warps": launcher.num_warps,
                "debug": _debug(), "backend": "b200",
-               "target": asdict(launcher.target) if launcher.target is not None else None}
+               "target": asdict(target) if target is not None else None}
     with torch.cuda.device(device):
         entry = compile_kernel(jf, consts, facts, launcher.num_warps, context)
         if entry.attrs is None or entry.attrs.get("_device") != device.index:

@@ -18,6 +18,7 @@ Triton is never imported on the B200 path.
 from __future__ import annotations
 
 import os
+import struct
 
 from ._reference import tila
 
@@ -52,13 +53,112 @@ def _is_cuda_launch(tensors):
     return torch is not None and isinstance(t0, torch.Tensor) and t0.is_cuda
 
 
+# ---------------------------------------------------------------------------
+# repeated-signature launches
+# ---------------------------------------------------------------------------
+#
+# Every launch runs Tila's launch contracts, bounds proofs and race analysis
+# (runtime.py:726-1039, about 20 ms) before the kernel.  Those checks read
+# only the binding signature - dtypes, shapes, strides, base alignment,
+# aliasing between arguments, explicit scalar values, Consts, grid, options -
+# never buffer contents, so a launch whose signature equals that of an earlier
+# successful launch of the same kernel passes them with the same outcome.
+# Such a launch skips them and goes straight to the compiled kernel with the
+# new buffer addresses.  The previous launch's evidence (race report,
+# alignment facts, backend resources) stays valid for it.  TILA_B200_FASTPATH=0
+# runs the full checks on every launch.
+
+_FAST_MAX = 64
+fast_hits = 0        # launches that took the repeated-signature path (for tests)
+_ENV_KEYS = ("TILA_INTERP", "TILA_DEBUG", "TILA_RACE", "TILA_EFFECTS", "TILA_BACKEND_ARTIFACTS")
+
+
+def _pow2_div(v, cap=256):
+    v = int(v)
+    if v == 0:
+        return cap
+    d = 1
+    while v % (d * 2) == 0 and d < cap:
+        d *= 2
+    return d
+
+
+def _arg_sig(a):
+    torch = _runtime.torch
+    if torch is not None and isinstance(a, torch.Tensor):
+        if not a.is_cuda:
+            return None
+        return ("T", str(a.dtype), a.device.index, tuple(a.shape), tuple(a.stride()),
+                _pow2_div(a.data_ptr()), a.requires_grad)
+    if isinstance(a, float):
+        # by bit pattern: -0.0 and 0.0 differ, a NaN matches itself
+        return ("S", "float", struct.pack("<d", a))
+    if isinstance(a, (bool, int)):
+        return ("S", type(a).__name__, a)
+    return None
+
+
+def _fast_key(launcher, args, kwargs):
+    if os.environ.get("TILA_B200_FASTPATH", "1") == "0":
+        return None
+    torch = _runtime.torch
+    sigs = []
+    spans = []
+    for i, a in enumerate(list(args) + [kwargs[k] for k in sorted(kwargs)]):
+        sig = _arg_sig(a)
+        if sig is None:
+            return None
+        sigs.append(sig)
+        if sig[0] == "T":
+            n = 0 if a.numel() == 0 else 1 + sum((d - 1) * st for d, st in zip(a.shape, a.stride()))
+            spans.append((i, a.data_ptr(), a.data_ptr() + n * a.element_size()))
+    if not spans:
+        return None
+    alias = tuple((i, j) for x, (i, lo, hi) in enumerate(spans) for (j, lo2, hi2) in spans[x + 1:]
+                  if lo < hi2 and lo2 < hi)
+    from .backend import current_program_range
+    grid = launcher.grid
+    if not isinstance(grid, (tuple, list)):
+        return None          # a grid derived from the obligations takes the full path
+    axes = []
+    for g in grid:
+        if type(g) is int:
+            axes.append(g)
+        elif isinstance(g, _runtime._Cdiv) and type(g.a) is int and type(g.b) is int:
+            axes.append(("cdiv", g.a, g.b))
+        else:
+            return None      # callable grid entries take the full path
+    grid = tuple(axes)
+    env = tuple(os.environ.get(k) for k in _ENV_KEYS)
+    return (grid, launcher.num_warps, tuple(sorted(kwargs)), tuple(sigs), alias,
+            current_program_range(), env)
+
+
+def _remember(launcher, key, args, kwargs):
+    last = getattr(launcher, "_b200_last_exec", None)
+    if last is None:
+        return
+    tensors, scalar_vals, stride_vals, consts, grid = last
+    vals = list(args) + [kwargs[k] for k in sorted(kwargs)]
+    names = {}
+    for name, t in tensors.items():
+        idx = [i for i, a in enumerate(vals) if a is t]
+        if len(idx) != 1:
+            return
+        names[name] = idx[0]
+    cache = launcher.jf.__dict__.setdefault("_b200_fast", {})
+    if len(cache) >= _FAST_MAX:
+        cache.clear()
+    cache[key] = (names, scalar_vals, stride_vals, consts, grid)
+
+
 def install():
     """Route CUDA launches of every ``@ti.jit`` kernel to the B200 backend."""
     global _installed
     if _installed is not None:
         return
     L = _runtime._Launcher
-    original = (L._resolve_target, L._execute)
+    original = (L._resolve_target, L._execute, L.__call__)
 
     def _resolve_target(self, tensors):
         if not _is_cuda_launch(tensors):
@@ -73,8 +173,33 @@ def install():
             return backend.execute(self, tensors, scalar_vals, stride_vals, consts, grid)
         return original[1](self, tensors, scalar_vals, stride_vals, consts, grid)
 
+    full_call = original[2]
+
+    def __call__(self, *args, **kwargs):
+        try:
+            key = _fast_key(self, args, kwargs)
+        except Exception:
+            key = None
+        if key is not None:
+            hit = self.jf.__dict__.get("_b200_fast", {}).get(key)
+            if hit is not None:
+                global fast_hits
+                fast_hits += 1
+                names, scalar_vals, stride_vals, consts, grid = hit
+                vals = list(args) + [kwargs[k] for k in sorted(kwargs)]
+                from . import backend
+                backend.execute(self, {n: vals[i] for n, i in names.items()}, scalar_vals,
+                                stride_vals, consts, grid)
+                return None
+        self._b200_last_exec = None
+        out = full_call(self, *args, **kwargs)
+        if key is not None and getattr(self, "_completed", False):
+            _remember(self, key, args, kwargs)
+        return out
+
     L._resolve_target = _resolve_target
     L._execute = _execute
+    L.__call__ = __call__
     _installed = original
 
 
@@ -83,7 +208,7 @@ def uninstall():
     if _installed is None:
         return
     L = _runtime._Launcher
-    L._resolve_target, L._execute = _installed
+    L._resolve_target, L._execute, L.__call__ = _installed
     _installed = None
 
 
