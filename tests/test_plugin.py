@@ -69,3 +69,23 @@ def test_resource_failures_produce_the_reference_artifact(tmp_path, monkeypatch)
                            resource=("threads", 2048, 1024))
     assert err.code == "TILA-TARGET-011"
     assert err.backend_artifact and (tmp_path / err.backend_artifact).exists()
+
+
+def test_build_cli_writes_cuda_tir_and_source_map(tmp_path):
+    """python -m tila_b200 build: the generated CUDA, the TIR exactly as
+    `tila build` writes it, a line map back to the Tila source, the cubin."""
+    import json
+    import semantics_support as S
+    from tila_b200.__main__ import main
+    from tila import cli as tila_cli
+    S.binary_program(tmp_path, "f32", "+")
+    src = next(tmp_path.glob("sem_bin_f32_add.py"))
+    out = tmp_path / "b200"
+    assert main(["build", str(src), "-o", str(out), "--cubin"]) == 0
+    cu = (out / "kernel.cu").read_text()
+    assert 'extern "C" __global__' in cu and "// @tila-line" in cu
+    smap = json.loads((out / "kernel.map.json").read_text())
+    assert smap["cuda_line_to_tila_line"] and (out / "kernel.cubin").stat().st_size > 0
+    ref = tmp_path / "ref"
+    assert tila_cli.main(["build", str(src), "-o", str(ref)]) == 0
+    assert (out / "kernel.tir.txt").read_text() == (ref / "kernel.tir.txt").read_text()

@@ -174,8 +174,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
-                 entry_name=None, debug=False, versioning=True):
+                 entry_name=None, debug=False, versioning=True, source_map=False):
         self.tk = tk
+        self.source_map = source_map     # annotate the output with Tila source lines
         self.versioning = versioning     # loop bodies specialised for interior tiles
         self.consts = dict(consts)
         self.buffers = buffers
@@ -1665,6 +1666,10 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         m = getattr(self, f"s_{type(s).__name__}", None)
         if m is None:
             self.fail(f"unsupported TIR statement {type(s).__name__}", getattr(s, "line", 0))
+        line = getattr(s, "line", 0)
+        if self.source_map and line:
+            # source map: the generated code below comes from this Tila line
+            self.emit(f"// @tila-line {line}")
         m(s)
 
     def s_TAssign(self, s):
