@@ -130,13 +130,13 @@ def test_uniform_divisor_takes_reciprocal_path(tmp_path):
     element-wise division by a tile keeps IEEE division."""
     import semantics_support as S
     spec = gen(W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
-    assert "tila::udiv_fast2(" in spec.source
+    assert "tila::udiv_q2(" in spec.source and "tila::udiv_track(" in spec.source
     for kind in ("scalar", "reduced"):
         k = S.uniform_div_program(tmp_path, kind)
         t = dict(x=torch.zeros(2048), out=torch.zeros(2048))
         if kind == "reduced":
             t["y"] = torch.zeros(2, 256)
-        assert "tila::udiv_fast" in gen(k, t).source
+        assert "tila::udiv_q" in gen(k, t).source
     k = S.binary_program(tmp_path, "f32", "/")
     src = gen(k, dict(x=torch.zeros(100), y=torch.zeros(100), out=torch.zeros(100))).source
     assert "udiv" not in src and " / " in src

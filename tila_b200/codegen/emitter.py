@@ -420,25 +420,48 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
 
     def _uniform_division(self, name, rows, divisor, dividend=None, nreg=None):
         """f32 quotients by a divisor shared by all of this thread's elements:
-        one reciprocal (tila::udiv_prepare), Markstein-corrected quotients,
-        and an IEEE recomputation if any dividend leaves the exact range."""
+        one reciprocal (tila::udiv_prepare), a range record of the dividends
+        (tila::udiv_track), then Markstein-corrected quotients, or IEEE
+        division if any dividend leaves the exact range.  Dividends that are
+        not plain register reads are computed once into a temporary, so that
+        the quotients can take over their registers."""
         ud = self.fresh("ud")
+        plain = re.compile(r"\(*\w+\[\(*r\)*\]\)*")
+        if rows is not None:
+            if not all(re.fullmatch(r"\(*\w+\[\d+\]\)*", a) for _, a in rows):
+                tmp = self.fresh("dv")
+                self.emit(f"float {tmp}[{len(rows)}];")
+                for r, a in rows:
+                    self.emit(f"{tmp}[{r}] = {a};")
+                rows = [(r, f"{tmp}[{r}]") for r, _ in rows]
+        elif not plain.fullmatch(dividend):
+            tmp = self.fresh("dv")
+            self.emit(f"float {tmp}[{nreg}];")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {nreg}; ++r) {tmp}[r] = {dividend};")
+            dividend = f"{tmp}[r]"
         self.emit(f"const tila::UDiv {ud} = tila::udiv_prepare({divisor});")
         self.emit(f"tila::u32 {ud}_hi = 0u, {ud}_lo = 0xffffffffu;")
         if rows is not None:
             for r, a in rows:
-                self.emit(f"{name}[{r}] = tila::udiv_fast(({a}), {ud}, {ud}_hi, {ud}_lo);")
+                self.emit(f"tila::udiv_track(({a}), {ud}_hi, {ud}_lo);")
+        else:
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {nreg}; ++r) tila::udiv_track(({dividend}), {ud}_hi, {ud}_lo);")
+        self.emit(f"if (tila::udiv_all_fast({ud}, {ud}_hi, {ud}_lo)) {{")
+        if rows is not None:
+            for r, a in rows:
+                self.emit(f"  {name}[{r}] = tila::udiv_q(({a}), {ud});")
         elif nreg % 2 == 0:
             d0 = re.sub(r"\br\b", "(r)", dividend)
             d1 = re.sub(r"\br\b", "(r + 1)", dividend)
-            self.emit("#pragma unroll")
-            self.emit(f"for (int r = 0; r < {nreg}; r += 2) "
-                      f"tila::udiv_fast2(({d0}), ({d1}), {ud}, {ud}_hi, {ud}_lo, {name}[r], {name}[r + 1]);")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int r = 0; r < {nreg}; r += 2) "
+                      f"tila::udiv_q2(({d0}), ({d1}), {ud}, {name}[r], {name}[r + 1]);")
         else:
-            self.emit("#pragma unroll")
-            self.emit(f"for (int r = 0; r < {nreg}; ++r) {name}[r] = "
-                      f"tila::udiv_fast(({dividend}), {ud}, {ud}_hi, {ud}_lo);")
-        self.emit(f"if (!tila::udiv_all_fast({ud}, {ud}_hi, {ud}_lo)) {{")
+            self.emit("  #pragma unroll")
+            self.emit(f"  for (int r = 0; r < {nreg}; ++r) {name}[r] = tila::udiv_q(({dividend}), {ud});")
+        self.emit("} else {")
         if rows is not None:
             for r, a in rows:
                 self.emit(f"  {name}[{r}] = (({a}) / ({divisor}));")

@@ -118,14 +118,15 @@ __device__ __forceinline__ float exp2_ftz(float x) {
 // with y = RN(1/b) can be off by up to 1.5 ulp (e.g. 1.5 / 1.9999999), so a
 // first correction makes it faithful (its error is then below 0.5 ulp plus
 // 2^-45 relative) and the second one rounds correctly.  Magnitudes in
-// [2^-60, 2^60) for both operands (and zero for
-// the dividend) keep every intermediate normal and finite; udiv_fast records
-// the dividends' range so that a thread whose dividends leave it (subnormals,
-// infinities, extreme exponents) recomputes its quotients with IEEE division.
+// [2^-60, 2^60) for both operands (and zero for the dividend) keep every
+// intermediate normal and finite.  A thread first records its dividends'
+// range (udiv_track); if one leaves it (subnormals, infinities, NaN, extreme
+// exponents) the thread divides with IEEE division instead (udiv_all_fast).
+// Tracking before dividing lets the quotients overwrite the dividends'
+// registers.
 struct UDiv {
   float b;      // the divisor
   float y;      // RN(1/b)
-  u32 sbits;    // sign bit of b
   bool ok;      // 2^-60 <= |b| < 2^60
 };
 __device__ __forceinline__ UDiv udiv_prepare(float b) {
@@ -133,26 +134,29 @@ __device__ __forceinline__ UDiv udiv_prepare(float b) {
   const u32 ub = __float_as_uint(b);
   d.b = b;
   d.y = __frcp_rn(b);
-  d.sbits = ub & 0x80000000u;
   d.ok = ((ub & 0x7fffffffu) - 0x21800000u) < (0x5d800000u - 0x21800000u);
   return d;
 }
-// Quotient for one dividend (valid when udiv_all_fast holds at the end);
-// updates the range record: hi = max of 2|a| bits, lo = min of (2|a| bits) - 1
-// (a zero dividend maps to 0 and 0xffffffff and so changes neither).  The
-// sign of a zero quotient is set from the operands' signs (the corrections
-// would turn -0 / b into +0).
-__device__ __forceinline__ float udiv_fast(float a, const UDiv &d, u32 &hi, u32 &lo) {
+// Range record of one dividend: hi = max of 2|a| bits, lo = min of
+// (2|a| bits) - 1 (a zero dividend maps to 0 and 0xffffffff and so changes
+// neither).
+__device__ __forceinline__ void udiv_track(float a, u32 &hi, u32 &lo) {
   const u32 ua = __float_as_uint(a);
   const u32 u2 = ua + ua;
   hi = max(hi, u2);
   lo = min(lo, u2 - 1u);
-  float q = __fmul_rn(a, d.y);
-  float r = __fmaf_rn(-d.b, q, a);
-  q = __fmaf_rn(r, d.y, q);
+}
+// Quotient of a recorded dividend (valid when udiv_all_fast holds).  The
+// first product p = a*y carries the sign of a/b, also for a zero dividend;
+// the corrections can turn a -0 quotient into +0 but never the reverse, so
+// OR-ing p's sign bit restores it (and changes nothing for other quotients).
+__device__ __forceinline__ float udiv_q(float a, const UDiv &d) {
+  const float p = __fmul_rn(a, d.y);
+  float r = __fmaf_rn(-d.b, p, a);
+  float q = __fmaf_rn(r, d.y, p);
   r = __fmaf_rn(-d.b, q, a);
   q = __fmaf_rn(r, d.y, q);
-  return __uint_as_float(__float_as_uint(q) | ((ua ^ d.sbits) & 0x80000000u));
+  return __uint_as_float(__float_as_uint(q) | (__float_as_uint(p) & 0x80000000u));
 }
 __device__ __forceinline__ bool udiv_all_fast(const UDiv &d, u32 hi, u32 lo) {
   return d.ok && hi < 0xbb000000u && lo >= 0x42ffffffu;   // 2|a| bits in [2^-60, 2^60)
@@ -197,21 +201,16 @@ __device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
 }
 
 // Two quotients by the same divisor with f32x2 arithmetic (same steps and
-// results as two udiv_fast calls).
-__device__ __forceinline__ void udiv_fast2(float a0, float a1, const UDiv &d, u32 &hi, u32 &lo,
-                                           float &q0, float &q1) {
-  const u32 ua0 = __float_as_uint(a0), ua1 = __float_as_uint(a1);
-  const u32 u20 = ua0 + ua0, u21 = ua1 + ua1;
-  hi = max(hi, max(u20, u21));
-  lo = min(lo, min(u20 - 1u, u21 - 1u));
+// results as two udiv_q calls).
+__device__ __forceinline__ void udiv_q2(float a0, float a1, const UDiv &d, float &q0, float &q1) {
   const u64 a = pk2(a0, a1), y = pk2(d.y, d.y), nb = pk2(-d.b, -d.b);
-  u64 q = mul2(a, y);
-  u64 r = fma2(nb, q, a);
-  q = fma2(r, y, q);
+  const u64 p = mul2(a, y);
+  u64 r = fma2(nb, p, a);
+  u64 q = fma2(r, y, p);
   r = fma2(nb, q, a);
   q = fma2(r, y, q);
-  q0 = __uint_as_float(__float_as_uint(lo2(q)) | ((ua0 ^ d.sbits) & 0x80000000u));
-  q1 = __uint_as_float(__float_as_uint(hi2(q)) | ((ua1 ^ d.sbits) & 0x80000000u));
+  q0 = __uint_as_float(__float_as_uint(lo2(q)) | (__float_as_uint(lo2(p)) & 0x80000000u));
+  q1 = __uint_as_float(__float_as_uint(hi2(q)) | (__float_as_uint(hi2(p)) & 0x80000000u));
 }
 
 // Round an f32 to the nearest f16 / bf16 value and widen back (the register
