@@ -49,6 +49,8 @@ class FusedContractionMixin:
         """Emit the whole kernel body as a 2 x 2 block of programs per CTA
         when the kernel is a single pipelined contraction; False otherwise."""
         body = self.tk.body
+        if self.T < 64:      # thread 32 is the copy producer
+            return False
         loops = [i for i, s in enumerate(body) if isinstance(s, T_.TFor)]
         if len(loops) != 1:
             return False
@@ -160,9 +162,6 @@ class FusedContractionMixin:
         self.emit("tila::tc_fence_before();")
         self.emit("__syncthreads();")
         self.emit("tila::tc_fence_after();")
-        self.emit("if (tid == 0) {")
-        self.indent += 1
-
         def issue(jexpr, st):
             self.emit("{")
             self.indent += 1
@@ -182,11 +181,22 @@ class FusedContractionMixin:
             self.indent -= 1
             self.emit("}")
 
-        self.emit(f"for (tila::i64 j = 0; j < cl_n && j < {S - 1}; ++j) {{")
+        # producer (thread 32): refills a stage as soon as the MMAs reading it
+        # have completed, so copy latency is hidden behind all S stages
+        self.emit("if (tid == 32) {")
         self.indent += 1
-        issue("j", "j")
+        self.emit("for (tila::i64 j = 0; j < cl_n; ++j) {")
+        self.indent += 1
+        self.emit(f"const int sj = (int)(j % {S});")
+        self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
+        issue("j", "sj")
         self.indent -= 1
         self.emit("}")
+        self.indent -= 1
+        self.emit("}")
+        # MMA issuer (thread 0)
+        self.emit("if (tid == 0) {")
+        self.indent += 1
         self.emit("for (tila::i64 i = 0; i < cl_n; ++i) {")
         self.indent += 1
         self.emit(f"const int st = (int)(i % {S});")
@@ -207,14 +217,6 @@ class FusedContractionMixin:
                     idesc = f"tila::idesc_f16_f32(128, {128 * nb}, {a_mn}, {b_mn})"
                     self.emit(f"tila::mma_f16_ss(tila_tmem + {cols[(i, j0)]}, {da}, {db}, {idesc}, 1u);")
         self.emit(f"tila::mma_commit({empty('st')});")
-        self.emit(f"const tila::i64 j = i + {S - 1};")
-        self.emit("if (j < cl_n) {")
-        self.indent += 1
-        self.emit(f"const int sj = (int)(j % {S});")
-        self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
-        issue("j", "sj")
-        self.indent -= 1
-        self.emit("}")
         self.indent -= 1
         self.emit("}")
         self.emit(f"tila::mma_commit({accbar});")
