@@ -205,6 +205,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self.fuse = None             # {axis: programs per CTA} when CTAs run program blocks
         self._wg_candidate = False   # an asynchronous loop allows two programs per CTA
         self._free_smem = []         # (offset, bytes) of buffers no longer in use
+        self._store_ring = None      # rotating TMA-store staging slots (see _try_tma_store)
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -441,7 +442,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit(f"for (int r = 0; r < {nreg}; ++r) {tmp}[r] = {dividend};")
             dividend = f"{tmp}[r]"
         self.emit(f"const tila::UDiv {ud} = tila::udiv_prepare({divisor});")
-        self.emit(f"tila::u32 {ud}_hi = 0u, {ud}_lo = 0xffffffffu;")
+        self.emit(f"float {ud}_hi = 0.0f; tila::u32 {ud}_lo = 0xffffffffu;")
         if rows is not None:
             for r, a in rows:
                 self.emit(f"tila::udiv_track(({a}), {ud}_hi, {ud}_lo);")
@@ -906,6 +907,18 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             return lambda a, b: f"tila::max_nan({a}, {b})"
         return lambda a, b: f"tila::max_int<{DT.ctype(dt)}>({a}, {b})"
 
+    def _thread_tree(self, op, dt, exprs):
+        """In-thread reduction of ``exprs`` (C++ expressions): f32 sums of 8 or
+        more terms use two interleaved trees in f32x2 lanes; otherwise a
+        balanced pairwise tree (short dependency chains)."""
+        fold = self._fold(op, dt)
+        if op == "sum" and dt.name == "f32" and len(exprs) % 2 == 0 and len(exprs) >= 8:
+            pairs = [f"tila::pk2({exprs[i]}, {exprs[i + 1]})" for i in range(0, len(exprs), 2)]
+            t = self.fresh("ps")
+            self.emit(f"const tila::u64 {t} = {_tree_fold(pairs, lambda a, b: f'tila::add2({a}, {b})')};")
+            return f"((tila::lo2({t})) + (tila::hi2({t})))"
+        return _tree_fold(exprs, fold)
+
     def _identity(self, op, dt):
         if op == "sum":
             return DT.literal(dt, 0)
@@ -943,18 +956,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             for r in range(lay.nreg):
                 c = self._owner_cond(lay, r)
                 self.emit(f"if ({c}) {part} = {fold(part, conv(f'{v.name}[{r}]'))};")
-        elif op == "sum" and acc_dt.name == "f32" and lay.nreg % 2 == 0 and lay.nreg >= 8:
-            # two interleaved trees in the lanes of f32x2 additions
-            pairs = [f"tila::pk2({conv(f'{v.name}[{r}]')}, {conv(f'{v.name}[{r + 1}]')})"
-                     for r in range(0, lay.nreg, 2)]
-            t = self.fresh("ps")
-            self.emit(f"const tila::u64 {t} = {_tree_fold(pairs, lambda a, b: f'tila::add2({a}, {b})')};")
-            self.emit(f"{part} = ((tila::lo2({t})) + (tila::hi2({t})));")
-            if own is not None:
-                self.emit(f"if (!({own})) {part} = {self._identity(op, acc_dt)};")
         else:
-            # balanced tree inside the thread (short dependency chains)
-            self.emit(f"{part} = {_tree_fold([conv(f'{v.name}[{r}]') for r in range(lay.nreg)], fold)};")
+            # a short tree inside the thread (see _thread_tree)
+            self.emit(f"{part} = {self._thread_tree(op, acc_dt, [conv(f'{v.name}[{r}]') for r in range(lay.nreg)])};")
             if own is not None:
                 self.emit(f"if (!({own})) {part} = {self._identity(op, acc_dt)};")
         return Val("scalar", acc_dt, expr=self._cta_allreduce(part, op, acc_dt))
@@ -1018,7 +1022,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self.emit(f"{ct} {name}[{n}];")
         own = owner_predicate(lay)
         for k, g in enumerate(outs):
-            self.emit(f"{name}[{k}] = {_tree_fold([conv(f'{v.name}[{r}]') for r in g], fold)};")
+            self.emit(f"{name}[{k}] = {self._thread_tree(op, acc_dt, [conv(f'{v.name}[{r}]') for r in g])};")
         if own is not None and own != "PER_SLOT":
             self.emit(f"if (!({own})) {{")
             self.emit(f"  #pragma unroll")
@@ -1416,7 +1420,18 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if coef != 1 or div % 4:
             return False
         size = plan.nbox * 128 * 128
-        base = self._store_staging(size)
+        ring = self._store_ring
+        if ring is not None and ring["size"] in (None, size) and ring["bytes"] // size >= 2:
+            # rotating staging slots: this store waits only for the store that
+            # used its slot before (one bulk group per store, in order)
+            ring["size"] = size
+            nslot = min(4, ring["bytes"] // size)
+            slot = ring["next"] % nslot
+            ring["next"] += 1
+            base = ring["base"] + slot * size
+        else:
+            ring = None
+            base = self._store_staging(size)
         if base is None:
             return False
         tm = self.tensor_map_param(plan)
@@ -1424,6 +1439,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         col0 = "(tid >> 7) * %d + " % lay.cpg if lay.groups > 1 else ""
         self.emit(f"{{ // TMA store of {s.buffer} ({shape[0]}x{shape[1]} f32) through shared memory")
         self.indent += 1
+        if ring is not None:
+            self.emit(f"if (tid == 0) tila::bulk_wait_read_n<{nslot - 1}>();   // staging slot {slot} is free")
+            self.emit("__syncthreads();")
         self.emit("const int row_ = tid & 127;")
         self.emit("#pragma unroll")
         self.emit(f"for (int r = 0; r < {lay.nreg}; r += 4) {{")
@@ -1442,10 +1460,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 cs[0] = f"({cs[0]} + {32 * b})"
             self.emit(f"tila::tma_store_{plan.rank}d(&{tm}, tila_smem + {base} + {b * 16384}, {', '.join(cs)});")
         self.emit("tila::bulk_commit();")
-        self.emit("tila::bulk_wait_read();")
+        if ring is None:
+            self.emit("tila::bulk_wait_read();")
         self.indent -= 1
         self.emit("}")
-        self.emit("__syncthreads();")
+        if ring is None:
+            self.emit("__syncthreads();")
         self.indent -= 1
         self.emit("}")
         return True

@@ -228,7 +228,11 @@ class FusedContractionMixin:
         self.emit("}")
         # every copy into the ring has been consumed by a completed MMA
         self._free_smem.append((ring, S * stage))
-        # epilogues, one program at a time (uniform branches: `live` depends on blockIdx)
+        # epilogues, one program at a time (uniform branches: `live` depends on
+        # blockIdx).  TMA stores rotate through staging slots in the freed
+        # ring; a program that does not run commits the same number of (empty)
+        # bulk groups, so that group k always belongs to store k.
+        self._store_ring = {"base": ring, "bytes": S * stage, "size": None, "next": 0}
         for (i, j) in inst:
             self.env = dict(envs[(i, j)])
             self._pid_expr = {ay: f"pid_{ay}_{i}", ax: f"pid_{ax}_{j}"}
@@ -236,9 +240,17 @@ class FusedContractionMixin:
             self.emit(f"if (live_{ay}_{i} && live_{ax}_{j}) {{")
             self.indent += 1
             self.conv_cache = {}
+            before = self._store_ring["next"]
             self.stmts(suffix)
+            used = self._store_ring["next"] - before
             self.indent -= 1
+            if used:
+                self.emit("} else if (tid == 0) {")
+                self.emit("  " + " ".join(["tila::bulk_commit();"] * used))
             self.emit("}")
+        if self._store_ring["next"]:
+            self.emit("if (tid == 0) tila::bulk_wait_read();   // staging reads done before exit")
+        self._store_ring = None
         self._pid_expr = {}
 
     def _smem_op(self, plan, base):

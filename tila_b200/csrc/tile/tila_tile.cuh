@@ -137,14 +137,12 @@ __device__ __forceinline__ UDiv udiv_prepare(float b) {
   d.ok = ((ub & 0x7fffffffu) - 0x21800000u) < (0x5d800000u - 0x21800000u);
   return d;
 }
-// Range record of one dividend: hi = max of 2|a| bits, lo = min of
-// (2|a| bits) - 1 (a zero dividend maps to 0 and 0xffffffff and so changes
-// neither).
-__device__ __forceinline__ void udiv_track(float a, u32 &hi, u32 &lo) {
+// Range record of one dividend: hi = max of |a| (NaN propagates), lo = min
+// of (2|a| bits) - 1 (a zero dividend maps to 0xffffffff and so leaves it).
+__device__ __forceinline__ void udiv_track(float a, float &hi, u32 &lo) {
   const u32 ua = __float_as_uint(a);
-  const u32 u2 = ua + ua;
-  hi = max(hi, u2);
-  lo = min(lo, u2 - 1u);
+  asm("max.NaN.f32 %0, %0, %1;" : "+f"(hi) : "f"(fabsf(a)));
+  lo = min(lo, ua + ua - 1u);
 }
 // Quotient of a recorded dividend (valid when udiv_all_fast holds).  The
 // first product p = a*y carries the sign of a/b, also for a zero dividend;
@@ -158,8 +156,8 @@ __device__ __forceinline__ float udiv_q(float a, const UDiv &d) {
   q = __fmaf_rn(r, d.y, q);
   return __uint_as_float(__float_as_uint(q) | (__float_as_uint(p) & 0x80000000u));
 }
-__device__ __forceinline__ bool udiv_all_fast(const UDiv &d, u32 hi, u32 lo) {
-  return d.ok && hi < 0xbb000000u && lo >= 0x42ffffffu;   // 2|a| bits in [2^-60, 2^60)
+__device__ __forceinline__ bool udiv_all_fast(const UDiv &d, float hi, u32 lo) {
+  return d.ok && hi < 0x1p60f && lo >= 0x42ffffffu;   // |a| in [2^-60, 2^60) or zero
 }
 
 // Packed f32 pairs (sm_100 f32x2 arithmetic): each lane is rounded exactly
@@ -493,6 +491,11 @@ __device__ __forceinline__ void bulk_commit() {
 }
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
 // ---------------------------------------------------------------------------
