@@ -197,3 +197,39 @@ def kernel(x: ti.ReadPtr[ti.{dtype}, N], out: ti.WritePtr[ti.{dtype}, N]):
     v = ti.load(x + i, mask=ok, other=0)
     ti.store(out + i, v + v, mask=ok)
 ''')
+
+
+def batched_matmul_program(directory):
+    """c[h] = a[h] @ b[h] over a 3-D grid (row tile, column tile, batch):
+    the batch axis keeps the block from being coarsened, so the kernel uses
+    the per-program pipelined contraction ring."""
+    return load_source(directory, "sem_bmm", '''import tila as ti
+B = ti.Dim("B")
+M = ti.Dim("M")
+N = ti.Dim("N")
+K = ti.Dim("K")
+
+@ti.jit
+def kernel(a: ti.Buffer[ti.f16, (B, M, K), ti.ReadOnly],
+           b: ti.Buffer[ti.f16, (B, K, N), ti.ReadOnly],
+           c: ti.Buffer[ti.f32, (B, M, N), ti.WriteOnly],
+           BM: ti.Const[int, ti.PowerOfTwo] = 128,
+           BN: ti.Const[int, ti.PowerOfTwo] = 128,
+           BK: ti.Const[int] = 64):
+    tm = ti.program_id(0)
+    tn = ti.program_id(1)
+    h = ti.program_id(2)
+    rows = tm * BM + ti.arange(0, BM)
+    cols = tn * BN + ti.arange(0, BN)
+    ks = ti.arange(0, BK)
+    row_ok = rows < M
+    col_ok = cols < N
+    total = ti.zeros((BM, BN), ti.f32)
+    for k0 in ti.range(0, K, BK):
+        kk = k0 + ks
+        k_ok = kk < K
+        lhs = ti.load(a, (h, rows[:, None], kk[None, :]), mask=row_ok[:, None] & k_ok[None, :])
+        rhs = ti.load(b, (h, kk[:, None], cols[None, :]), mask=k_ok[:, None] & col_ok[None, :])
+        total = ti.dot(lhs, rhs, acc=total)
+    ti.store(c, (h, rows[:, None], cols[None, :]), total, mask=row_ok[:, None] & col_ok[None, :])
+''')

@@ -171,3 +171,16 @@ def test_ptr_programs_compile(tmp_path):
     import semantics_support as S
     k = S.ptr_copy_program(tmp_path, "f32")
     gen(k, dict(x=torch.zeros(100), out=torch.zeros(100)))
+
+
+def test_batched_matmul_uses_split_copy_and_mma_threads(tmp_path):
+    """A 3-D grid (batch axis) is not coarsened: the per-program contraction
+    ring runs with a copy thread (32) and an MMA thread (0)."""
+    import semantics_support as S
+    k = S.batched_matmul_program(tmp_path)
+    t = dict(a=torch.zeros(2, 256, 320, dtype=f16), b=torch.zeros(2, 320, 384, dtype=f16),
+             c=torch.zeros(2, 256, 384))
+    spec = gen(k, t, BM=128, BN=128, BK=64)
+    assert "pipelined contraction loop" in spec.source and "if (tid == 32)" in spec.source
+    assert not spec.fuse
+    native.compile_spec(spec)

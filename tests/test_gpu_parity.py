@@ -229,3 +229,21 @@ def test_repeated_signature_launches_skip_checks_and_use_new_buffers():
         assert torch.equal(x_alias, xs[2] + ys[2])
     assert plugin.fast_hits == hits + 2
     _no_device_errors()
+
+
+@pytest.mark.parametrize("shape", [(3, 256, 384, 320), (2, 200, 136, 72)])
+def test_batched_matmul_contraction_ring(tmp_path, shape):
+    """3-D grid matmul (the per-program TMA ring with split copy / MMA
+    threads): within the K * eps_f32 bound of the f64 product per batch."""
+    import semantics_support as S
+    k = S.batched_matmul_program(tmp_path)
+    bsz, m, n, kd = shape
+    rng = np.random.default_rng(11)
+    a = (rng.standard_normal((bsz, m, kd)) / 8).astype(np.float16)
+    b = (rng.standard_normal((bsz, kd, n)) / 8).astype(np.float16)
+    c = torch.zeros((bsz, m, n), dtype=torch.float32, device="cuda")
+    k[(ti.cdiv(m, 128), ti.cdiv(n, 128), bsz)](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)
+    _no_device_errors()
+    got = c.cpu().numpy()
+    for h in range(bsz):
+        assert np.all(np.abs(got[h] - restate.matmul_f64(a[h], b[h])) <= restate.matmul_bound(a[h], b[h]))

@@ -472,9 +472,6 @@ class MmaMixin:
             for name in (d.a_name, d.b_name):
                 if name not in cl.loads:
                     self.emit_smem_wait(self.env[name])
-        self.emit("if (tid == 0) {")
-        self.indent += 1
-
         def issue(jexpr, stage_expr):
             self.emit("{")
             self.indent += 1
@@ -493,45 +490,75 @@ class MmaMixin:
             self.indent -= 1
             self.emit("}")
 
-        self.emit(f"for (tila::i64 j = 0; j < cl_n && j < {S - 1}; ++j) {{")
-        self.indent += 1
-        issue("j", "j")
-        self.indent -= 1
-        self.emit("}")
-        self.emit("for (tila::i64 i = 0; i < cl_n; ++i) {")
-        self.indent += 1
-        self.emit(f"const int st = (int)(i % {S});")
-        self.emit(f"tila::mbar_wait({full('st')}, (tila::u32)((i / {S}) & 1), tila_err, __LINE__, &tila_dead);")
-        self.emit("tila::tc_fence_after();")
-        for d in cl.dots:
-            col, N = acc_cols[d.acc]
-            ops = {}
-            for role, node, name in (("A", d.a, d.a_name), ("B", d.b, d.b_name)):
-                if name in cl.loads:
-                    sv = self._smem_val(D.f16, plans[name].shape,
-                                        SmemOperand(plans[name], f"{ring} + st * {stage} + {offs[name]}"))
-                else:
-                    sv = self.env[name]
-                ops[role] = sv
-            K = ops["A"].shape[1]
-            a_mn = self._operand_desc(ops["A"], "A", 0)[1]
-            b_mn = self._operand_desc(ops["B"], "B", 0)[1]
-            idesc = f"tila::idesc_f16_f32(128, {N}, {a_mn}, {b_mn})"
-            for kk in range(K // 16):
-                da, _ = self._operand_desc(ops["A"], "A", kk)
-                db, _ = self._operand_desc(ops["B"], "B", kk)
-                self.emit(f"tila::mma_f16_ss(tila_tmem + {col}, {da}, {db}, {idesc}, 1u);")
-        self.emit(f"tila::mma_commit({empty('st')});")
-        self.emit(f"const tila::i64 j = i + {S - 1};")
-        self.emit("if (j < cl_n) {")
-        self.indent += 1
-        self.emit(f"const int sj = (int)(j % {S});")
-        self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
-        issue("j", "sj")
-        self.indent -= 1
-        self.emit("}")
-        self.indent -= 1
-        self.emit("}")
+        def mmas():
+            for d in cl.dots:
+                col, N = acc_cols[d.acc]
+                ops = {}
+                for role, node, name in (("A", d.a, d.a_name), ("B", d.b, d.b_name)):
+                    if name in cl.loads:
+                        sv = self._smem_val(D.f16, plans[name].shape,
+                                            SmemOperand(plans[name], f"{ring} + st * {stage} + {offs[name]}"))
+                    else:
+                        sv = self.env[name]
+                    ops[role] = sv
+                K = ops["A"].shape[1]
+                a_mn = self._operand_desc(ops["A"], "A", 0)[1]
+                b_mn = self._operand_desc(ops["B"], "B", 0)[1]
+                idesc = f"tila::idesc_f16_f32(128, {N}, {a_mn}, {b_mn})"
+                for kk in range(K // 16):
+                    da, _ = self._operand_desc(ops["A"], "A", kk)
+                    db, _ = self._operand_desc(ops["B"], "B", kk)
+                    self.emit(f"tila::mma_f16_ss(tila_tmem + {col}, {da}, {db}, {idesc}, 1u);")
+            self.emit(f"tila::mma_commit({empty('st')});")
+
+        if self.T >= 64:
+            # copy producer (thread 32) refills a stage as soon as its MMAs have
+            # completed; the MMA issuer (thread 0) never waits on a refill
+            self.emit("if (tid == 32) {")
+            self.indent += 1
+            self.emit("for (tila::i64 j = 0; j < cl_n; ++j) {")
+            self.indent += 1
+            self.emit(f"const int sj = (int)(j % {S});")
+            self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
+            issue("j", "sj")
+            self.indent -= 1
+            self.emit("}")
+            self.indent -= 1
+            self.emit("}")
+            self.emit("if (tid == 0) {")
+            self.indent += 1
+            self.emit("for (tila::i64 i = 0; i < cl_n; ++i) {")
+            self.indent += 1
+            self.emit(f"const int st = (int)(i % {S});")
+            self.emit(f"tila::mbar_wait({full('st')}, (tila::u32)((i / {S}) & 1), tila_err, __LINE__, &tila_dead);")
+            self.emit("tila::tc_fence_after();")
+            mmas()
+            self.indent -= 1
+            self.emit("}")
+        else:
+            self.emit("if (tid == 0) {")
+            self.indent += 1
+            self.emit(f"for (tila::i64 j = 0; j < cl_n && j < {S - 1}; ++j) {{")
+            self.indent += 1
+            issue("j", "j")
+            self.indent -= 1
+            self.emit("}")
+            self.emit("for (tila::i64 i = 0; i < cl_n; ++i) {")
+            self.indent += 1
+            self.emit(f"const int st = (int)(i % {S});")
+            self.emit(f"tila::mbar_wait({full('st')}, (tila::u32)((i / {S}) & 1), tila_err, __LINE__, &tila_dead);")
+            self.emit("tila::tc_fence_after();")
+            mmas()
+            self.emit(f"const tila::i64 j = i + {S - 1};")
+            self.emit("if (j < cl_n) {")
+            self.indent += 1
+            self.emit(f"const int sj = (int)(j % {S});")
+            self.emit(f"if (j >= {S}) tila::mbar_wait({empty('sj')}, (tila::u32)(((j / {S}) - 1) & 1), tila_err, __LINE__, &tila_dead);")
+            issue("j", "sj")
+            self.indent -= 1
+            self.emit("}")
+            self.indent -= 1
+            self.emit("}")
         self.emit(f"tila::mma_commit({accbar});")
         self.indent -= 1
         self.emit("}")
