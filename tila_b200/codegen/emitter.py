@@ -206,6 +206,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._wg_candidate = False   # an asynchronous loop allows two programs per CTA
         self._free_smem = []         # (offset, bytes) of buffers no longer in use
         self._store_ring = None      # rotating TMA-store staging slots (see _try_tma_store)
+        self._contracted = False     # an FMA was contracted (see _try_contract)
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -401,8 +402,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             exprs = [self.elem(v, layout, "r") for v in ops]
             if isinstance(make_expr, _UniformDivisor) and not re.search(r"\br\b", exprs[1]):
                 self._uniform_division(name, None, exprs[1], exprs[0], layout.nreg)
-            elif isinstance(make_expr, _PackedBin) and dt.name == "f32" and layout.nreg % 2 == 0 \
-                    and layout.nreg >= 4:
+            elif isinstance(make_expr, (_PackedBin, _PackedFma)) and dt.name == "f32" \
+                    and layout.nreg % 2 == 0 and layout.nreg >= 4:
                 # two elements per f32x2 instruction
                 e0 = [self.elem(v, layout, "(r)") for v in ops]
                 e1 = [self.elem(v, layout, "(r + 1)") for v in ops]
@@ -775,6 +776,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     def e_TBin(self, x):
         dt, shape, is_ptr = self.vt_info(x.vt)
         op = x.op
+        fused = self._try_contract(x, dt, shape)
+        if fused is not None:
+            return fused
         l = self.value(x.left)
         if op in ("and", "or") and l.kind == "scalar" and l.const is not None:
             if op == "and" and not l.const:
@@ -806,6 +810,24 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                     return Val("func", D.bool_, tuple(shape), fn=lambda idx: "true")
         mk = self._bin_maker(op, odt, dt)
         return self.combine(dt, shape, [l, r], mk)
+
+    def _try_contract(self, x, dt, shape):
+        """In kernels with dots (compiled with multiply-add contraction, like
+        nvcc's default), an f32 tile sum whose operand is an unnamed product,
+        (a * b) + c, becomes one FMA per element."""
+        if x.op != "+" or not self.dot_rows or dt.name != "f32" or not shape or x.staged:
+            return None
+        for prod, other in ((x.left, x.right), (x.right, x.left)):
+            if isinstance(prod, T_.TBin) and prod.op == "*" and not prod.staged:
+                pdt, pshape, pptr = self.vt_info(prod.vt)
+                if pdt.name != "f32" or pptr or tuple(pshape) != tuple(shape):
+                    continue
+                a = self.coerce(self.value(prod.left), D.f32)
+                b = self.coerce(self.value(prod.right), D.f32)
+                c = self.coerce(self.value(other), D.f32)
+                self._contracted = True
+                return self.combine(dt, shape, [a, b, c], _PackedFma())
+        return None
 
     @staticmethod
     def _py_bin(op, a, b):
@@ -2209,7 +2231,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             floor_bytes = 233472 // (max_ctas + 1) - 1024 + 1
             smem = max(smem, floor_bytes)
         self.tmem_cols = cta_cols
-        return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma,
+        return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma or self._contracted,
                           tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
 
@@ -2224,6 +2246,15 @@ class _PackedBin:
 
     def __call__(self, e):
         return f"(({e[0]}) {self.op} ({e[1]}))"
+
+
+class _PackedFma:
+    """Expression maker of a contracted f32 a * b + c (one rounding); packed
+    two elements per f32x2 FMA like _PackedBin."""
+    fn = "fma2"
+
+    def __call__(self, e):
+        return f"__fmaf_rn(({e[0]}), ({e[1]}), ({e[2]}))"
 
 
 class _UniformDivisor:

@@ -312,10 +312,12 @@ class MmaMixin:
                 # MMAs complete in issue order: the accumulating dot issued
                 # before this one is done too (its buffers can be refilled)
                 self.wait_all_accs(release=True)
+            # refill the operands this dot consumed before waiting for the
+            # hand-off, so the copies overlap the wait
+            self.release_after_sync_dot([a, b])
             if getattr(ctx, "pingpong", False):
                 # start of the CUDA-core phase of the iteration (see WG_ACQUIRE)
                 self.emit(WG_ACQUIRE)
-            self.release_after_sync_dot([a, b])
         from .emitter import Val
         res = Val("tmem", D.f32, (M, N), tmem_col=col)
         reg = self.tmem_to_reg(res)
