@@ -1453,11 +1453,20 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             base = ring["base"] + slot * size
         else:
             ring = None
+            base = self._store_staging(size, allocate=False)
+        boxes = None
+        if base is None and lay.groups == 1 and len(self._box_slots(16384, 4)) >= 2:
+            # freed operand buffers hold at least two boxes: stage through them
+            # instead of a new allocation (less shared memory per CTA)
+            boxes = self._box_slots(16384, 4)
+        elif base is None:
             base = self._store_staging(size)
-        if base is None:
-            return False
+            if base is None:
+                return False
         tm = self.tensor_map_param(plan)
         origin = self._tma_coords(plan, coords)
+        if boxes is not None:
+            return self._box_ring_store(s, shape, value, lay, plan, tm, origin, boxes)
         col0 = "(tid >> 7) * %d + " % lay.cpg if lay.groups > 1 else ""
         self.emit(f"{{ // TMA store of {s.buffer} ({shape[0]}x{shape[1]} f32) through shared memory")
         self.indent += 1
@@ -1492,14 +1501,56 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self.emit("}")
         return True
 
-    def _store_staging(self, size):
+    def _box_slots(self, size, limit):
+        """Up to ``limit`` slots of ``size`` bytes carved from freed regions."""
+        slots = []
+        for off, n in self._free_smem:
+            o = (off + 1023) // 1024 * 1024
+            while o + size <= off + n and len(slots) < limit:
+                slots.append(o)
+                o += size
+        return slots
+
+    def _box_ring_store(self, s, shape, value, lay, plan, tm, origin, slots):
+        """TMA store staged one 32-column box at a time through a few freed
+        16 KB slots: each box waits only for the store that last used its
+        slot, so writing box b+1 overlaps the copy-out of box b."""
+        k = len(slots)
+        self.emit(f"{{ // TMA store of {s.buffer} ({shape[0]}x{shape[1]} f32) through {k} 16 KB staging slots")
+        self.indent += 1
+        self.emit("const int row_ = tid & 127;")
+        for b in range(plan.nbox):
+            slot = slots[b % k]
+            if b >= k:
+                self.emit(f"if (tid == 0) tila::bulk_wait_read_n<{k - 1}>();")
+                self.emit("__syncthreads();")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = {32 * b}; r < {32 * b + 32}; r += 4) {{")
+            self.emit(f"  *reinterpret_cast<float4*>(tila_smem + {slot} + row_ * 128 + "
+                      f"((((r % 32) / 4) ^ (row_ & 7)) * 16)) = "
+                      f"make_float4({value.name}[r], {value.name}[r + 1], {value.name}[r + 2], {value.name}[r + 3]);")
+            self.emit("}")
+            self.emit("tila::fence_proxy_async_smem();")
+            self.emit("__syncthreads();")
+            cs = list(origin)
+            if b:
+                cs[0] = f"({cs[0]} + {32 * b})"
+            self.emit(f"if (tid == 0) {{ tila::tma_store_{plan.rank}d(&{tm}, tila_smem + {slot}, {', '.join(cs)}); "
+                      f"tila::bulk_commit(); }}")
+        self.emit("if (tid == 0) tila::bulk_wait_read();")
+        self.emit("__syncthreads();")
+        self.indent -= 1
+        self.emit("}")
+        return True
+
+    def _store_staging(self, size, allocate=True):
         """Shared memory for a TMA store: a region freed by a finished
-        pipelined loop when one is large enough, else a new allocation
-        (None when that would not fit)."""
+        pipelined loop when one is large enough, else (``allocate``) a new
+        allocation (None when that would not fit)."""
         for off, n in self._free_smem:
             if n >= size:
                 return off
-        if self.smem.top + size > 200 * 1024:
+        if not allocate or self.smem.top + size > 200 * 1024:
             return None
         return self.smem.alloc(size, 1024)
 
@@ -1753,6 +1804,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 return
         if isinstance(s.value, T_.TLoad):
             v = self.try_tma_load(s.value, assigned_name=s.name)
+            if v is not None:
+                v.smem_name = s.name
         if v is None:
             v = self.value(s.value)
         if v.kind == "scalar" and v.const is None and not _is_simple(v.expr):
@@ -2165,6 +2218,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x + pid_off_0);")
         out.append("  const tila::i32 pid_1 = (tila::i32)(blockIdx.y + pid_off_1);")
         out.append("  const tila::i32 pid_2 = (tila::i32)(blockIdx.z + pid_off_2);")
+        if self.uses_mma:
+            # shared-memory matrix descriptors are built from this base (tila::sdesc)
+            out.append("  const tila::u32 tila_sb4 = tila::smem_u32(tila_smem) >> 4;")
         # fixed shared-memory head: mbarrier, tmem slot, dead flag; scratch follows the plan
         out.append(f"  tila::u64* tila_mma_bar = reinterpret_cast<tila::u64*>(tila_smem);")
         out.append(f"  tila::u32* tila_tmem_slot = reinterpret_cast<tila::u32*>(tila_smem + 8);")

@@ -44,6 +44,7 @@ class SmemOperand:
     bar: str | None = None     # mbarrier of a one-shot load (None: ready by construction)
     phase: str = "0u"
     flag: str | None = None
+    nbytes: int = 0            # size of a one-shot load's buffer (0: not a one-shot load)
 
 
 class MmaMixin:
@@ -161,7 +162,7 @@ class MmaMixin:
         flag = self._tma_state_var(f"tila_w_{bar_off}")
         self.emit(f"{flag} = 0u;")
         dt, shape, _ = self.vt_info(x.vt)
-        return self._smem_val(dt, shape, SmemOperand(plan, str(off), bar, phase, flag))
+        return self._smem_val(dt, shape, SmemOperand(plan, str(off), bar, phase, flag, nbytes=size))
 
     def _tma_state_var(self, name):
         """Per-thread state of a one-shot TMA barrier (declared at kernel entry)."""
@@ -198,9 +199,9 @@ class MmaMixin:
         if k_major:
             box, within = divmod(k0, 64)
             off = f"{op.base} + {box * plan.box_bytes + within * 2}"
-            return (f"tila::smem_desc(tila::smem_u32(tila_smem + {off}), 16, 1024, 2)", 0)
+            return (f"tila::sdesc<16, 1024, 2>(tila_sb4, (tila::u32)({off}))", 0)
         off = f"{op.base} + {k0 * 128}"
-        return (f"tila::smem_desc(tila::smem_u32(tila_smem + {off}), {plan.box_bytes}, 1024, 2)", 1)
+        return (f"tila::sdesc<{plan.box_bytes}, 1024, 2>(tila_sb4, (tila::u32)({off}))", 1)
 
     # -- dot ----------------------------------------------------------------------------
 
@@ -253,13 +254,13 @@ class MmaMixin:
         if a.kind != "smem":
             a_off = self.smem.alloc(128 * K * 2, 1024)
             self._stage_operand(a, a_off, K, transpose=False)
-            descs["A"] = lambda kk, o=a_off: (f"tila::smem_desc(tila::smem_u32(tila_smem + {o}) + {kk} * 256, 128, {K * 16}, 0)", 0)
+            descs["A"] = lambda kk, o=a_off: (f"tila::sdesc<128, {K * 16}, 0>(tila_sb4, (tila::u32)({o} + {kk} * 256))", 0)
         else:
             descs["A"] = lambda kk, v=a: self._operand_desc(v, "A", kk)
         if b.kind != "smem":
             b_off = self.smem.alloc(Npad * K * 2, 1024)
             self._stage_operand(b, b_off, K, transpose=True)
-            descs["B"] = lambda kk, o=b_off: (f"tila::smem_desc(tila::smem_u32(tila_smem + {o}) + {kk} * 256, 128, {K * 16}, 0)", 0)
+            descs["B"] = lambda kk, o=b_off: (f"tila::sdesc<128, {K * 16}, 0>(tila_sb4, (tila::u32)({o} + {kk} * 256))", 0)
         else:
             descs["B"] = lambda kk, v=b: self._operand_desc(v, "B", kk)
         accumulate = "0"
@@ -307,6 +308,15 @@ class MmaMixin:
         self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
         self.emit("tila_mma_phase ^= 1u;")
         self.emit("tila::tc_fence_after();")
+        if ctx is None and not self._loopvars:
+            # one-shot TMA operands read only by this dot are dead once its MMAs
+            # completed: their shared memory can stage later stores
+            for v in (a, b):
+                name = getattr(v, "smem_name", None)
+                op = getattr(v, "smem", None)
+                if v.kind == "smem" and name and len(self.uses.get(name, [])) == 1 \
+                        and op.nbytes and op.base.isdigit():
+                    self._free_smem.append((int(op.base), op.nbytes))
         if ctx is not None:
             if hoist:
                 # MMAs complete in issue order: the accumulating dot issued

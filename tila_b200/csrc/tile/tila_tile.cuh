@@ -534,6 +534,20 @@ __device__ __forceinline__ u64 smem_desc(u32 saddr, u32 lbo, u32 sbo, u32 swizzl
   return d;
 }
 
+// The same descriptor from a precomputed base: base4 = (shared address of the
+// dynamic shared memory) >> 4 and a 16-byte aligned offset; the LBO / SBO /
+// swizzle fields are compile-time constants.  Costs one add and one OR per
+// descriptor instead of recomputing every field (the MMA-issuing thread is
+// otherwise the bottleneck for N <= 128 instructions).  Shared addresses stay
+// below 2^18, so the start-address field cannot carry into LBO.
+template <u32 LBO, u32 SBO, u32 SW>
+__device__ __forceinline__ u64 sdesc(u32 base4, u32 off) {
+  constexpr u64 fields = (static_cast<u64>((LBO >> 4) & 0x3FFFu) << 16) |
+                         (static_cast<u64>((SBO >> 4) & 0x3FFFu) << 32) |
+                         (static_cast<u64>(1) << 46) | (static_cast<u64>(SW & 7u) << 61);
+  return fields | static_cast<u64>(base4 + (off >> 4));
+}
+
 // Instruction descriptor for kind::f16 with f16 inputs and f32 accumulate:
 //   [4,6) D format (1 = f32), [7,10) A format (0 = f16), [10,13) B format,
 //   [15] A major (0 = K-major, 1 = MN-major), [16] B major,
