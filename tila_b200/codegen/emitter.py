@@ -1787,6 +1787,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             # source map: the generated code below comes from this Tila line
             self.emit(f"// @tila-line {line}")
         m(s)
+        if self.actx is not None:
+            self.emit_early_p(s)
 
     def s_TAssign(self, s):
         v = None

@@ -651,6 +651,8 @@ class AsyncLoopMixin:
         ctx = AsyncCtx(al, s.var, stepv, f"(tila::i64)({end.expr})", {}, {})
         ctx.body = s.body
         ctx.cast_loads = set(al.cast_loads)
+        ctx.p_early_after = self._early_p_points(s.body, al)
+        ctx.p_early = False
         for name, ld in al.loads.items():
             plan = self.tma_plan(ld, cast=name in al.cast_loads)
             size = plan.nbox * max(plan.outer_extent, 128) * 128
@@ -716,6 +718,79 @@ class AsyncLoopMixin:
             self._wg_candidate = True
         self.actx = ctx
         return ctx
+
+    def _early_p_points(self, body, al):
+        """{id(statement): (acc name, register tile name)}: for an accumulating
+        dot whose A operand is cast[f16](R) of a register tile R, the last
+        statement of the loop body before the dot that mentions R.  P is
+        packed and stored into tensor memory right after it, so R's
+        registers are free for the rest of the iteration (the dot then only
+        issues the MMAs)."""
+        points = {}
+        for name, dot in al.accs.items():
+            if not (isinstance(dot.a, T_.TCast) and isinstance(dot.a.operand, T_.TName)):
+                continue
+            r = dot.a.operand.name
+            if r in al.loads:
+                continue
+            d = next((i for i, st in enumerate(body)
+                      if isinstance(st, T_.TAssign) and st.value is dot), None)
+            if d is None:
+                continue
+
+            def mentions(node, found=None):
+                found = found if found is not None else [False]
+                if isinstance(node, T_.TName) and node.name == r:
+                    found[0] = True
+                if isinstance(node, T_.TAssign) and node.name == r:
+                    found[0] = True
+                if dataclasses.is_dataclass(node):
+                    for f in dataclasses.fields(node):
+                        if f.name in ("vt", "definition", "effect"):
+                            continue
+                        v = getattr(node, f.name)
+                        for x in (v if isinstance(v, list) else [v]):
+                            if dataclasses.is_dataclass(x):
+                                mentions(x, found)
+                return found[0]
+            k = max((i for i in range(d) if mentions(body[i])), default=None)
+            if k is None or not (isinstance(body[k], T_.TAssign) or any(
+                    isinstance(body[i], T_.TAssign) and body[i].name == r for i in range(k))):
+                continue
+            points[id(body[k])] = (name, r)
+        return points
+
+    def emit_early_p(self, st):
+        """Called after each statement of an asynchronous loop body."""
+        ctx = self.actx
+        if ctx is None or id(st) not in getattr(ctx, "p_early_after", {}):
+            return
+        name, r = ctx.p_early_after[id(st)]
+        v = self.env.get(r)
+        if v is None or v.kind not in ("reg", "func", "tmem"):
+            return
+        self.wait_all_accs(release=True)
+        self._store_p(v, ctx)
+        ctx.p_early = True
+
+    def _store_p(self, pv, ctx):
+        """cast[f16](R): round and pack pairs from R and store them into the
+        P columns of tensor memory (one cvt per pair)."""
+        K = pv.shape[1]
+        play = TmemRows((128, K), self.T)
+        if pv.dt.name not in ("f32", "f16"):
+            pv = self.coerce(pv, D.f32)
+        pv = self.materialize(pv, play) if not (pv.kind == "reg" and pv.layout == play) else pv
+        half = play.nreg // 2
+        self.emit("{")
+        self.indent += 1
+        self.emit(f"float pk[{half}];")
+        self.emit("#pragma unroll")
+        self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float(tila::pack_f16x2({pv.name}[2 * c], {pv.name}[2 * c + 1]));")
+        goff = f" + (tid >> 7) * {play.cpg // 2}" if play.groups > 1 else ""
+        self.emit(f"tila::tmem_store_row<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
+        self.indent -= 1
+        self.emit("}")
 
     def _reuse_smem(self, size):
         """1024-aligned shared memory for a loop buffer: part of a region a
@@ -888,26 +963,18 @@ class AsyncLoopMixin:
         K = bv.shape[0]
         ts = isinstance(x.a, T_.TCast)
         cast_src = None
-        if ts:
+        if ts and ctx.p_early:
+            # P was packed into tensor memory right after its last other use
+            ctx.p_early = False
+            adesc = None
+        elif ts:
             # cast[f16](R): round and pack pairs straight from R (one cvt per pair)
             pv = self.value(x.a.operand)
             play = TmemRows((128, K), self.T)
             if pv.kind == "smem":
                 cast_src = getattr(pv, "smem_name", None)
                 pv = self.smem_rows_to_reg(pv, play)
-            if pv.dt.name not in ("f32", "f16"):
-                pv = self.coerce(pv, D.f32)
-            pv = self.materialize(pv, play) if not (pv.kind == "reg" and pv.layout == play) else pv
-            half = play.nreg // 2
-            self.emit("{")
-            self.indent += 1
-            self.emit(f"float pk[{half}];")
-            self.emit("#pragma unroll")
-            self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float(tila::pack_f16x2({pv.name}[2 * c], {pv.name}[2 * c + 1]));")
-            goff = f" + (tid >> 7) * {play.cpg // 2}" if play.groups > 1 else ""
-            self.emit(f"tila::tmem_store_row<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
-            self.indent -= 1
-            self.emit("}")
+            self._store_p(pv, ctx)
             adesc = None
         else:
             av = self.value(x.a)
