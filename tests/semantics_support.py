@@ -233,3 +233,32 @@ def kernel(a: ti.Buffer[ti.f16, (B, M, K), ti.ReadOnly],
         total = ti.dot(lhs, rhs, acc=total)
     ti.store(c, (h, rows[:, None], cols[None, :]), total, mask=row_ok[:, None] & col_ok[None, :])
 ''')
+
+
+def rank3_program(directory, op="sum", axis=2):
+    """512-element blocks reshaped to (4, 8, 16) tiles, reduced along one
+    axis (sum or max, after an element-wise exp / scale and a product with a
+    (4, 1, 16) broadcast operand), reshaped back to 1-D and stored."""
+    keep = [d for i, d in enumerate((4, 8, 16)) if i != axis]
+    n_out = keep[0] * keep[1]
+    body = "ti.exp(t * 0.25)" if op == "max" else "t * 2.0"
+    return load_source(directory, f"sem_r3_{op}_{axis}", f'''import tila as ti
+N = ti.Dim("N")
+M = ti.Dim("M")
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.f32, (N,), ti.ReadOnly],
+           w: ti.Buffer[ti.f32, (M,), ti.ReadOnly],
+           out: ti.Buffer[ti.f32, (M,), ti.WriteOnly]):
+    pid = ti.program_id(0)
+    i = pid * 512 + ti.arange(0, 512)
+    v = ti.load(x, i, mask=i < N, other=0.0)
+    k = pid * 64 + ti.arange(0, 64)
+    g = ti.load(w, k, mask=k < M, other=1.0)
+    t = ti.reshape(v, (4, 8, 16))
+    b = ti.reshape(g, (4, 1, 16))
+    s = ti.{op}({body} * b, {axis})
+    u = ti.reshape(s, ({n_out},))
+    j = pid * {n_out} + ti.arange(0, {n_out})
+    ti.store(out, j, u, mask=j < M)
+''')

@@ -184,3 +184,14 @@ def test_batched_matmul_uses_split_copy_and_mma_threads(tmp_path):
     assert "pipelined contraction loop" in spec.source and "if (tid == 32)" in spec.source
     assert not spec.fuse
     native.compile_spec(spec)
+
+
+def test_rank3_tiles_compile(tmp_path):
+    """Tiles of rank 3 (from reshape) get a blocked layout over the flattened
+    leading dimensions; reductions along every axis compile."""
+    import semantics_support as S
+    for op in ("sum", "max"):
+        for axis in (0, 1, 2):
+            k = S.rank3_program(tmp_path, op, axis)
+            spec = gen(k, dict(x=torch.zeros(1000), w=torch.zeros(384), out=torch.zeros(384)))
+            native.compile_spec(spec)

@@ -356,3 +356,27 @@ def test_ptr_form_load_store(n):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(down(out), cpu)
     np.testing.assert_array_equal(cpu, x + x)
+
+
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("axis", [0, 1, 2])
+def test_rank3_tiles_match_interpreter(tmp_path, op, axis):
+    """(4, 8, 16) tiles from reshape: element-wise work, a broadcast (4, 1, 16)
+    operand and a reduction along each axis, against the interpreter."""
+    k = S.rank3_program(tmp_path, op, axis)
+    n_out = {0: 128, 1: 64, 2: 32}[axis]
+    progs = 5
+    rng = np.random.default_rng(40 + axis)
+    x = rng.standard_normal(512 * progs - 37).astype(np.float32)
+    w = rng.standard_normal(max(64, n_out) * progs).astype(np.float32)
+    cpu = np.zeros_like(w)
+    k[(progs,)](x, w, cpu)
+    gpu = torch.zeros(w.size, device="cuda")
+    k[(progs,)](torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), gpu)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    got = gpu.cpu().numpy()
+    if op == "max":
+        np.testing.assert_allclose(got, cpu, rtol=1e-6, atol=0)
+    else:
+        np.testing.assert_allclose(got, cpu, rtol=1e-5, atol=1e-6)

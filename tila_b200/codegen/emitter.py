@@ -302,8 +302,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if len(shape) == 2 and shape[0] <= 128 and any(
                 shape[0] == m and shape[1] in (n, 1) for m, n in self.dot_rows):
             return TmemRows(tuple(shape), self.T)
-        if len(shape) not in (1, 2):
-            self.fail(f"tiles of rank {len(shape)} are not supported by the B200 backend")
+        if not shape or any(int(n) & (int(n) - 1) for n in shape):
+            self.fail(f"tile shape {tuple(shape)} is not a product of powers of two")
         last = shape[-1]
         V = 4
         if dt is not None and DT.size(dt) == 2:

@@ -73,7 +73,8 @@ def _tid_table(T):
 
 @dataclass(eq=False)
 class Blocked(Layout):
-    """Row-major blocked distribution of an (R, C) tile (1-D tiles: R = 1, rank 1).
+    """Row-major blocked distribution of an (R, C) tile (1-D tiles: R = 1, rank 1;
+    rank >= 3: R is the product of the leading dimensions, row-major).
 
     Threads form a ``tr x tc`` grid with columns fastest (coalesced).  Each
     thread holds ``RA`` rows (strided by ``tr``) and ``CB`` chunks of ``V``
@@ -86,7 +87,10 @@ class Blocked(Layout):
 
     def __post_init__(self):
         self.rank = len(self.shape)
-        R, C = (1, self.shape[0]) if self.rank == 1 else self.shape
+        if self.rank == 1:
+            R, C = 1, self.shape[0]
+        else:
+            R, C = int(np.prod(self.shape[:-1])), self.shape[-1]
         self.R, self.C = R, C
         V = min(self.V, C)
         self.V = V
@@ -116,7 +120,15 @@ class Blocked(Layout):
         if self.rank == 1:
             return (col,)
         row = f"({trow} + {self.tr} * {a})"
-        return (row, col)
+        if self.rank == 2:
+            return (row, col)
+        lead = self.shape[:-1]
+        out = []
+        for k in range(len(lead)):
+            stride = int(np.prod(lead[k + 1:]))
+            e = f"({row} / {stride})" if stride > 1 else row
+            out.append(f"({e} % {lead[k]})" if k else e)
+        return (*out, col)
 
     def owner_expr(self, r):
         return None if self.active >= self.T else f"(tid < {self.active})"
@@ -134,8 +146,12 @@ class Blocked(Layout):
         owner = np.broadcast_to(tid < self.active, (T, self.nreg))
         if self.rank == 1:
             coords = col[..., None]
-        else:
+        elif self.rank == 2:
             coords = np.stack(np.broadcast_arrays(row, col), axis=-1)
+        else:
+            lead = self.shape[:-1]
+            parts = [(row // int(np.prod(lead[k + 1:]))) % lead[k] for k in range(len(lead))]
+            coords = np.stack(np.broadcast_arrays(*parts, col), axis=-1)
         return np.broadcast_to(coords, (T, self.nreg, self.rank)).copy(), owner.copy()
 
     # thread-index bits that separate the partial results of a reduction
@@ -144,7 +160,14 @@ class Blocked(Layout):
         lc, lr = int(math.log2(self.tc)), int(math.log2(self.tr))
         if self.rank == 1 or axis == self.rank - 1:
             return list(range(0, lc))
-        return list(range(lc, lc + lr))
+        if self.rank == 2:
+            return list(range(lc, lc + lr))
+        # a leading axis occupies bits [lo, hi) of the flattened row index; the
+        # thread's row (tid bits lc..lc+lr) holds the row index's low lr bits
+        lead = self.shape[:-1]
+        lo = int(math.log2(int(np.prod(lead[axis + 1:]))))
+        hi = lo + int(math.log2(lead[axis]))
+        return [lc + b for b in range(lo, min(hi, lr))]
 
 
 @dataclass(eq=False)
