@@ -51,7 +51,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 L2_BYTES = 126 * (1 << 20)
-ORDER = ["softmax", "add", "matmul", "unfused_attention", "fused_attention"]
+ORDER = ["softmax", "add", "matmul", "unfused_attention", "fused_attention", "fused_attention_causal"]
 
 
 def _peaks():
@@ -298,6 +298,34 @@ class Case:
                                     lambda args, out: W.flash_attention[grid](*args, out, scale,
                                                                               BM=128, BN=128, BD=128))
 
+    # -- causal fused attention (the CAUSAL=1 kernel of the same example) --
+    def _setup_fused_attention_causal(self):
+        W, torch = self.W, self.torch
+        bh1, l, d = 128, 4096, 128
+        bh = bh1 * self.world
+        q, k, v = W.attention_inputs(bh, l, d, seed=0)
+        self.host_inputs = [q, k, v]
+        self.sets = [(self._dev(q), self._dev(k), self._dev(v),
+                      torch.empty((bh, l, d), device=self.device))]
+        grid = (l // 128, bh)
+        self.axis, self.grid_axis_total = 1, bh
+        scale = d ** -0.5
+        self.launches = [lambda s: W.flash_attention_causal[grid](s[0], s[1], s[2], s[3], scale,
+                                                                  BM=128, BN=128, BD=128)]
+        self.kernels = [W.flash_attention_causal]
+        self.out_index = 3
+        self.units_per_rank = W.causal_flops(bh1, l, d)
+        self.dominant = 0
+        self.dominant_units = self.units_per_rank
+        self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
+        self.dtype = "f16 in, f32 accumulate"
+        self.config = {"workload": "fused_attention_causal", "batch": 4, "heads": 32, "seq": l,
+                       "head_dim": d, "BM": 128, "BN": 128, "causal": True,
+                       "flop_count": "half of the non-causal 4*BH*L^2*D"}
+        self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
+                                    lambda args, out: W.flash_attention_causal[grid](
+                                        *args, out, scale, BM=128, BN=128, BD=128))
+
     # -- launching ---------------------------------------------------------
 
     def _ranges(self):
@@ -448,7 +476,7 @@ def run_ours(args, world, rank, device, keys):
 
 
 W_ROOF = {"add": "hbm", "softmax": "hbm", "matmul": "tensor", "unfused_attention": "hbm",
-          "fused_attention": "tensor"}
+          "fused_attention": "tensor", "fused_attention_causal": "tensor"}
 
 
 def _gather(out, case, world, rank, device):
@@ -565,6 +593,12 @@ def cpu_baseline(key, repeats=1):
             W.attention_pv[(8, 1)](p, v, o, BM=128, BN=128, BD=64)
         units, unit, scale = W.unfused_flops(1, 1024, 64), "TFLOP/s", 1e12
         sample, cores = "1 of the 128 batch*heads (L=1024, D=64)", _blas_threads()
+    elif key == "fused_attention_causal":
+        q, k, v = W.attention_inputs(1, 4096, 128)
+        o = np.zeros((1, 4096, 128), np.float32)
+        fn = lambda: W.flash_attention_causal[(32, 1)](q, k, v, o, 128 ** -0.5, BM=128, BN=128, BD=128)
+        units, unit, scale = W.causal_flops(1, 4096, 128), "TFLOP/s", 1e12
+        sample, cores = "1 of the 128 batch*heads (L=4096, D=128, causal)", _blas_threads()
     else:
         q, k, v = W.attention_inputs(1, 4096, 128)
         o = np.zeros((1, 4096, 128), np.float32)

@@ -380,5 +380,12 @@ def fused_flops(bh=128, l=4096, d=128):
     return 4 * bh * l * l * d
 
 
+def causal_flops(bh=128, l=4096, d=128):
+    """Causal attention counted as half of the full score and P@V work (the
+    usual convention; the kernel also computes the masked half of the
+    diagonal blocks)."""
+    return 2 * bh * l * l * d
+
+
 def cdiv(a, b):
     return -(-a // b)
