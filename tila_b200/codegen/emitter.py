@@ -207,6 +207,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._free_smem = []         # (offset, bytes) of buffers no longer in use
         self._store_ring = None      # rotating TMA-store staging slots (see _try_tma_store)
         self._contracted = False     # an FMA was contracted (see _try_contract)
+        self._uneven_loops = 0       # hand-off loops with program-dependent trip counts
+        self._loop_acc_cols = set()  # (column, N) of asynchronous-loop accumulators
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -2182,7 +2184,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         per_prog = -(-(scratch_off + self.smem.scratch) // 1024) * 1024
         # two programs of axis 0 per CTA, one per warpgroup (see _pingpong_ok)
         wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
-              and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448)
+              and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3)
         if wg:
             self.fuse = {0: 2}
         for ax in sorted(self.fuse or {}):
@@ -2212,6 +2214,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append("  const bool tila_live = (tila::i32)(blockIdx.x * 2 + tila_wg) < launch_0;")
             out.append("  const bool tila_partner_live = (tila::i32)(blockIdx.x * 2 + (tila_wg ^ 1)) < launch_0;")
             out.append(f"  tila::u64* const tila_tok = reinterpret_cast<tila::u64*>(tila_smem_all + {2 * per_prog});")
+            out.append(f"  volatile tila::i64* const tila_trips = reinterpret_cast<volatile tila::i64*>(tila_smem_all + {2 * per_prog + 16});")
+            out.append("  (void)tila_trips;")
             out.append("  tila::u32 tila_tok_ph = 0, tila_tok_n = 0;")
             out.append("  (void)tila_partner_live; (void)tila_tok; (void)tila_tok_ph; (void)tila_tok_n;")
         else:
@@ -2262,19 +2266,37 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append("  __syncthreads();")
         out.append("  do {")
         if wg:
-            from .mma import WG_ACQUIRE, WG_RELEASE
+            from .mma import WG_ACQUIRE, WG_RELEASE, WG_TRIPS, WG_TURNS
             acquire = ("if (tila_partner_live && (tila_wg == 1 || tila_tok_n > 0)) { "
                        "tila::mbar_wait(&tila_tok[tila_wg], tila_tok_ph, tila_err, __LINE__, &tila_dead); "
                        "tila_tok_ph ^= 1u; } ++tila_tok_n;")
             release = "if (tila_partner_live) tila::mbar_arrive(&tila_tok[tila_wg ^ 1]);"
             out.append("    if (!tila_live) break;")
             for line in body:
+                st = line.strip()
+                ind = line[:len(line) - len(line.lstrip())]
+                if st.startswith(WG_TRIPS):
+                    # both programs reach this point (no early exits); a CTA-wide
+                    # barrier orders the exchange (the partner is live, so both run)
+                    k = int(st.split()[-1])
+                    out.append(f"{ind}tila::i64 tila_ptrip_{k} = 0;")
+                    out.append(f"{ind}if (tila_partner_live) {{")
+                    out.append(f"{ind}  if (tid == 0) tila_trips[{2 * k} + tila_wg] = tila_trip_{k};")
+                    out.append(f"{ind}  tila::cta_sync();")
+                    out.append(f"{ind}  tila_ptrip_{k} = tila_trips[{2 * k} + (tila_wg ^ 1)];")
+                    out.append(f"{ind}}}")
+                    continue
+                if st.startswith(WG_TURNS):
+                    k = int(st.split()[-1])
+                    out.append(f"{ind}for (tila::i64 t_ = tila_trip_{k}; t_ < tila_ptrip_{k}; ++t_) {{ {acquire} {release} }}")
+                    continue
                 line = line.replace("__syncthreads();", "tila::wg_sync(tila_wg);")
                 line = line.replace(WG_ACQUIRE, acquire).replace(WG_RELEASE, release)
                 out.append(line)
         else:
-            from .mma import WG_ACQUIRE, WG_RELEASE
-            out.extend(l for l in body if l.strip() not in (WG_ACQUIRE, WG_RELEASE))
+            from .mma import WG_ACQUIRE, WG_RELEASE, WG_TRIPS, WG_TURNS
+            out.extend(l for l in body if l.strip() not in (WG_ACQUIRE, WG_RELEASE)
+                       and not l.strip().startswith((WG_TRIPS, WG_TURNS)))
         out.append("  } while (0);")
         if self.uses_tmem:
             out.append("  tila::tc_fence_before();")

@@ -601,6 +601,11 @@ class MmaMixin:
 # and releases it when it issues the accumulating dot.
 WG_ACQUIRE = "/*@wg_acquire*/"
 WG_RELEASE = "/*@wg_release*/"
+# loops whose trip count depends on program_id(0): "WG_TRIPS k" before the
+# loop (exchange of the two programs' trip counts), "WG_TURNS k" after it (the
+# program with fewer iterations takes the partner's remaining hand-off turns)
+WG_TRIPS = "/*@wg_trips*/"
+WG_TURNS = "/*@wg_turns*/"
 
 
 @dataclass
@@ -665,7 +670,13 @@ class AsyncLoopMixin:
                                    flag=self._tma_state_var(f"tila_w_{bar_off}"))
         for name, dot in al.accs.items():
             _, (M, N), _ = self.vt_info(dot.vt)
-            col = self.tmem_alloc_cols(N)
+            pre = self.env.get(name)
+            if pre is not None and pre.kind == "tmem" and (str(pre.tmem_col), N) in self._loop_acc_cols:
+                # the accumulator of an earlier loop continues in place
+                col = int(pre.tmem_col)
+            else:
+                col = self.tmem_alloc_cols(N)
+                self._loop_acc_cols.add((str(col), N))
             bar_off = self.smem.alloc(8, 8)
             releases = [op.name for op in (dot.a, dot.b)
                         if isinstance(op, T_.TName) and op.name in al.loads]
@@ -684,6 +695,8 @@ class AsyncLoopMixin:
         for name, a in ctx.accs.items():
             pre = self.env[name]
             lay = TmemRows((128, a["N"]), self.T)
+            if pre.kind == "tmem" and str(pre.tmem_col) == str(a["col"]):
+                continue
             if pre.kind == "tmem":
                 pre = self.tmem_to_reg(pre)
             if pre.dt.name != "f32":
@@ -714,8 +727,19 @@ class AsyncLoopMixin:
             v = Val("tmem", D.f32, (128, a["N"]), tmem_col=str(a["col"]))
             self.env[name] = v
         ctx.pingpong = self._pingpong_ok(s, start, al)
+        ctx.turns = None
         if ctx.pingpong:
             self._wg_candidate = True
+            if any(node is not None and not self._pid0_free(node) for node in (s.start, s.end)):
+                # the partner program may run a different number of iterations:
+                # exchange trip counts, and let the shorter one take its
+                # remaining hand-off turns after its loop (see WG_TRIPS)
+                k = self._uneven_loops
+                self._uneven_loops += 1
+                ctx.turns = k
+                self.emit(f"const tila::i64 tila_trip_{k} = ((tila::i64)({end.expr}) > (tila::i64)({start.expr})) ? "
+                          f"((tila::i64)({end.expr}) - (tila::i64)({start.expr}) + {stepv - 1}) / {stepv} : 0;")
+                self.emit(f"{WG_TRIPS} {k}")
         self.actx = ctx
         return ctx
 
@@ -816,9 +840,10 @@ class AsyncLoopMixin:
             _walk(st, lambda n: has_return.__setitem__(0, has_return[0] or isinstance(n, T_.TReturn)))
         if has_return[0] or len(al.accs) != 1:
             return False
-        for node in (s.start, s.end, s.step):
-            if node is not None and not self._pid0_free(node):
-                return False
+        # bounds that depend on program_id(0) are allowed (the two programs then
+        # run different trip counts; see the token turns in generate())
+        if s.step is not None and not self._pid0_free(s.step):
+            return False
         dots = []
         for st in s.body:
             _walk(st, lambda n: dots.append(n) if isinstance(n, T_.TDot) else None)
@@ -1106,6 +1131,8 @@ class AsyncLoopMixin:
 
     def finish_async_loop(self, ctx):
         from .emitter import Val
+        if getattr(ctx, "turns", None) is not None:
+            self.emit(f"{WG_TURNS} {ctx.turns}")
         for name in ctx.accs:
             self.emit_acc_wait(name, release=False)
         # all loop copies were consumed (the last iteration issues none)

@@ -393,6 +393,8 @@ __device__ __forceinline__ void grid_dep_release() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Barrier over the whole CTA (both warpgroups in two-program mode).
+__device__ __forceinline__ void cta_sync() { __syncthreads(); }
 // Barrier of one 128-thread warpgroup (named barrier 1 + wg) in kernels that
 // run one program per warpgroup.
 __device__ __forceinline__ void wg_sync(int wg) {
