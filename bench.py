@@ -404,6 +404,10 @@ def run_ours(args, world, rank, device, keys):
             while time.perf_counter() < t_end:
                 graph.replay()
                 torch.cuda.synchronize(device)
+            # a short device-side spin ahead of the start event keeps the GPU
+            # busy while the host submits the graph, so the events bracket the
+            # K steps themselves, not the host's graph-launch latency
+            torch.cuda._sleep(200_000)
             start.record(cur)
             graph.replay()
             end.record(cur)
