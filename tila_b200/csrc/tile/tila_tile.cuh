@@ -526,22 +526,12 @@ __device__ __forceinline__ void tc_fence_after() {
 //   [32,46) stride byte offset >> 4, [46,48) version = 1,
 //   [49,52) base offset, [52] LBO mode, [61,64) swizzle mode
 //   (0 none, 2 = 128B, 4 = 64B, 6 = 32B).
-__device__ __forceinline__ u64 smem_desc(u32 saddr, u32 lbo, u32 sbo, u32 swizzle) {
-  u64 d = 0;
-  d |= static_cast<u64>((saddr & 0x3FFFFu) >> 4);
-  d |= static_cast<u64>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<u64>((sbo >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<u64>(1) << 46;
-  d |= static_cast<u64>(swizzle & 7u) << 61;
-  return d;
-}
-
-// The same descriptor from a precomputed base: base4 = (shared address of the
-// dynamic shared memory) >> 4 and a 16-byte aligned offset; the LBO / SBO /
-// swizzle fields are compile-time constants.  Costs one add and one OR per
-// descriptor instead of recomputing every field (the MMA-issuing thread is
-// otherwise the bottleneck for N <= 128 instructions).  Shared addresses stay
-// below 2^18, so the start-address field cannot carry into LBO.
+// Built from a precomputed base: base4 = (shared address of the dynamic
+// shared memory) >> 4 and a 16-byte aligned offset; the LBO / SBO / swizzle
+// fields are compile-time constants, so a descriptor costs one add and one OR
+// (the MMA-issuing thread would otherwise spend more time building
+// descriptors than an N <= 128 instruction takes to execute).  Shared
+// addresses stay below 2^18, so the start-address field cannot carry into LBO.
 template <u32 LBO, u32 SBO, u32 SW>
 __device__ __forceinline__ u64 sdesc(u32 base4, u32 off) {
   constexpr u64 fields = (static_cast<u64>((LBO >> 4) & 0x3FFFu) << 16) |
