@@ -146,7 +146,7 @@ def test_fused_attention_ragged_128_tiles(l, d):
     assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
 
 
-@pytest.mark.parametrize("l,d,blk", [(65, 32, 32), (256, 64, 128)])
+@pytest.mark.parametrize("l,d,blk", [(65, 32, 32), (256, 64, 128), (200, 64, 128)])
 def test_unfused_attention(l, d, blk):
     bh = 2
     q, k, v = W.attention_inputs(bh, l, d, seed=12)
