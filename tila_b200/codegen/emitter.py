@@ -209,6 +209,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._contracted = False     # an FMA was contracted (see _try_contract)
         self._uneven_loops = 0       # hand-off loops with program-dependent trip counts
         self._loop_acc_cols = set()  # (column, N) of asynchronous-loop accumulators
+        self._prefetch = []          # L2 prefetches of top-level loads (see _prefetch_load)
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -1212,6 +1213,36 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         return self._tile_load(x.buffer, list(x.coords), coords, mask, other, dt, shape, layout,
                                mask_node=x.mask)
 
+    _PREFETCH_NAMES = re.compile(r"\b(?!tid\b|pid_[012]\b|p_\w+\b|nprog_[012]\b|pid_off_[012]\b|"
+                                 r"launch_[012]\b|tila\b|r0\b|r\b|g\b|off\b|all\b|a_\b|int\b|bool\b|"
+                                 r"const\b|true\b|false\b|return\b|pragma\b|unroll\b|for\b|if\b)"
+                                 r"(?<!::)(?<![\w.])[A-Za-z_]\w*")
+
+    def _prefetch_load(self, buffer, layout, groups, width, dt, off, lane_cond):
+        """A load at the top level of the program (not in a loop or branch)
+        whose addresses and bounds depend only on program ids, thread index
+        and kernel parameters: the same groups are prefetched into L2 ahead of
+        the grid-dependency wait (one thread per 64 bytes)."""
+        if self._loopvars or self.actx is not None or self._guard_mode:
+            return
+        if DT.size(dt) * width != 16 or groups > 16 or not isinstance(layout, Blocked):
+            return
+        allc = "true" if lane_cond is None else \
+            f"[&] {{ int r = r0; const bool a_ = {lane_cond}; r = r0 + {width - 1}; return a_ && ({lane_cond}); }}()"
+        who = "(tid & 3) == 0" if layout.tc >= 4 else "true"
+        code = (f"{{ // L2 prefetch of {buffer}\n"
+                f"  #pragma unroll\n"
+                f"  for (int g = 0; g < {groups}; ++g) {{\n"
+                f"    const int r0 = g * {width};\n"
+                f"    const tila::i64 off = {off};\n"
+                f"    if (({who}) && {allc}) tila::prefetch_l2(p_{buffer} + off);\n"
+                f"  }}\n"
+                f"}}")
+        if self._PREFETCH_NAMES.search(f"{off} {lane_cond or ''}"):
+            return
+        if len(self._prefetch) < 8:
+            self._prefetch.append(code)
+
     def _scalar_load(self, buffer, coords, mask, other, dt):
         name = self.fresh("ld")
         addr = " + ".join(f"(tila::i64)p_{buffer}_stride{i} * (tila::i64)({c.expr})"
@@ -1225,6 +1256,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         return Val("scalar", dt, expr=name)
 
     def _tile_load(self, buffer, coord_nodes, coords, mask, other, dt, shape, layout, mask_node=None):
+        top_level = self.indent == 2
         ops = list(coords) + ([mask] if mask is not None else []) + ([other] if other is not None else [])
         ops, maps, straight = self.prepare_operands(ops, layout, shape)
         nc = len(coords)
@@ -1273,6 +1305,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 self.emit(f"for (int j = 0; j < {width}; ++j) {{ const int r = r0 + j; m[j] = {lane_cond}; all = all && m[j]; }}")
             else:
                 self.emit("const bool all = true;")
+            if top_level and (lane_cond is None or interval):
+                self._prefetch_load(buffer, layout, groups, width, dt, off, lane_cond)
             cond = "all" if aligned else f"all && ((reinterpret_cast<unsigned long long>(p_{buffer} + off) & {DT.size(dt) * width - 1}) == 0)"
             self.emit(f"if ({cond}) {{")
             self.emit(f"  const {vt} w = *reinterpret_cast<const {vt}*>(p_{buffer} + off);")
@@ -2246,7 +2280,10 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append("  if (threadIdx.x == 0) { tila::mbar_init(&tila_tok[0], 128); "
                        "tila::mbar_init(&tila_tok[1], 128); tila::mbar_fence_init(); }")
         # everything above touches only shared memory and kernel parameters;
-        # global memory (and tensor memory) only after the previous grid ends
+        # global memory (and tensor memory) only after the previous grid ends,
+        # except for L2 prefetch hints of the program's first loads
+        for code in self._prefetch:
+            out.extend("  " + ln for ln in code.split("\n"))
         out.append("  tila::grid_dep_wait();")
         out.append("  tila::grid_dep_release();")
         if self.uses_tmem:

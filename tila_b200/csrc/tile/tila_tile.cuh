@@ -389,6 +389,13 @@ __device__ __forceinline__ bool mbar_try_wait(u64 *bar, u32 parity) {
 __device__ __forceinline__ void grid_dep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+// Hint: bring the 128-byte line holding `p` into L2.  Issued before
+// grid_dep_wait for a program's first loads, so their DRAM traffic overlaps
+// the previous grid; L2 is the point of coherence, so the loads after the
+// wait still observe everything the previous grid wrote.
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ void grid_dep_release() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
