@@ -495,18 +495,30 @@ W_ROOF = {"add": "hbm", "softmax": "hbm", "matmul": "tensor", "unfused_attention
           "fused_attention": "tensor", "fused_attention_causal": "tensor"}
 
 
+_COMM = {}
+
+
+def _communicator(world, rank, device):
+    """The C-ABI NCCL communicator (tila_mg_*) of this run, created once."""
+    from tila_b200.multigpu import Communicator
+    if "comm" not in _COMM:
+        _COMM["comm"] = Communicator(world, rank, device)
+    return _COMM["comm"]
+
+
 def _gather(out, case, world, rank, device):
-    """NCCL all-gather of the output rows each rank computed (timed on the
-    device, max over ranks)."""
+    """NCCL all-gather (through the library's C ABI) of the output rows each
+    rank computed, timed on the device, max over ranks."""
     import torch
     import torch.distributed as dist
     from tila_b200.multigpu import gather_leading
-    gather_leading(out, world, rank)        # first call sets up the communicator's buffers
+    comm = _communicator(world, rank, device)
+    gather_leading(out, world, rank, comm=comm)     # first call sets up NCCL's buffers
     dist.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    gather_leading(out, world, rank)
+    gather_leading(out, world, rank, comm=comm)
     e1.record()
     torch.cuda.synchronize(device)
     t = torch.tensor([e0.elapsed_time(e1)], device=device)
@@ -737,7 +749,11 @@ def main():
         line["workloads"] = {k: v for k, v in res.items() if k != keys[0]}
         print(json.dumps(line))
     if world > 1:
+        import torch
         import torch.distributed as dist
+        torch.cuda.synchronize()
+        if "comm" in _COMM:
+            _COMM.pop("comm").close()
         dist.destroy_process_group()
 
 

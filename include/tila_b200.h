@@ -139,6 +139,31 @@ int tila_device_info(int *sm_count, int *max_smem_optin, int *cc_major,
 
 const char *tila_status_string(int status);
 
+/* ---- multi-GPU: gather of output shards (one process per GPU) ----------------
+ * The reference has no multi-GPU path; these entry points implement the
+ * gather of the grid-partitioned launch (each rank runs a contiguous range of
+ * program_id values, then the ranks exchange the rows they wrote) over NCCL,
+ * which is opened at run time (libnccl.so.2, the copy PyTorch loaded when it is
+ * present).  Communicator handles are opaque; streams are CUstream handles. */
+#define TILA_MG_UNIQUE_ID_BYTES 128
+
+/* A fresh communicator id (rank 0 creates it and shares it with the others). */
+int tila_mg_unique_id(unsigned char id_out[TILA_MG_UNIQUE_ID_BYTES], char *log,
+                      size_t log_cap);
+
+/* Joins the communicator `id` as `rank` of `nranks` on the current device
+ * (collective: every rank calls it). */
+int tila_mg_comm_init(const unsigned char id[TILA_MG_UNIQUE_ID_BYTES], int nranks,
+                      int rank, void **comm_out, char *log, size_t log_cap);
+
+/* recvbuf[r * bytes_per_rank .. (r + 1) * bytes_per_rank) = rank r's sendbuf,
+ * for every rank r (an all-gather; every rank calls it, asynchronously on
+ * `stream`).  sendbuf may alias this rank's slot of recvbuf. */
+int tila_mg_gather(void *comm, const void *sendbuf, void *recvbuf, size_t bytes_per_rank,
+                   uint64_t stream, char *log, size_t log_cap);
+
+int tila_mg_comm_destroy(void *comm);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,3 +59,17 @@ def test_argument_validation():
     lib = native.library()
     assert lib.tila_launch(None, None, None, None, 0) == native.TILA_ERR_ARGUMENT
     assert lib.tila_library_load(None, 0, None, None, 0) == native.TILA_ERR_ARGUMENT
+
+
+def test_gather_entry_points_validate_arguments():
+    """The multi-GPU gather rejects bad arguments before touching NCCL."""
+    lib = native.library()
+    log = ctypes.create_string_buffer(256)
+    handle = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(native.MG_UNIQUE_ID_BYTES)
+    assert lib.tila_mg_comm_init(uid, 2, 5, ctypes.byref(handle), log, len(log)) == -6
+    assert lib.tila_mg_comm_init(uid, 0, 0, ctypes.byref(handle), log, len(log)) == -6
+    assert lib.tila_mg_gather(None, None, None, 16, 0, log, len(log)) == -6
+    assert lib.tila_mg_comm_destroy(None) == -6
+    with pytest.raises(ValueError):
+        native.mg_comm_init(b"short", 1, 0)

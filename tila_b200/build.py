@@ -28,7 +28,7 @@ def build_library(verbose=False) -> Path:
     """nvcc build of the C-ABI library: the launcher (host C++) and the
     no-allocation entry point (a .cu with a device array, sm_100a)."""
     out = PKG / "libtila_b200.so"
-    srcs = [PKG / "csrc" / "launcher.cpp", PKG / "csrc" / "noalloc.cu"]
+    srcs = [PKG / "csrc" / "launcher.cpp", PKG / "csrc" / "noalloc.cu", PKG / "csrc" / "mg.cpp"]
     hdr = ROOT / "include" / "tila_b200.h"
     if out.exists() and out.stat().st_mtime > max([p.stat().st_mtime for p in srcs] + [hdr.stat().st_mtime]):
         return out

@@ -36,12 +36,50 @@ def shard(axis: int, total: int, world: int, rank: int):
         yield lo, hi
 
 
-def gather_leading(out, world: int, rank: int, group=None):
+class Communicator:
+    """NCCL communicator of the ranks' GPUs behind the C ABI (``tila_mg_*``):
+    rank 0 creates the id, ``torch.distributed`` (any backend) carries it to
+    the other ranks, and every rank joins on its current device."""
+
+    def __init__(self, world: int, rank: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+        from . import native
+        box = [native.mg_unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(box, src=0, group=group)
+        with torch.cuda.device(device):
+            self.handle = native.mg_comm_init(box[0], world, rank)
+        self.world, self.rank, self.device = world, rank, device
+
+    def all_gather(self, send, recv):
+        """recv (world x send.numel() elements, contiguous) = every rank's send,
+        in rank order, on the current stream."""
+        import torch
+        from . import native
+        if not (send.is_contiguous() and recv.is_contiguous()):
+            raise ValueError("gather buffers must be contiguous")
+        nbytes = send.numel() * send.element_size()
+        if recv.numel() * recv.element_size() != nbytes * self.world:
+            raise ValueError("receive buffer must hold world x send bytes")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        native.mg_gather(self.handle, send.data_ptr(), recv.data_ptr(), nbytes, stream)
+
+    def close(self):
+        from . import native
+        if self.handle:
+            native.mg_comm_destroy(self.handle)
+            self.handle = None
+
+
+def gather_leading(out, world: int, rank: int, group=None, comm: Communicator = None):
     """All-gather the leading-dimension shards of ``out`` in place.
 
     Rank r owns rows ``shard_range(out.shape[0], world, r)`` of ``out``; after
     the call every rank holds the full tensor.  Shards may differ in size by
-    one row; they are padded to the largest shard for the collective.
+    one row; they are padded to the largest shard for the collective, which
+    runs through ``comm`` (the C-ABI NCCL communicator) when given, else
+    through ``torch.distributed``.
     """
     import torch
     import torch.distributed as dist
@@ -51,8 +89,13 @@ def gather_leading(out, world: int, rank: int, group=None):
     lo, hi = ranges[rank]
     send = torch.zeros((width,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
     send[: hi - lo] = out[lo:hi]
-    recv = [torch.empty_like(send) for _ in range(world)]
-    dist.all_gather(recv, send, group=group)
+    if comm is not None:
+        flat = torch.empty((world,) + tuple(send.shape), dtype=out.dtype, device=out.device)
+        comm.all_gather(send, flat)
+        recv = list(flat.unbind(0))
+    else:
+        recv = [torch.empty_like(send) for _ in range(world)]
+        dist.all_gather(recv, send, group=group)
     for r, (a, b) in enumerate(ranges):
         if r != rank:
             out[a:b] = recv[r][: b - a]

@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "tila_library_load", "tila_library_unload", "tila_kernel_get",
     "tila_kernel_attrs_get", "tila_launch", "tila_encode_tensor_map",
     "tila_device_info", "tila_status_string", "tila_launch_noalloc",
+    "tila_mg_unique_id", "tila_mg_comm_init", "tila_mg_gather", "tila_mg_comm_destroy",
 )
 
 #: Capacity of the static scratch behind tila_launch_noalloc (include/tila_b200.h).
@@ -122,6 +123,12 @@ def library() -> ctypes.CDLL:
                                             c_char_p, c_size_t]
         lib.tila_status_string.argtypes = [c_int]
         lib.tila_status_string.restype = c_char_p
+        lib.tila_mg_unique_id.argtypes = [c_void_p, c_char_p, c_size_t]
+        lib.tila_mg_comm_init.argtypes = [c_void_p, c_int, c_int, ctypes.POINTER(c_void_p),
+                                          c_char_p, c_size_t]
+        lib.tila_mg_gather.argtypes = [c_void_p, c_void_p, c_void_p, c_size_t, ctypes.c_uint64,
+                                       c_char_p, c_size_t]
+        lib.tila_mg_comm_destroy.argtypes = [c_void_p]
         _lib = lib
         return lib
 
@@ -322,3 +329,39 @@ def device_info() -> dict:
            "device info", log)
     return dict(zip(("sm_count", "max_smem_optin", "cc_major", "cc_minor"),
                     (v.value for v in vals)))
+
+
+# -- multi-GPU gather (tila_mg_*): NCCL behind the C ABI ----------------------
+
+MG_UNIQUE_ID_BYTES = 128
+
+
+def mg_unique_id() -> bytes:
+    """A fresh communicator id (created by rank 0, shared with the others)."""
+    buf = ctypes.create_string_buffer(MG_UNIQUE_ID_BYTES)
+    log = ctypes.create_string_buffer(1024)
+    _check(library().tila_mg_unique_id(buf, log, len(log)), "communicator id", log)
+    return buf.raw
+
+
+def mg_comm_init(uid: bytes, nranks: int, rank: int) -> int:
+    """Join communicator ``uid`` on the current device; returns the handle."""
+    if len(uid) != MG_UNIQUE_ID_BYTES:
+        raise ValueError("communicator id must have 128 bytes")
+    buf = ctypes.create_string_buffer(uid, MG_UNIQUE_ID_BYTES)
+    handle = ctypes.c_void_p()
+    log = ctypes.create_string_buffer(1024)
+    _check(library().tila_mg_comm_init(buf, nranks, rank, ctypes.byref(handle), log, len(log)),
+           "communicator init", log)
+    return handle.value
+
+
+def mg_gather(comm: int, send_ptr: int, recv_ptr: int, bytes_per_rank: int, stream: int) -> None:
+    """recv[r * bytes_per_rank:(r + 1) * bytes_per_rank] = rank r's send, for every rank."""
+    log = ctypes.create_string_buffer(1024)
+    _check(library().tila_mg_gather(ctypes.c_void_p(comm), ctypes.c_void_p(send_ptr), ctypes.c_void_p(recv_ptr),
+                                    bytes_per_rank, stream, log, len(log)), "gather", log)
+
+
+def mg_comm_destroy(comm: int) -> None:
+    _check(library().tila_mg_comm_destroy(ctypes.c_void_p(comm)), "communicator destroy")
