@@ -2282,8 +2282,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         # everything above touches only shared memory and kernel parameters;
         # global memory (and tensor memory) only after the previous grid ends,
         # except for L2 prefetch hints of the program's first loads
-        for code in self._prefetch:
-            out.extend("  " + ln for ln in code.split("\n"))
+        if self._prefetch:
+            # only programs that exist (two-program CTAs may hold one past the grid)
+            out.append("  if (tila_live) {" if wg else "  {")
+            for code in self._prefetch:
+                out.extend("    " + ln for ln in code.split("\n"))
+            out.append("  }")
         out.append("  tila::grid_dep_wait();")
         out.append("  tila::grid_dep_release();")
         if self.uses_tmem:
