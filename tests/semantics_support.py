@@ -262,3 +262,27 @@ def kernel(x: ti.Buffer[ti.f32, (N,), ti.ReadOnly],
     j = pid * {n_out} + ti.arange(0, {n_out})
     ti.store(out, j, u, mask=j < M)
 ''')
+
+
+def assume_gather_program(directory):
+    """The reference's gather (tests/test_bounds.py:144-163) with a second,
+    stricter assumption ``idx < limit`` that the caller can make false while
+    every index stays inside the buffer."""
+    return load_source(directory, "sem_assume_gather", '''import tila as ti
+N = ti.Dim("N")
+
+@ti.jit
+def kernel(idx_buf: ti.Buffer[ti.i32, (N,), ti.ReadOnly],
+           data: ti.Buffer[ti.f32, (N,), ti.ReadOnly],
+           out: ti.Buffer[ti.f32, (N,), ti.WriteOnly],
+           limit: ti.i32,
+           BLOCK: ti.Const[int, ti.PowerOfTwo] = 64):
+    pid = ti.program_id(0)
+    offs = pid * BLOCK + ti.arange(0, BLOCK)
+    m = offs < N
+    idx = ti.load(idx_buf, offs, mask=m, other=0)
+    ti.assume((idx >= 0) & (idx < N))
+    ti.assume(idx < limit)
+    v = ti.load(data, idx)
+    ti.store(out, offs, v, mask=m)
+''')

@@ -195,3 +195,18 @@ def test_rank3_tiles_compile(tmp_path):
             k = S.rank3_program(tmp_path, op, axis)
             spec = gen(k, dict(x=torch.zeros(1000), w=torch.zeros(384), out=torch.zeros(384)))
             native.compile_spec(spec)
+
+
+def test_assume_checks_only_in_debug_builds(tmp_path):
+    """ti.assume is free normally; with debug checks each false lane records
+    its line and the program stops before the access it guards."""
+    import semantics_support as S
+    k = S.assume_gather_program(tmp_path)
+    t = dict(idx_buf=torch.zeros(100, dtype=torch.int32), data=torch.zeros(100), out=torch.zeros(100))
+    facts = binding_facts(k.tk, t)
+    plain = KernelEmitter(k.tk, dict(BLOCK=64), facts, num_warps=4).generate()
+    debug = KernelEmitter(k.tk, dict(BLOCK=64), facts, num_warps=4, debug=True).generate()
+    assert "kErrAssumption" not in plain.source and not plain.assume_lines
+    assert "kErrAssumption" in debug.source and "goto tila_program_end" in debug.source
+    assert len(debug.assume_lines) == 2
+    native.compile_spec(debug)

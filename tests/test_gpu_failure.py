@@ -67,3 +67,28 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     W.vector_add[(4,)](torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev), o, BLOCK=1024)
     assert tila_b200.read_device_errors(dev) == 0
     np.testing.assert_array_equal(o.cpu().numpy(), x + y)
+
+
+def test_debug_assume_stops_the_program_and_raises(tmp_path, monkeypatch):
+    """TILA_DEBUG=1: a false ti.assume raises like the interpreter's
+    device_assert; the indices stay inside the buffer, so nothing unsafe runs."""
+    import semantics_support as S
+    monkeypatch.setenv("TILA_DEBUG", "1")
+    k = S.assume_gather_program(tmp_path)
+    n = 100
+    rng = np.random.default_rng(3)
+    idx = rng.integers(0, n, size=n).astype(np.int32)
+    data = rng.standard_normal(n).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    gi, gd = torch.from_numpy(idx).to(dev), torch.from_numpy(data).to(dev)
+    out = torch.zeros(n, device=dev)
+    k[(2,)](gi, gd, out, n)                      # every assumption holds
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), data[idx])
+    with pytest.raises(AssertionError, match="ti.assume"):
+        k[(2,)](gi, gd, out, 50)                 # idx < 50 is false for some lanes
+    assert tila_b200.read_device_errors(dev) == 0
+    out.zero_()
+    k[(2,)](gi, gd, out, n)                      # the next launch runs normally
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), data[idx])

@@ -320,6 +320,14 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
                 raise _failure(exc, "resources", entry.spec.source, context,
                                resource=("launch", entry.spec.smem_bytes, exc.log)) from exc
             raise _failure(exc, "launch", entry.spec.source, context) from exc
+        if entry.spec.assume_lines:
+            # debug build: a false ti.assume stopped its program and left its
+            # line in the error word (the interpreter asserts there too)
+            word = read_device_errors(device, reset=False)
+            if word >> 24 == 3:
+                read_device_errors(device)
+                raise AssertionError(f"device_assert failed: ti.assume at line {word & 0xFFFFFF} "
+                                     f"of {tk.name} (TILA_DEBUG=1)")
 
 
 def launch_flags() -> int:

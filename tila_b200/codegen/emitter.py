@@ -122,6 +122,8 @@ class KernelSpec:
     # are compared within a tolerance; kernels without a dot keep every f32
     # multiply and add separately rounded, like NumPy)
     fp_contract: bool = False
+    # Tila lines of the ti.assume checks compiled in (TILA_DEBUG=1 builds)
+    assume_lines: list = field(default_factory=list)
 
 
 # ---------------------------------------------------------------------------
@@ -210,6 +212,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._uneven_loops = 0       # hand-off loops with program-dependent trip counts
         self._loop_acc_cols = set()  # (column, N) of asynchronous-loop accumulators
         self._prefetch = []          # L2 prefetches of top-level loads (see _prefetch_load)
+        self._assume_lines = []      # debug checks of ti.assume (see s_TAssume)
+        self._assume_stop = False    # a failed check leaves the program (label at its end)
         self._scan_dots(tk.body)
 
     # -- small utilities ---------------------------------------------------
@@ -1858,7 +1862,33 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         self._defs[s.name] = s.value
 
     def s_TAssume(self, s):
-        return  # assumptions are proof facts; debug checks are not emitted
+        """ti.assume: a proof fact, free in normal builds.  With TILA_DEBUG=1
+        (lowering.py:339-342 emits tl.device_assert there) every thread
+        checks its lanes of the predicate; a false lane records the Tila line
+        in the launch's error word, and the whole program then stops before
+        the accesses the assumption was meant to justify (the host raises).
+        Inside a pipelined loop the check only records."""
+        if not self.debug:
+            return
+        v = self.value(s.pred)
+        line = int(getattr(s, "line", 0) or 0)
+        flag = self.fresh("af")
+        if v.kind == "scalar":
+            self.emit(f"const bool {flag} = !({v.expr});")
+        else:
+            if v.kind != "reg":
+                v = self.materialize(v)
+            lay = v.layout
+            valid = lay.valid_expr()
+            self.emit(f"bool {flag} = false;")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int r = 0; r < {lay.nreg}; ++r) "
+                      f"if ({'(' + valid + ') && ' if valid else ''}!({v.name}[r])) {flag} = true;")
+        self.emit(f"if ({flag}) tila::report_error(tila_err, tila::kErrAssumption, {line}u);")
+        if self.actx is None:
+            self.emit(f"if (__syncthreads_or({flag})) goto tila_program_end;")
+            self._assume_stop = True
+        self._assume_lines.append(line)
 
     def s_TAtomicStmt(self, s):
         self.e_TAtomicAdd(s.value)
@@ -2218,7 +2248,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         per_prog = -(-(scratch_off + self.smem.scratch) // 1024) * 1024
         # two programs of axis 0 per CTA, one per warpgroup (see _pingpong_ok)
         wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
-              and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3)
+              and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3
+              and not self._assume_lines)
         if wg:
             self.fuse = {0: 2}
         for ax in sorted(self.fuse or {}):
@@ -2339,6 +2370,8 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.extend(l for l in body if l.strip() not in (WG_ACQUIRE, WG_RELEASE)
                        and not l.strip().startswith((WG_TRIPS, WG_TURNS)))
         out.append("  } while (0);")
+        if self._assume_stop:
+            out.append("  tila_program_end: ;")
         if self.uses_tmem:
             out.append("  tila::tc_fence_before();")
             out.append("  __syncthreads();")
@@ -2353,6 +2386,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             smem = max(smem, floor_bytes)
         self.tmem_cols = cta_cols
         return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma or self._contracted,
+                          assume_lines=list(self._assume_lines),
                           tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
 

@@ -33,6 +33,7 @@ enum ErrorCode : u32 {
   kErrNone = 0,
   kErrMbarrierTimeout = 1,   // a bounded mbarrier wait gave up
   kErrTmemAlloc = 2,         // tensor memory allocation failed
+  kErrAssumption = 3,        // a ti.assume predicate was false (debug builds)
 };
 
 // Records the first error of a launch.  `err` points at a device word the
