@@ -380,3 +380,49 @@ def test_rank3_tiles_match_interpreter(tmp_path, op, axis):
         np.testing.assert_allclose(got, cpu, rtol=1e-6, atol=0)
     else:
         np.testing.assert_allclose(got, cpu, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f64"])
+@pytest.mark.parametrize("op", ["sum", "max"])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_reductions_narrow_and_wide_floats(dtype, op, axis):
+    """f16/bf16 sums accumulate in f32 and round once to the input type;
+    f64 stays f64; max is exact and propagates NaN (interp.py:324-333,
+    ADR-008)."""
+    kernel = S.reduce_program(KDIR, dtype, op, axis)
+    rng = np.random.default_rng(309)
+    m, n = 24, 50
+    x = rng.normal(size=(m, n)).astype(np.float32).astype(NP[dtype])
+    x[3, 7] = np.nan
+    x[11, :] = -0.0
+    out_shape = (m,) if axis == 1 else (m // 8, n)
+    cpu, gpu = both(kernel, (m // 8,), [x], [dtype], out_shape, dtype)
+    c, g = np.asarray(cpu, np.float64), np.asarray(gpu, np.float64)
+    assert np.array_equal(np.isnan(c), np.isnan(g)) and np.isnan(g).any()
+    if op == "max":
+        np.testing.assert_array_equal(g, c)
+    else:
+        # one rounding of the f32 (f64) sum: orders of summation may differ by
+        # an ulp of the accumulator, which the final rounding usually hides
+        ulp = {"f16": 2.0 ** -10, "bf16": 2.0 ** -7, "f64": 2.0 ** -50}[dtype]
+        np.testing.assert_allclose(g, c, rtol=2 * ulp, atol=2 * ulp, equal_nan=True)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f64"])
+@pytest.mark.parametrize("op", ["+", "-", "*", "/"])
+def test_float_binary_correctly_rounded(dtype, op):
+    """Narrow floats compute in f32 and round once; f32 carries more than
+    2p+2 bits for p = 11 and p = 8, so the result is the correctly rounded
+    narrow operation, bit for bit the interpreter's."""
+    kernel = S.binary_program(KDIR, dtype, op)
+    rng = np.random.default_rng(311)
+    n = 100
+    x = (rng.normal(size=n) * 8).astype(np.float32).astype(NP[dtype])
+    y = (rng.normal(size=n) * 8).astype(np.float32).astype(NP[dtype])
+    x[:6] = [0.0, -0.0, np.inf, -np.inf, np.nan, 1.0]
+    y[:6] = [0.0, 0.0, np.inf, 2.0, 1.0, -0.0]
+    cpu, gpu = both(kernel, (4,), [x, y], [dtype, dtype], (n,), dtype)
+    nan = np.isnan(np.asarray(cpu, np.float64))
+    assert np.array_equal(nan, np.isnan(np.asarray(gpu, np.float64)))
+    bits = {"f16": np.uint16, "bf16": np.uint16, "f64": np.uint64}[dtype]
+    np.testing.assert_array_equal(gpu[~nan].view(bits), cpu[~nan].view(bits))
