@@ -305,7 +305,7 @@ class Case:
         self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
         self.dtype = "f16 in, f32 accumulate"
         self.config = {"workload": "fused_attention", "batch": 4, "heads": 32, "seq": l,
-                       "head_dim": d, "BM": 128, "BN": 128, "causal": False}
+                       "head_dim": d, "BM": 128, "BN": 128, "causal": False, "num_warps": 4}
         self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
                                     lambda args, out: W.flash_attention[grid](*args, out, scale,
                                                                               BM=128, BN=128, BD=128))
@@ -322,8 +322,11 @@ class Case:
         grid = (l // 128, bh)
         self.axis, self.grid_axis_total = 1, bh
         scale = d ** -0.5
-        self.launches = [lambda s: W.flash_attention_causal[grid](s[0], s[1], s[2], s[3], scale,
-                                                                  BM=128, BN=128, BD=128)]
+        # 8 warps: one program per CTA, each row's 128 scores split over two
+        # thread halves; two such CTAs share an SM (faster here than pairing
+        # the programs of uneven trip counts in one CTA)
+        causal = W.flash_attention_causal[grid].with_options(num_warps=8)
+        self.launches = [lambda s: causal(s[0], s[1], s[2], s[3], scale, BM=128, BN=128, BD=128)]
         self.kernels = [W.flash_attention_causal]
         self.out_index = 3
         self.units_per_rank = W.causal_flops(bh1, l, d)
@@ -332,11 +335,11 @@ class Case:
         self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
         self.dtype = "f16 in, f32 accumulate"
         self.config = {"workload": "fused_attention_causal", "batch": 4, "heads": 32, "seq": l,
-                       "head_dim": d, "BM": 128, "BN": 128, "causal": True,
+                       "head_dim": d, "BM": 128, "BN": 128, "causal": True, "num_warps": 8,
                        "flop_count": "half of the non-causal 4*BH*L^2*D"}
         self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
-                                    lambda args, out: W.flash_attention_causal[grid](
-                                        *args, out, scale, BM=128, BN=128, BD=128))
+                                    lambda args, out: causal(*args, out, scale,
+                                                             BM=128, BN=128, BD=128))
 
     # -- launching ---------------------------------------------------------
 

@@ -32,6 +32,9 @@ def test_softmax_reductions():
     spec = gen(W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
     src = spec.source
     assert "tila::max_nan" in src and "expf" in src and "shfl_xor" in src
+    # the two cross-warp stages alternate between halves of their scratch:
+    # one barrier each (after the partials are written)
+    assert src.count("__syncthreads();") == 2 and src.count("tila_rsel ^= tila_red_half;") == 2
 
 
 def test_matmul_uses_tma_ring_and_tcgen05():

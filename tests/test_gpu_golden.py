@@ -44,14 +44,16 @@ def test_golden_on_b200(case):
         assert restate.rel_frobenius(got, want) <= 2e-3
 
 
+@pytest.mark.parametrize("warps", [4, 8])
 @pytest.mark.parametrize("l,d", [(128, 64), (300, 64), (384, 128)])
-def test_causal_flash_attention_128_tiles(l, d):
+def test_causal_flash_attention_128_tiles(l, d, warps):
     """The two-stage causal kernel (stage loops whose trip count depends on
-    program_id(0): one program per CTA) at 128x128 tiles."""
+    program_id(0): two programs per CTA with different trip counts) at
+    128x128 tiles."""
     q, k, v = W.attention_inputs(2, l, d, seed=17)
     o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    W.flash_attention_causal[(-(-l // 128), 2)](_cuda(q), _cuda(k), _cuda(v), o, d ** -0.5,
-                                                BM=128, BN=128, BD=d)
+    W.flash_attention_causal[(-(-l // 128), 2)].with_options(num_warps=warps)(
+        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, BM=128, BN=128, BD=d)
     torch.cuda.synchronize()
     assert tila_b200.read_device_errors() == 0
     ref = restate.attention_f64(q, k, v, causal=True)

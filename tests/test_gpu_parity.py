@@ -133,15 +133,17 @@ def test_fused_attention_128_tiles():
     assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
 
 
+@pytest.mark.parametrize("warps", [4, 8])
 @pytest.mark.parametrize("l,d", [(300, 64), (300, 128), (128, 128), (1000, 128)])
-def test_fused_attention_ragged_128_tiles(l, d):
-    """128x128 tiles (two programs per CTA, pipelined score MMAs) with a
+def test_fused_attention_ragged_128_tiles(l, d, warps):
+    """128x128 tiles (two programs per CTA, pipelined score MMAs; with 8
+    warps each program's rows are split into two column halves) with a
     partial last key block, a partial last query block, and odd numbers of
     query blocks (a CTA whose second program does not exist)."""
     q, k, v = W.attention_inputs(3, l, d, seed=13)
     o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    W.flash_attention[(ti.cdiv(l, 128), 3)](_cuda(q), _cuda(k), _cuda(v), o, d ** -0.5,
-                                            BM=128, BN=128, BD=d)
+    W.flash_attention[(ti.cdiv(l, 128), 3)].with_options(num_warps=warps)(
+        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, BM=128, BN=128, BD=d)
     _no_device_errors()
     assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
 

@@ -156,7 +156,8 @@ class _Smem:
 
     def __init__(self):
         self.top = 0
-        self.scratch = 0        # size of the shared redistribution/reduction scratch
+        self.scratch = 0        # size of the shared redistribution scratch
+        self.red = 0            # one half of the cross-warp reduction scratch
 
     def alloc(self, nbytes, align=16):
         self.top = (self.top + align - 1) // align * align
@@ -166,6 +167,9 @@ class _Smem:
 
     def need_scratch(self, nbytes):
         self.scratch = max(self.scratch, nbytes)
+
+    def need_red(self, nbytes):
+        self.red = max(self.red, (nbytes + 127) // 128 * 128)
 
 
 # ---------------------------------------------------------------------------
@@ -1002,16 +1006,16 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         if W == 1:
             return part
         esize = 8 if DT.size(dt) == 8 else 4
-        self.smem.need_scratch(W * esize)
+        self.smem.need_red(W * esize)
         buf = self.fresh("red")
         out = self.fresh("tot")
-        self.emit("__syncthreads();")
-        self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_scratch);")
+        self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_red + tila_rsel);")
         self.emit(f"if ((tid & 31) == 0) {buf}[tid >> 5] = {part};")
         self.emit("__syncthreads();")
         self.emit(f"{ct} {out} = {buf}[0];")
         self.emit("#pragma unroll")
         self.emit(f"for (int w = 1; w < {W}; ++w) {out} = {fold(out, f'{buf}[w]')};")
+        self.emit("tila_rsel ^= tila_red_half;")
         return out
 
     def _axis_reduce(self, v: Val, op, axis, acc_dt, out_dt) -> Val:
@@ -1064,14 +1068,14 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.emit("#pragma unroll")
             self.emit(f"for (int k = 0; k < {n}; ++k) {name}[k] = {fold(f'{name}[k]', f'tila::shfl_xor({name}[k], {1 << b})')};")
         if warp_bits:
-            # shared-memory stage across warps: slot [output][group]
+            # shared-memory stage across warps: slot [group][output], so the
+            # lanes of a warp (consecutive outputs) touch consecutive words
             G = 1 << len(warp_bits)
             numel_out = int(np.prod(keep_shape))
             esize = 8 if DT.size(acc_dt) == 8 else 4
-            self.smem.need_scratch(numel_out * G * esize)
+            self.smem.need_red(numel_out * G * esize)
             buf = self.fresh("rs")
-            self.emit("__syncthreads();")
-            self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_scratch);")
+            self.emit(f"{ct}* {buf} = reinterpret_cast<{ct}*>(tila_red + tila_rsel);")
             gexpr = " | ".join(f"(((tid >> {b}) & 1) << {i})" for i, b in enumerate(warp_bits))
             lane_mask = sum(1 << b for b in lane_bits)
             out_lay = Derived(lay, ("slice", axis), keep_shape, regs)
@@ -1083,16 +1087,17 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 flat = " + ".join(f"({c}) * {int(np.prod(keep_shape[i + 1:]))}" for i, c in enumerate(crd)) or "0"
                 conds = ([f"(tid & {lane_mask}) == 0"] if lane_mask else []) + ([f"({lvalid})"] if lvalid else [])
                 cond = f"if ({' && '.join(conds)}) " if conds else ""
-                self.emit(f"{cond}{buf}[({flat}) * {G} + {buf}_g] = {name}[{k}];")
+                self.emit(f"{cond}{buf}[{buf}_g * {numel_out} + ({flat})] = {name}[{k}];")
             self.emit("__syncthreads();")
             for k in range(n):
                 crd = out_lay.coord(k)
                 flat = " + ".join(f"({c}) * {int(np.prod(keep_shape[i + 1:]))}" for i, c in enumerate(crd)) or "0"
-                acc = f"{buf}[({flat}) * {G}]"
+                acc = f"{buf}[({flat})]"
                 for gi in range(1, G):
-                    acc = fold(acc, f"{buf}[({flat}) * {G} + {gi}]")
+                    acc = fold(acc, f"{buf}[{gi * numel_out} + ({flat})]")
                 pre = f"if ({lvalid}) " if lvalid else ""
                 self.emit(f"{pre}{name}[{k}] = {acc};")
+            self.emit("tila_rsel ^= tila_red_half;")
         out_lay = Derived(lay, ("slice", axis), keep_shape, regs, owner_fn=dedupe_owner)
         res = Val("reg", acc_dt, keep_shape, name=name, layout=out_lay)
         if acc_dt.name != out_dt.name:
@@ -2106,11 +2111,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     def _snapshot(self):
         return (list(self.lines), dict(self.env), self.counter, self.smem.top, self.smem.scratch,
                 self.tmem_cols, dict(self.conv_cache), dict(self._defs), set(self._pidnames),
-                dict(self._loopvars), self.uses_tmem, self.uses_mma, self.indent)
+                dict(self._loopvars), self.uses_tmem, self.uses_mma, self.indent, self.smem.red)
 
     def _restore(self, snap):
         (self.lines, self.env, _, self.smem.top, self.smem.scratch, self.tmem_cols, self.conv_cache,
-         self._defs, self._pidnames, self._loopvars, self.uses_tmem, self.uses_mma, self.indent) = snap
+         self._defs, self._pidnames, self._loopvars, self.uses_tmem, self.uses_mma, self.indent,
+         self.smem.red) = snap
         # keep the counter monotonic so names never collide
 
     def _carried_val(self, pre, end, name, dry=False):
@@ -2245,7 +2251,12 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             if total_cols > 512:
                 self.fail(f"kernel needs {total_cols} tensor-memory columns (limit 512)")
             self.tmem_cols = _pow2_at_least(max(32, total_cols))
-        per_prog = -(-(scratch_off + self.smem.scratch) // 1024) * 1024
+        # cross-warp reductions alternate between two halves of their own
+        # region (tila_rsel): the barrier after a reduction's writes also
+        # orders the previous reduction's reads before the next writes there
+        red_off = scratch_off + (self.smem.scratch + 127) // 128 * 128
+        prog_bytes = red_off + 2 * self.smem.red
+        per_prog = -(-prog_bytes // 1024) * 1024
         # two programs of axis 0 per CTA, one per warpgroup (see _pingpong_ok)
         wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
               and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3
@@ -2298,6 +2309,10 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         out.append(f"  volatile int& tila_dead = *reinterpret_cast<volatile int*>(tila_smem + 12);")
         out.append(f"  unsigned char* tila_scratch = tila_smem + {scratch_off};")
         out.append("  (void)tila_scratch; (void)tila_mma_bar; (void)tila_tmem_slot;")
+        if self.smem.red:
+            out.append(f"  unsigned char* const tila_red = tila_smem + {red_off};")
+            out.append(f"  constexpr tila::u32 tila_red_half = {self.smem.red};")
+            out.append("  tila::u32 tila_rsel = 0;")
         out.append("  tila::u32 tila_mma_phase = 0; (void)tila_mma_phase;")
         for v in self._phase_vars:
             out.append(f"  tila::u32 {v} = 0;")
@@ -2378,7 +2393,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             out.append(f"  if (threadIdx.x < 32) tila::tmem_dealloc(tila_tmem, {cta_cols});")
         out.append("}")
         src = "\n".join(out) + "\n"
-        smem = 2 * per_prog + 64 if wg else scratch_off + self.smem.scratch
+        smem = 2 * per_prog + 64 if wg else prog_bytes
         if self.uses_tmem:
             # keep (resident CTAs) x (TMEM columns) within the SM's 512 columns
             max_ctas = max(1, 512 // cta_cols)
