@@ -1103,6 +1103,35 @@ class AsyncLoopMixin:
         self.wait_all_accs(release=True)
         chunk = 32 if lay.cpg % 32 == 0 else 8
         base = f"tila_tmem + {a['col']}" + (f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else "") + " + ((tid & 96u) << 16)"
+        if chunk == 32 and lay.cpg >= 64 and getattr(mk, "fn", None):
+            # software-pipelined: the next chunk's load is in flight while this
+            # chunk is scaled and stored; one wait for the stores at the end
+            nch = lay.cpg // 32
+            xt, xo = ("tila::pk2(t_[c & 1][j], t_[c & 1][j + 1])", "tila::pk2(o_, o_)")
+            args = f"{xt}, {xo}" if acc_left else f"{xo}, {xt}"
+            self.emit("{ // in-place TMEM update of " + name + " (loads one chunk ahead)")
+            self.indent += 1
+            self.emit(f"const float o_ = {oexpr};")
+            self.emit("float t_[2][32];")
+            self.emit(f"tila::tmem_ld32({base}, t_[0]);")
+            self.emit("tila::tmem_wait_ld();")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int c = 0; c < {nch}; ++c) {{")
+            self.indent += 1
+            self.emit(f"if (c + 1 < {nch}) tila::tmem_ld32({base} + (c + 1) * 32, t_[(c + 1) & 1]);")
+            self.emit("#pragma unroll")
+            self.emit(f"for (int j = 0; j < 32; j += 2) {{ const tila::u64 q_ = tila::{mk.fn}({args}); "
+                      f"t_[c & 1][j] = tila::lo2(q_); t_[c & 1][j + 1] = tila::hi2(q_); }}")
+            self.emit(f"tila::tmem_st32({base} + c * 32, t_[c & 1]);")
+            self.emit(f"if (c + 1 < {nch}) tila::tmem_wait_ld();")
+            self.indent -= 1
+            self.emit("}")
+            self.emit("tila::tmem_wait_st();")
+            self.indent -= 1
+            self.emit("}")
+            from .emitter import Val
+            self.env[name] = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
+            return True
         self.emit("{ // in-place TMEM update of " + name)
         self.indent += 1
         self.emit(f"const float o_ = {oexpr};")
