@@ -812,7 +812,9 @@ class AsyncLoopMixin:
         self.emit("#pragma unroll")
         self.emit(f"for (int c = 0; c < {half}; ++c) pk[c] = __uint_as_float(tila::pack_f16x2({pv.name}[2 * c], {pv.name}[2 * c + 1]));")
         goff = f" + (tid >> 7) * {play.cpg // 2}" if play.groups > 1 else ""
-        self.emit(f"tila::tmem_store_row<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
+        # no store wait here: the P@V issue below waits once for every TMEM
+        # store of the iteration (P and the accumulator rescale)
+        self.emit(f"tila::tmem_store_row_async<{half}>(tila_tmem + {ctx.p_col}{goff} + ((tid & 96u) << 16), pk);")
         self.indent -= 1
         self.emit("}")
 
@@ -1008,6 +1010,8 @@ class AsyncLoopMixin:
         self.emit_smem_wait(bv)
         if not ts:
             self.emit_smem_wait(av)
+        else:
+            self.emit("tila::tmem_wait_st();")
         self.emit("tila::fence_proxy_async_smem();")
         self.emit("tila::tc_fence_before();")
         self.emit("__syncthreads();")

@@ -658,6 +658,17 @@ __device__ __forceinline__ void tmem_store_row(u32 taddr, const float *v) {
   for (; c < N; c += 8) tmem_st8(taddr + c, v + c);
   tmem_wait_st();
 }
+// The same stores without the wait: the caller issues tmem_wait_st() before
+// anything reads these columns (an MMA operand read included).
+template <int N>
+__device__ __forceinline__ void tmem_store_row_async(u32 taddr, const float *v) {
+  static_assert(N % 8 == 0, "TMEM row stores move multiples of 8 columns");
+  int c = 0;
+#pragma unroll
+  for (; c + 32 <= N; c += 32) tmem_st32(taddr + c, v + c);
+#pragma unroll
+  for (; c < N; c += 8) tmem_st8(taddr + c, v + c);
+}
 
 // ---------------------------------------------------------------------------
 // operand staging layouts for register-sourced MMA operands
