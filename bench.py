@@ -173,8 +173,8 @@ class Case:
         self.sets = [(self._dev(x), self._dev(y), torch.empty(n, device=self.device)) for _ in range(nset)]
         grid = (n // 1024,)
         self.axis, self.grid_axis_total = 0, grid[0]
-        self.launches = [lambda s: W.vector_add[grid](s[0], s[1], s[2], BLOCK=1024)]
-        self.kernels = [W.vector_add]
+        self.launches = [lambda s: W.add_kernel[grid](s[0], s[1], s[2], BLOCK=1024)]
+        self.kernels = [W.add_kernel]
         self.out_index = 2
         self.units_per_rank = W.add_bytes(n1)
         self.dominant = 0
@@ -183,7 +183,7 @@ class Case:
         self.dtype = "f32"
         self.config = {"workload": "add", "N": n1, "BLOCK": 1024, "dtype": "f32"}
         self.e2e_call = lambda xs: (grid, [xs[0], xs[1]], lambda: torch.empty(n, device=self.device),
-                                    lambda args, out: W.vector_add[grid](args[0], args[1], out, BLOCK=1024))
+                                    lambda args, out: W.add_kernel[grid](args[0], args[1], out, BLOCK=1024))
 
     # -- softmax --
     def _setup_softmax(self):
@@ -196,8 +196,8 @@ class Case:
         self.sets = [(self._dev(x), torch.empty((m, ncol), device=self.device)) for _ in range(nset)]
         grid = (m,)
         self.axis, self.grid_axis_total = 0, m
-        self.launches = [lambda s: W.row_softmax[grid](s[0], s[1], BN=1024)]
-        self.kernels = [W.row_softmax]
+        self.launches = [lambda s: W.softmax_kernel[grid](s[0], s[1], BN=1024)]
+        self.kernels = [W.softmax_kernel]
         self.out_index = 1
         self.units_per_rank = W.softmax_bytes(m1, ncol)
         self.dominant = 0
@@ -206,7 +206,7 @@ class Case:
         self.dtype = "f32"
         self.config = {"workload": "softmax", "M": m1, "N": ncol, "BN": 1024, "dtype": "f32"}
         self.e2e_call = lambda xs: (grid, [xs[0]], lambda: torch.empty((m, ncol), device=self.device),
-                                    lambda args, out: W.row_softmax[grid](args[0], out, BN=1024))
+                                    lambda args, out: W.softmax_kernel[grid](args[0], out, BN=1024))
 
     # -- matmul --
     def _setup_matmul(self):
@@ -220,8 +220,8 @@ class Case:
                      for _ in range(nset)]
         grid = (m // 128, 4096 // 128)
         self.axis, self.grid_axis_total = 0, grid[0]
-        self.launches = [lambda s: W.tiled_matmul[grid](s[0], s[1], s[2], BM=128, BN=128, BK=64)]
-        self.kernels = [W.tiled_matmul]
+        self.launches = [lambda s: W.matmul_kernel[grid](s[0], s[1], s[2], BM=128, BN=128, BK=64)]
+        self.kernels = [W.matmul_kernel]
         self.out_index = 2
         self.units_per_rank = W.matmul_flops()
         self.dominant = 0
@@ -232,7 +232,7 @@ class Case:
                        "BN": 128, "BK": 64}
         self.e2e_call = lambda xs: (grid, [xs[0], xs[1]],
                                     lambda: torch.empty((m, 4096), device=self.device),
-                                    lambda args, out: W.tiled_matmul[grid](args[0], args[1], out,
+                                    lambda args, out: W.matmul_kernel[grid](args[0], args[1], out,
                                                                            BM=128, BN=128, BK=64))
 
     # -- unfused attention --
@@ -252,10 +252,10 @@ class Case:
         self.multi_shard = [(2, bh), (0, bh * l), (1, bh)]
         self.launches = [
             lambda st: W.attention_scores[g1](st[0], st[1], st[3], 0.125, BM=128, BN=128, BD=64),
-            lambda st: W.row_softmax[g2](st[3].view(bh * l, l), st[4].view(bh * l, l), BN=1024),
+            lambda st: W.softmax_kernel[g2](st[3].view(bh * l, l), st[4].view(bh * l, l), BN=1024),
             lambda st: W.attention_pv[g3](st[4], st[2], st[5], BM=128, BN=128, BD=64),
         ]
-        self.kernels = [W.attention_scores, W.row_softmax, W.attention_pv]
+        self.kernels = [W.attention_scores, W.softmax_kernel, W.attention_pv]
         self.out_index = 5
         self.units_per_rank = W.unfused_flops(bh1, l, d)
         self.bytes_per_rank = W.unfused_bytes(bh1, l, d)
@@ -275,7 +275,7 @@ class Case:
             s_ = torch.empty((bh, l, l), device=self.device)
             p_ = torch.empty_like(s_)
             steps = [lambda: W.attention_scores[g1](args[0], args[1], s_, 0.125, BM=128, BN=128, BD=64),
-                     lambda: W.row_softmax[g2](s_.view(bh * l, l), p_.view(bh * l, l), BN=1024),
+                     lambda: W.softmax_kernel[g2](s_.view(bh * l, l), p_.view(bh * l, l), BN=1024),
                      lambda: W.attention_pv[g3](p_, args[2], out, BM=128, BN=128, BD=64)]
             for (ax, lo, hi), fn in zip(self._ranges(), steps):
                 with self.tila_b200.program_range(ax, lo, hi):
@@ -295,9 +295,9 @@ class Case:
         grid = (l // 128, bh)
         self.axis, self.grid_axis_total = 1, bh
         scale = d ** -0.5
-        self.launches = [lambda s: W.flash_attention[grid](s[0], s[1], s[2], s[3], scale,
-                                                           BM=128, BN=128, BD=128)]
-        self.kernels = [W.flash_attention]
+        self.launches = [lambda s: W.fused_attention_kernel[grid](s[0], s[1], s[2], s[3], scale,
+                                                           CAUSAL=0, BM=128, BN=128, BD=128)]
+        self.kernels = [W.fused_attention_kernel]
         self.out_index = 3
         self.units_per_rank = W.fused_flops(bh1, l, d)
         self.dominant = 0
@@ -307,8 +307,8 @@ class Case:
         self.config = {"workload": "fused_attention", "batch": 4, "heads": 32, "seq": l,
                        "head_dim": d, "BM": 128, "BN": 128, "causal": False, "num_warps": 4}
         self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
-                                    lambda args, out: W.flash_attention[grid](*args, out, scale,
-                                                                              BM=128, BN=128, BD=128))
+                                    lambda args, out: W.fused_attention_kernel[grid](*args, out, scale,
+                                                                              CAUSAL=0, BM=128, BN=128, BD=128))
 
     # -- causal fused attention (the CAUSAL=1 kernel of the same example) --
     def _setup_fused_attention_causal(self):
@@ -325,9 +325,9 @@ class Case:
         # 8 warps: one program per CTA, each row's 128 scores split over two
         # thread halves; two such CTAs share an SM (faster here than pairing
         # the programs of uneven trip counts in one CTA)
-        causal = W.flash_attention_causal[grid].with_options(num_warps=8)
-        self.launches = [lambda s: causal(s[0], s[1], s[2], s[3], scale, BM=128, BN=128, BD=128)]
-        self.kernels = [W.flash_attention_causal]
+        causal = W.fused_attention_kernel[grid].with_options(num_warps=8)
+        self.launches = [lambda s: causal(s[0], s[1], s[2], s[3], scale, CAUSAL=1, BM=128, BN=128, BD=128)]
+        self.kernels = [W.fused_attention_kernel]
         self.out_index = 3
         self.units_per_rank = W.causal_flops(bh1, l, d)
         self.dominant = 0
@@ -338,7 +338,7 @@ class Case:
                        "head_dim": d, "BM": 128, "BN": 128, "causal": True, "num_warps": 8,
                        "flop_count": "half of the non-causal 4*BH*L^2*D"}
         self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
-                                    lambda args, out: causal(*args, out, scale,
+                                    lambda args, out: causal(*args, out, scale, CAUSAL=1,
                                                              BM=128, BN=128, BD=128))
 
     # -- launching ---------------------------------------------------------
@@ -624,19 +624,19 @@ def cpu_baseline(key, repeats=1):
         n = 1 << 20
         x, y = W.add_inputs(n)
         out = np.zeros_like(x)
-        fn = lambda: W.vector_add[(n // 1024,)](x, y, out, BLOCK=1024)
+        fn = lambda: W.add_kernel[(n // 1024,)](x, y, out, BLOCK=1024)
         units, unit, scale, sample, cores = W.add_bytes(n), "GB/s", 1e9, "full workload (N=1048576)", 1
     elif key == "softmax":
         m = 1024
         x = W.softmax_inputs(m, 1000)
         o = np.zeros_like(x)
-        fn = lambda: W.row_softmax[(m,)](x, o, BN=1024)
+        fn = lambda: W.softmax_kernel[(m,)](x, o, BN=1024)
         units, unit, scale, sample, cores = W.softmax_bytes(m, 1000), "GB/s", 1e9, \
             "1024 of the 8192 rows (1000 columns, BN=1024)", 1
     elif key == "matmul":
         a, b = W.matmul_inputs(128, 512, 4096)
         c = np.zeros((128, 512), np.float32)
-        fn = lambda: W.tiled_matmul[(1, 4)](a, b, c, BM=128, BN=128, BK=64)
+        fn = lambda: W.matmul_kernel[(1, 4)](a, b, c, BM=128, BN=128, BK=64)
         units, unit, scale = W.matmul_flops(128, 512, 4096), "TFLOP/s", 1e12
         sample, cores = "4 of the 1024 output tiles (128x512 of C, full K=4096)", _blas_threads()
     elif key == "unfused_attention":
@@ -647,20 +647,20 @@ def cpu_baseline(key, repeats=1):
 
         def fn():
             W.attention_scores[(8, 8, 1)](q, k, s, 0.125, BM=128, BN=128, BD=64)
-            W.row_softmax[(1024,)](s.reshape(1024, 1024), p.reshape(1024, 1024), BN=1024)
+            W.softmax_kernel[(1024,)](s.reshape(1024, 1024), p.reshape(1024, 1024), BN=1024)
             W.attention_pv[(8, 1)](p, v, o, BM=128, BN=128, BD=64)
         units, unit, scale = W.unfused_flops(1, 1024, 64), "TFLOP/s", 1e12
         sample, cores = "1 of the 128 batch*heads (L=1024, D=64)", _blas_threads()
     elif key == "fused_attention_causal":
         q, k, v = W.attention_inputs(1, 4096, 128)
         o = np.zeros((1, 4096, 128), np.float32)
-        fn = lambda: W.flash_attention_causal[(32, 1)](q, k, v, o, 128 ** -0.5, BM=128, BN=128, BD=128)
+        fn = lambda: W.fused_attention_kernel[(32, 1)](q, k, v, o, 128 ** -0.5, CAUSAL=1, BM=128, BN=128, BD=128)
         units, unit, scale = W.causal_flops(1, 4096, 128), "TFLOP/s", 1e12
         sample, cores = "1 of the 128 batch*heads (L=4096, D=128, causal)", _blas_threads()
     else:
         q, k, v = W.attention_inputs(1, 4096, 128)
         o = np.zeros((1, 4096, 128), np.float32)
-        fn = lambda: W.flash_attention[(32, 1)](q, k, v, o, 128 ** -0.5, BM=128, BN=128, BD=128)
+        fn = lambda: W.fused_attention_kernel[(32, 1)](q, k, v, o, 128 ** -0.5, CAUSAL=0, BM=128, BN=128, BD=128)
         units, unit, scale = W.fused_flops(1, 4096, 128), "TFLOP/s", 1e12
         sample, cores = "1 of the 128 batch*heads (L=4096, D=128)", _blas_threads()
     fn()                      # warm (decoration caches, first-call imports)

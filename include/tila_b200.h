@@ -119,19 +119,52 @@ int tila_encode_tensor_map(void *tensor_map_out, int dtype, int rank,
 #define TILA_NOALLOC_SCRATCH_BYTES 256
 
 /* No counterpart in the reference (its launches allocate through PyTorch).
- * Same as tila_launch for callers that cannot allocate device memory - code
- * recording a CUDA graph, hosts whose own pool owns all device memory, loops
- * that cannot afford cudaMalloc's synchronisation.  args[scratch_arg] (the
- * kernel's scratch pointer, normally the error word) is replaced by the
- * address of a file-scope device array of TILA_NOALLOC_SCRATCH_BYTES bytes;
- * larger scratch_bytes are rejected with TILA_ERR_ARGUMENT.  The first call
- * on a device looks up that address (issue it before any stream capture).
- * The array is shared by every call and keeps the previous contents: the
- * first scratch_bytes are cleared on cfg->stream before the launch, and calls
- * that overlap on the GPU race on it.  Allocates nothing. */
+ * Same as tila_launch, for callers that cannot allocate device memory: hosts
+ * whose own pool owns every byte of device memory and forbid the CUDA
+ * allocator, and latency-critical loops that cannot afford cudaMalloc's
+ * implicit device synchronisation.  args[scratch_arg] (the kernel's scratch
+ * pointer: its error block, TILA_ERROR_BLOCK_BYTES) is replaced by the address
+ * of a file-scope device array of TILA_NOALLOC_SCRATCH_BYTES bytes, which
+ * every GPU that loads this library holds until the process exits; larger
+ * scratch_bytes are rejected with TILA_ERR_ARGUMENT.  The first call on a
+ * device (and in a new CUDA context) looks up that array's address with the
+ * device current, so issue it before any stream capture.  The array is shared
+ * by every call and keeps the previous call's contents: its first
+ * scratch_bytes are cleared on cfg->stream before the launch, and calls that
+ * overlap on the GPU race on it.  Allocates nothing. */
 int tila_launch_noalloc(void *kernel, const tila_launch_config *cfg, void **args,
                         int scratch_arg, uint32_t scratch_bytes, char *log,
                         size_t log_cap);
+
+/* No counterpart in the reference.  Reads the error word that the last
+ * tila_launch_noalloc launch on the current device recorded in the static
+ * scratch ((code << 24) | Tila source line, 0 = none; codes as for the error
+ * block below) into *word_out: a 4-byte copy on `stream` after the work
+ * already queued there, then a synchronisation of `stream`.  reset != 0
+ * clears the word after the copy.  Allocates nothing. */
+int tila_noalloc_read_error(uint32_t *word_out, uint64_t stream, int reset,
+                            char *log, size_t log_cap);
+
+/* Error block of a launch.  Every generated kernel takes one pointer to a
+ * 16-byte device block (the "err" parameter): bytes 0-3 hold the first device
+ * error of the launch ((code << 24) | Tila source line; codes: 1 a bounded
+ * mbarrier wait timed out, 2 tensor memory allocation failed, 3 a ti.assume
+ * was false in a TILA_DEBUG=1 build), bytes 8-15 the device address of a
+ * notification word (0 = none).  The thread that records the first error also
+ * stores it into the notification word, so a host holding that word in
+ * page-locked memory sees device errors without synchronising.  The reference
+ * reports device-side failures through Triton's device_assert
+ * (lowering.py:339-342); this block is its counterpart. */
+#define TILA_ERROR_BLOCK_BYTES 16
+
+/* A zeroed 64-byte page-locked host buffer that kernels can write through
+ * *device_address_out (CU_MEMHOSTALLOC_DEVICEMAP | PORTABLE), for the
+ * notification word of an error block.  Needs a current context. */
+int tila_host_word_alloc(uint32_t **host_out, uint64_t *device_address_out,
+                         char *log, size_t log_cap);
+
+/* Frees a buffer from tila_host_word_alloc (no kernel may still write it). */
+int tila_host_word_free(uint32_t *host);
 
 /* Number of SMs and opt-in shared memory per block of the current device. */
 int tila_device_info(int *sm_count, int *max_smem_optin, int *cc_major,

@@ -9,7 +9,7 @@ outputs as ``tests/golden/<case>.npz``.  The tests read only those files.
 
 Usage (in a container that has the reference source tree):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <Tila checkout>
 """
 
 from __future__ import annotations
@@ -89,7 +89,7 @@ def cases():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="a Tila source checkout (with src/ and examples/)")
     args = ap.parse_args(argv)
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "src"))

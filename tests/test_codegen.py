@@ -21,7 +21,7 @@ def gen(jf, tensors, warps=4, **consts):
 
 @pytest.mark.parametrize("warps", [4, 8])
 def test_add_vectorised(warps):
-    spec = gen(W.vector_add, dict(x=torch.zeros(4096), y=torch.zeros(4096), out=torch.zeros(4096)),
+    spec = gen(W.add_kernel, dict(x=torch.zeros(4096), y=torch.zeros(4096), out=torch.zeros(4096)),
                warps, BLOCK=1024)
     assert "uint4" in spec.source and "tcgen05" not in spec.source
     # small reduction-free programs run with 2 warps under the default num_warps
@@ -29,7 +29,7 @@ def test_add_vectorised(warps):
 
 
 def test_softmax_reductions():
-    spec = gen(W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
+    spec = gen(W.softmax_kernel, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
     src = spec.source
     assert "tila::max_nan" in src and "expf" in src and "shfl_xor" in src
     # the two cross-warp stages alternate between halves of their scratch:
@@ -39,7 +39,7 @@ def test_softmax_reductions():
 
 def test_matmul_uses_tma_ring_and_tcgen05():
     t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
-    spec = gen(W.tiled_matmul, t, BM=128, BN=128, BK=64)
+    spec = gen(W.matmul_kernel, t, BM=128, BN=128, BK=64)
     # a 2 x 2 block of programs per CTA sharing A and B tiles, N = 256 MMAs
     assert "2x2 programs per CTA" in spec.source and spec.fuse == {0: 2, 1: 2}
     assert "tma_load_2d" in spec.source and "idesc_f16_f32(128, 256" in spec.source
@@ -50,13 +50,13 @@ def test_matmul_uses_tma_ring_and_tcgen05():
 def test_matmul_strided_falls_back_to_register_staging():
     a = torch.zeros(256, 256, dtype=f16).t()
     t = dict(a=a, b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
-    spec = gen(W.tiled_matmul, t, BM=128, BN=128, BK=64)
+    spec = gen(W.matmul_kernel, t, BM=128, BN=128, BK=64)
     assert "kmajor_offset" in spec.source          # operand A staged from registers
 
 
 def test_small_tiles_compile():
     t = dict(a=torch.zeros(19, 35, dtype=f16), b=torch.zeros(35, 23, dtype=f16), c=torch.zeros(19, 23))
-    gen(W.tiled_matmul, t, BM=16, BN=16, BK=32)
+    gen(W.matmul_kernel, t, BM=16, BN=16, BK=32)
 
 
 def test_attention_kernels_compile():
@@ -66,14 +66,39 @@ def test_attention_kernels_compile():
     gen(W.attention_pv, dict(p=torch.zeros(2, 256, 256), v=q.clone(), o=torch.zeros(2, 256, 64)),
         BM=128, BN=128, BD=64)
     q = torch.zeros(2, 256, 128, dtype=f16)
-    gen(W.flash_attention, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
-        BM=128, BN=128, BD=128)
+    gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
+        CAUSAL=0, BM=128, BN=128, BD=128)
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_reference_fused_attention_takes_two_program_plan(causal):
+    """examples/fused_attention.py puts each of its loops inside ``if CAUSAL
+    == 1: ... else:``; the static if is resolved per specialisation before
+    the loop matchers run, so at 128x128 tiles the loop of the taken branch
+    gets the two-programs-per-CTA plan (256 threads, one 128-row program per
+    warpgroup)."""
+    q = torch.zeros(2, 512, 128, dtype=f16)
+    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+               CAUSAL=causal, BM=128, BN=128, BD=128)
+    assert spec.fuse == {0: 2} and spec.threads == 256 and spec.tmem_cols == 512
+
+
+def test_static_if_resolution_leaves_kernel_untouched():
+    from tila_b200.codegen.emitter import resolve_static_ifs
+    tk = W.fused_attention_kernel.tk
+    before = [type(s).__name__ for s in tk.body]
+    assert "TStaticIf" in before
+    for causal, loops in ((0, 1), (1, 2)):
+        flat = resolve_static_ifs(tk, dict(CAUSAL=causal, BM=128, BN=128, BD=128))
+        kinds = [type(s).__name__ for s in flat.body]
+        assert "TStaticIf" not in kinds and kinds.count("TFor") == loops
+    assert [type(s).__name__ for s in tk.body] == before
 
 
 def test_tmem_budget_and_occupancy():
     q = torch.zeros(2, 256, 128, dtype=f16)
-    spec = gen(W.flash_attention, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
-               BM=128, BN=128, BD=128)
+    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 256, 128)),
+               CAUSAL=0, BM=128, BN=128, BD=128)
     cols = spec.tmem_cols
     assert cols in (32, 64, 128, 256, 512)
     resident = 233472 // (spec.smem_bytes + 1024)
@@ -132,7 +157,7 @@ def test_uniform_divisor_takes_reciprocal_path(tmp_path):
     parameter) goes through the shared-reciprocal path (tila::udiv_*);
     element-wise division by a tile keeps IEEE division."""
     import semantics_support as S
-    spec = gen(W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
+    spec = gen(W.softmax_kernel, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), BN=1024)
     assert "tila::udiv_q2(" in spec.source and "tila::udiv_track(" in spec.source
     for kind in ("scalar", "reduced"):
         k = S.uniform_div_program(tmp_path, kind)
@@ -153,10 +178,10 @@ def test_f32_tile_epilogues_store_through_tma():
     src = gen(W.attention_scores, t, BM=128, BN=128, BD=64).source
     assert "tila::tma_store_3d(" in src and "bulk_wait_read" in src
     t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
-    assert "tila::tma_store_2d(" in gen(W.tiled_matmul, t, BM=128, BN=128, BK=64).source
+    assert "tila::tma_store_2d(" in gen(W.matmul_kernel, t, BM=128, BN=128, BK=64).source
     # a column offset that is not a multiple of 4 elements keeps plain stores
     t = dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000))
-    assert "tma_store" not in gen(W.row_softmax, t, BN=1024).source
+    assert "tma_store" not in gen(W.softmax_kernel, t, BN=1024).source
 
 
 @pytest.mark.parametrize("dt", ["i32", "u32", "f32"])

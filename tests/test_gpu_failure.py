@@ -50,12 +50,12 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     opts = native.default_options(extra=["-DTILA_WAIT_NS=2000000ull"])
     lib = native.Library(native.compile_cubin(SOURCE, "tila_wait_timeout_probe", opts))
     kern = lib.kernel("tila_wait_timeout_probe")
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(native.ERROR_BLOCK_BYTES // 4, dtype=torch.int32, device=dev)   # no host word
     out = torch.full((4,), -1, dtype=torch.int64, device=dev)
     kern.launch((1, 1, 1), (32, 1, 1), [ctypes.c_void_p(err.data_ptr()), ctypes.c_void_p(out.data_ptr())],
                 stream=torch.cuda.current_stream(dev).cuda_stream)
     torch.cuda.synchronize()
-    word = int(err.item()) & 0xFFFFFFFF
+    word = int(err[0].item()) & 0xFFFFFFFF
     assert word >> 24 == 1                      # kErrMbarrierTimeout
     assert word & 0xFFFFFF == 4242              # the first wait that gave up
     first_ok, first_ns, second_ok, second_ns = out.tolist()
@@ -64,7 +64,39 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     # the context is intact: a generated kernel runs and matches the interpreter
     x, y = W.add_inputs(4096, seed=3)
     o = torch.zeros(4096, device=dev)
-    W.vector_add[(4,)](torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev), o, BLOCK=1024)
+    W.add_kernel[(4,)](torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev), o, BLOCK=1024)
+    assert tila_b200.read_device_errors(dev) == 0
+    np.testing.assert_array_equal(o.cpu().numpy(), x + y)
+
+
+def test_device_error_raises_at_the_next_launch():
+    """A launch that recorded a device error (here the timed-out wait of the
+    probe, given the backend's error block for the device) makes the next
+    kernel[grid] call on that device raise TILA-TARGET-005 with the recorded
+    line, without the host synchronising; the launch after that runs."""
+    from tila_b200.backend import _error_word
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    opts = native.default_options(extra=["-DTILA_WAIT_NS=2000000ull"])
+    lib = native.Library(native.compile_cubin(SOURCE, "tila_wait_timeout_probe", opts))
+    kern = lib.kernel("tila_wait_timeout_probe")
+    x, y = W.add_inputs(4096, seed=4)
+    xg, yg = torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)
+    o = torch.zeros(4096, device=dev)
+    W.add_kernel[(4,)](xg, yg, o, BLOCK=1024)              # creates the device's error block
+    out = torch.full((4,), -1, dtype=torch.int64, device=dev)
+    kern.launch((1, 1, 1), (32, 1, 1), [ctypes.c_void_p(_error_word(dev).data_ptr()),
+                                        ctypes.c_void_p(out.data_ptr())],
+                stream=torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize()
+    with pytest.raises(tila_b200.tila.errors.TilaError) as exc:
+        W.add_kernel[(4,)](xg, yg, o, BLOCK=1024)
+    assert exc.value.code == "TILA-TARGET-005"
+    assert exc.value.loc.line == 4242 and "timed out" in str(exc.value)
+    o.zero_()
+    W.add_kernel[(4,)](xg, yg, o, BLOCK=1024)               # reported once; the device is usable
+    torch.cuda.synchronize()
+    tila_b200.check_device_errors(dev)
     assert tila_b200.read_device_errors(dev) == 0
     np.testing.assert_array_equal(o.cpu().numpy(), x + y)
 

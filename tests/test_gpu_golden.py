@@ -10,7 +10,7 @@ import torch
 import tila_b200
 from tila_b200 import workloads as W
 from oracle import restate
-from test_oracle import CASES, load, our_program
+from test_oracle import CASES, load, example_kernel
 
 pytestmark = pytest.mark.gpu
 
@@ -22,7 +22,7 @@ def _cuda(a):
 @pytest.mark.parametrize("case", CASES)
 def test_golden_on_b200(case):
     inputs, want, meta = load(case)
-    prog, consts = our_program(meta)
+    prog, consts = example_kernel(meta)
     out = torch.zeros(want.shape, dtype=torch.float32, device="cuda")
     prog[tuple(meta["grid"])](*(_cuda(a) for a in inputs), out, *meta["scalars"], **consts)
     torch.cuda.synchronize()
@@ -52,8 +52,8 @@ def test_causal_flash_attention_128_tiles(l, d, warps):
     128x128 tiles."""
     q, k, v = W.attention_inputs(2, l, d, seed=17)
     o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    W.flash_attention_causal[(-(-l // 128), 2)].with_options(num_warps=warps)(
-        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, BM=128, BN=128, BD=d)
+    W.fused_attention_kernel[(-(-l // 128), 2)].with_options(num_warps=warps)(
+        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, CAUSAL=1, BM=128, BN=128, BD=d)
     torch.cuda.synchronize()
     assert tila_b200.read_device_errors() == 0
     ref = restate.attention_f64(q, k, v, causal=True)

@@ -46,7 +46,7 @@ def execute(kernel, grid, inputs, out_shape, *scalars, warps=4, **consts):
 def test_add_bit_exact(n, warps):
     rng = np.random.default_rng(301)
     x, y = [rng.normal(size=n).astype(np.float32) for _ in range(2)]
-    cpu, gpu = execute(W.vector_add, (ti.cdiv(n, 128),), [x, y], (n,), warps=warps, BLOCK=128)
+    cpu, gpu = execute(W.add_kernel, (ti.cdiv(n, 128),), [x, y], (n,), warps=warps, BLOCK=128)
     np.testing.assert_array_equal(cpu, x + y)
     np.testing.assert_array_equal(gpu, cpu)
 
@@ -54,7 +54,7 @@ def test_add_bit_exact(n, warps):
 def test_add_full_size_bit_exact():
     x, y = W.add_inputs()
     out = torch.zeros(x.shape, dtype=torch.float32, device="cuda")
-    W.vector_add[(ti.cdiv(x.size, 1024),)](_cuda(x), _cuda(y), out, BLOCK=1024)
+    W.add_kernel[(ti.cdiv(x.size, 1024),)](_cuda(x), _cuda(y), out, BLOCK=1024)
     _no_device_errors()
     np.testing.assert_array_equal(out.cpu().numpy(), restate.vector_add(x, y))
 
@@ -63,7 +63,7 @@ def test_add_full_size_bit_exact():
 @pytest.mark.parametrize("n", [31, 32, 33])
 def test_softmax(n, warps):
     x = np.random.default_rng(302).normal(size=(3, n)).astype(np.float32)
-    cpu, gpu = execute(W.row_softmax, (3,), [x], x.shape, warps=warps, BN=64)
+    cpu, gpu = execute(W.softmax_kernel, (3,), [x], x.shape, warps=warps, BN=64)
     ref = restate.row_softmax_f64(x)
     np.testing.assert_allclose(gpu, ref, rtol=2e-6, atol=2e-7)
     np.testing.assert_allclose(gpu, cpu, rtol=1e-6, atol=0)
@@ -72,7 +72,7 @@ def test_softmax(n, warps):
 def test_softmax_full_size():
     x = W.softmax_inputs()
     out = torch.zeros(x.shape, dtype=torch.float32, device="cuda")
-    W.row_softmax[(x.shape[0],)](_cuda(x), out, BN=1024)
+    W.softmax_kernel[(x.shape[0],)](_cuda(x), out, BN=1024)
     _no_device_errors()
     got = out.cpu().numpy()
     # the interpreter's arithmetic restated (bit-for-bit the same NumPy calls)
@@ -93,7 +93,7 @@ def test_matmul_small(shape, strided, warps):
     if strided:
         a = np.ascontiguousarray(a.T).T
         b = np.ascontiguousarray(b.T).T
-    cpu, gpu = execute(W.tiled_matmul, (ti.cdiv(m, 16), ti.cdiv(n, 16)), [a, b], (m, n),
+    cpu, gpu = execute(W.matmul_kernel, (ti.cdiv(m, 16), ti.cdiv(n, 16)), [a, b], (m, n),
                        warps=warps, BM=16, BN=16, BK=32)
     ref = restate.matmul_f64(a, b)
     bound = restate.matmul_bound(a, b)
@@ -106,7 +106,7 @@ def test_matmul_128_tiles(shape):
     m, n, k = shape
     a, b = W.matmul_inputs(m, n, k, seed=7)
     c = torch.zeros((m, n), dtype=torch.float32, device="cuda")
-    W.tiled_matmul[(ti.cdiv(m, 128), ti.cdiv(n, 128))](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)
+    W.matmul_kernel[(ti.cdiv(m, 128), ti.cdiv(n, 128))](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)
     _no_device_errors()
     got = c.cpu().numpy()
     assert np.all(np.abs(got - restate.matmul_f64(a, b)) <= restate.matmul_bound(a, b))
@@ -117,8 +117,8 @@ def test_matmul_128_tiles(shape):
 def test_fused_attention_small(n, warps):
     rng = np.random.default_rng(305)
     q, k, v = [rng.normal(size=(2, n, 32)).astype(np.float16) for _ in range(3)]
-    cpu, gpu = execute(W.flash_attention, (ti.cdiv(n, 32), 2), [q, k, v], (2, n, 32),
-                       1 / np.sqrt(32), warps=warps, BM=32, BN=32, BD=32)
+    cpu, gpu = execute(W.fused_attention_kernel, (ti.cdiv(n, 32), 2), [q, k, v], (2, n, 32),
+                       1 / np.sqrt(32), warps=warps, CAUSAL=0, BM=32, BN=32, BD=32)
     ref = restate.attention_f64(q, k, v)
     np.testing.assert_allclose(gpu, ref, rtol=2e-3, atol=2e-3)
     assert restate.rel_frobenius(gpu, cpu) <= 2e-3
@@ -127,8 +127,8 @@ def test_fused_attention_small(n, warps):
 def test_fused_attention_128_tiles():
     q, k, v = W.attention_inputs(2, 384, 128, seed=11)
     o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    W.flash_attention[(ti.cdiv(384, 128), 2)](_cuda(q), _cuda(k), _cuda(v), o, 128 ** -0.5,
-                                              BM=128, BN=128, BD=128)
+    W.fused_attention_kernel[(ti.cdiv(384, 128), 2)](_cuda(q), _cuda(k), _cuda(v), o, 128 ** -0.5,
+                                              CAUSAL=0, BM=128, BN=128, BD=128)
     _no_device_errors()
     assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
 
@@ -142,8 +142,8 @@ def test_fused_attention_ragged_128_tiles(l, d, warps):
     query blocks (a CTA whose second program does not exist)."""
     q, k, v = W.attention_inputs(3, l, d, seed=13)
     o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    W.flash_attention[(ti.cdiv(l, 128), 3)].with_options(num_warps=warps)(
-        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, BM=128, BN=128, BD=d)
+    W.fused_attention_kernel[(ti.cdiv(l, 128), 3)].with_options(num_warps=warps)(
+        _cuda(q), _cuda(k), _cuda(v), o, d ** -0.5, CAUSAL=0, BM=128, BN=128, BD=d)
     _no_device_errors()
     assert restate.rel_frobenius(o.cpu().numpy(), restate.attention_f64(q, k, v)) <= 2e-3
 
@@ -159,7 +159,7 @@ def test_unfused_attention(l, d, blk):
     o = torch.zeros((bh, l, d), dtype=torch.float32, device="cuda")
     W.attention_scores[(ti.cdiv(l, blk), ti.cdiv(l, blk), bh)](qg, kg, s, scale, BM=blk, BN=blk, BD=d)
     bn = 1 << (l - 1).bit_length()
-    W.row_softmax[(bh * l,)](s.view(bh * l, l), p.view(bh * l, l), BN=max(bn, 16))
+    W.softmax_kernel[(bh * l,)](s.view(bh * l, l), p.view(bh * l, l), BN=max(bn, 16))
     W.attention_pv[(ti.cdiv(l, blk), bh)](p, vg, o, BM=blk, BN=blk, BD=d)
     _no_device_errors()
     ref = restate.attention_f64(q, k, v, scale)
@@ -176,21 +176,21 @@ def test_program_range_shards_reproduce_the_full_launch(world):
     from tila_b200.multigpu import shard
     x = torch.from_numpy(W.softmax_inputs(300, 1000, seed=13)).cuda()
     full = torch.zeros_like(x)
-    W.row_softmax[(300,)](x, full, BN=1024)
+    W.softmax_kernel[(300,)](x, full, BN=1024)
     parts = torch.full_like(x, float("nan"))
     for rank in range(world):
         with shard(0, 300, world, rank):
-            W.row_softmax[(300,)](x, parts, BN=1024)
+            W.softmax_kernel[(300,)](x, parts, BN=1024)
     _no_device_errors()
     assert torch.equal(parts, full)
     a, b = W.matmul_inputs(384, 256, 128, seed=14)
     ag, bg = _cuda(a), _cuda(b)
     c_full = torch.zeros((384, 256), device="cuda")
-    W.tiled_matmul[(3, 2)](ag, bg, c_full, BM=128, BN=128, BK=64)
+    W.matmul_kernel[(3, 2)](ag, bg, c_full, BM=128, BN=128, BK=64)
     c_part = torch.full_like(c_full, float("nan"))
     for rank in range(world):
         with shard(0, 3, world, rank):
-            W.tiled_matmul[(3, 2)](ag, bg, c_part, BM=128, BN=128, BK=64)
+            W.matmul_kernel[(3, 2)](ag, bg, c_part, BM=128, BN=128, BK=64)
     _no_device_errors()
     assert torch.equal(c_part, c_full)
 
@@ -205,25 +205,25 @@ def test_repeated_signature_launches_skip_checks_and_use_new_buffers():
     ys = [torch.randn(n, device="cuda") for _ in range(3)]
     outs = [torch.empty(n, device="cuda") for _ in range(3)]
     grid = (ti.cdiv(n, 1024),)
-    W.vector_add[grid](xs[0], ys[0], outs[0], BLOCK=1024)
+    W.add_kernel[grid](xs[0], ys[0], outs[0], BLOCK=1024)
     hits = plugin.fast_hits
     for i in (1, 2):
-        W.vector_add[grid](xs[i], ys[i], outs[i], BLOCK=1024)
+        W.add_kernel[grid](xs[i], ys[i], outs[i], BLOCK=1024)
     torch.cuda.synchronize()
     assert plugin.fast_hits == hits + 2
     for i in range(3):
         assert torch.equal(outs[i], xs[i] + ys[i])
-    assert W.vector_add.last_backend_resources is not None
+    assert W.add_kernel.last_backend_resources is not None
     # a new shape and an aliased output are checked again
     m = 2000
     o2 = torch.empty(m, device="cuda")
-    W.vector_add[(ti.cdiv(m, 1024),)](xs[0][:m], ys[0][:m], o2, BLOCK=1024)
+    W.add_kernel[(ti.cdiv(m, 1024),)](xs[0][:m], ys[0][:m], o2, BLOCK=1024)
     assert plugin.fast_hits == hits + 2
     torch.cuda.synchronize()
     assert torch.equal(o2, xs[0][:m] + ys[0][:m])
     x_alias = xs[2].clone()
     try:
-        W.vector_add[grid](x_alias, ys[2], x_alias, BLOCK=1024)
+        W.add_kernel[grid](x_alias, ys[2], x_alias, BLOCK=1024)
     except ti.errors.TilaError:
         pass                       # the checker may reject the aliasing: also not cached
     else:

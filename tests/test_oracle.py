@@ -1,8 +1,10 @@
 """The oracle, pinned: the golden fixtures (the reference's example kernels
 run on its NumPy interpreter, tests/golden/make_golden.py) reproduced by
 
-* this repository's programs (tila_b200.workloads) on the same interpreter,
-  bit for bit - they compute exactly what the reference examples compute;
+* the installed example kernels (tila_b200.workloads loads them from the
+  installed Tila tree) on the interpreter of this environment, bit for bit -
+  the kernels the backend is measured on are the ones the fixtures came from,
+  and this NumPy computes what the generating one did;
 * the NumPy restatement (oracle.restate) - bit for bit for add and softmax,
   within the reference suite's bounds for matmul and attention
   (tests/gpu_examples.py:28-97);
@@ -33,18 +35,17 @@ def load(case):
     return inputs, z["out"], meta
 
 
-def our_program(meta):
+def example_kernel(meta):
     ex, consts = meta["example"], dict(meta["consts"])
     if ex.endswith("add_kernel.py"):
-        return W.vector_add, consts
+        return W.add_kernel, consts
     if ex.endswith("softmax.py"):
-        return W.row_softmax, consts
+        return W.softmax_kernel, consts
     if ex.endswith("matmul.py"):
-        return W.tiled_matmul, consts
+        return W.matmul_kernel, consts
     if ex.endswith("self_attention.py"):
-        return W.causal_self_attention, consts
-    causal = consts.pop("CAUSAL")
-    return (W.flash_attention_causal if causal else W.flash_attention), consts
+        return W.self_attention_kernel, consts
+    return W.fused_attention_kernel, consts
 
 
 def test_fixtures_present():
@@ -52,9 +53,9 @@ def test_fixtures_present():
 
 
 @pytest.mark.parametrize("case", CASES)
-def test_programs_reproduce_reference_examples_bit_exact(case):
+def test_installed_examples_reproduce_fixtures_bit_exact(case):
     inputs, want, meta = load(case)
-    prog, consts = our_program(meta)
+    prog, consts = example_kernel(meta)
     out = np.zeros_like(want)
     with np.errstate(all="ignore"):
         prog[tuple(meta["grid"])](*inputs, out, *meta["scalars"], **consts)

@@ -26,7 +26,7 @@ def test_b200_capability_matches_the_reference_limits():
 def test_cpu_arrays_still_run_on_the_interpreter():
     x = np.arange(300, dtype=np.float32)
     out = np.zeros_like(x)
-    W.vector_add[(ti.cdiv(300, 128),)](x, x, out, BLOCK=128)
+    W.add_kernel[(ti.cdiv(300, 128),)](x, x, out, BLOCK=128)
     np.testing.assert_array_equal(out, x + x)
 
 

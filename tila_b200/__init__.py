@@ -8,9 +8,9 @@ C++, compiled with NVRTC for sm_100a and launched through the native C ABI
 
 from ._reference import tila
 from .plugin import B200, install, installed, uninstall
-from .backend import program_range, read_device_errors, generated_source
+from .backend import check_device_errors, program_range, read_device_errors, generated_source
 
 install()
 
 __all__ = ["tila", "B200", "install", "uninstall", "installed", "program_range",
-           "read_device_errors", "generated_source"]
+           "read_device_errors", "check_device_errors", "generated_source"]

@@ -42,3 +42,26 @@ def import_tila():
 
 
 tila = import_tila()
+
+
+def reference_tree() -> Path:
+    """The directory holding Tila's ``examples/`` and ``tests/`` (copied beside
+    the package by ``tila_b200.build.ensure_reference_install``, or named by
+    ``TILA_REFERENCE_TREE``)."""
+    env = os.environ.get("TILA_REFERENCE_TREE")
+    for path in ([Path(env)] if env else []) + [REPO_ROOT / "baseline" / "_ref" / "tila_reference_tree"]:
+        if (path / "examples").is_dir():
+            return path
+    raise ImportError(
+        "Tila's examples/ are not installed: run __graft_entry__.build() (or "
+        "tila_b200.build.ensure_reference_install with a Tila checkout), or set "
+        "TILA_REFERENCE_TREE to a directory containing examples/ and tests/")
+
+
+def example(module: str):
+    """Import one of Tila's own example modules (``examples/<module>.py``)
+    unchanged; the kernels they define run on the backend as they are."""
+    path = str(reference_tree() / "examples")
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    return importlib.import_module(module)

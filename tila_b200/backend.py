@@ -62,32 +62,98 @@ def current_program_range():
 
 
 # ---------------------------------------------------------------------------
-# device error words
+# device errors
 # ---------------------------------------------------------------------------
+#
+# Every generated kernel takes a 16-byte error block (include/tila_b200.h,
+# TILA_ERROR_BLOCK_BYTES): the first device error of a launch - a bounded
+# wait that timed out, a failed tensor-memory allocation, a false ti.assume in
+# a debug build - is recorded there with its Tila source line, and the thread
+# that records it also stores it into a page-locked host word whose device
+# address the block carries.  The host reads that word without synchronising:
+# every launch on the device first checks it and raises TILA-TARGET-005 for an
+# error an earlier launch recorded, so a kernel that stopped early is never
+# taken for a result by the next step.  ``check_device_errors`` does the same
+# check on demand; ``read_device_errors`` synchronises and reads the block.
 
-_err_words = {}
+ERROR_CODES = {
+    1: "a bounded wait on an mbarrier timed out (a TMA copy, tensor-core commit or "
+       "partner warpgroup never arrived); the program stopped early and its outputs are incomplete",
+    2: "tensor memory allocation failed",
+    3: "a ti.assume predicate was false (TILA_DEBUG=1 build)",
+}
+
+
+class _ErrorBlock:
+    def __init__(self, device):
+        import torch
+        self.device = device
+        self.block = torch.zeros(native.ERROR_BLOCK_BYTES // 4, dtype=torch.int32, device=device)
+        with torch.cuda.device(device):
+            self.host, addr = native.host_word_alloc()
+        self.block.view(torch.int64)[1] = addr
+        self.word = ctypes.c_uint32.from_address(self.host)
+
+    def pending(self) -> int:
+        return self.word.value
+
+    def clear(self):
+        """Stream-ordered reset of the block's error word and of the host word."""
+        self.word.value = 0
+        self.block[0].zero_()
+
+
+_err_blocks = {}
+
+
+def _error_block(device) -> _ErrorBlock:
+    b = _err_blocks.get(device.index)
+    if b is None:
+        b = _err_blocks[device.index] = _ErrorBlock(device)
+    return b
 
 
 def _error_word(device):
+    """The error block tensor passed to every launch on ``device``."""
+    return _error_block(device).block
+
+
+def describe_error(word: int) -> str:
+    code, line = word >> 24, word & 0xFFFFFF
+    what = ERROR_CODES.get(code, f"device error code {code}")
+    return f"{what} (Tila source line {line})"
+
+
+def check_device_errors(device=None) -> None:
+    """Raise ``TILA-TARGET-005`` if a kernel launched on ``device`` has
+    recorded a device error that no one has read yet.  Does not synchronise:
+    it sees errors of kernels that have reached them."""
     import torch
-    key = device.index
-    w = _err_words.get(key)
-    if w is None:
-        w = _err_words[key] = torch.zeros(1, dtype=torch.int32, device=device)
-    return w
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index
+    b = _err_blocks.get(idx)
+    if b is None:
+        return
+    word = b.pending()
+    if word:
+        b.clear()
+        raise TilaError("TILA-TARGET-005", "a kernel launched earlier on this device failed",
+                        Loc(word & 0xFFFFFF),
+                        details=[f"device: cuda:{idx}", f"error: {describe_error(word)}"],
+                        fixes=["the outputs of that launch are incomplete: launch it again"])
 
 
 def read_device_errors(device=None, reset=True) -> int:
     """Synchronise and return the first in-kernel error recorded on ``device``
-    (0 = none; high byte = code: 1 mbarrier wait timed out)."""
+    (0 = none; high byte = code, low 24 bits = Tila source line; see
+    ``ERROR_CODES``).  ``reset`` clears it."""
     import torch
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    w = _err_words.get(device.index)
-    if w is None:
+    b = _err_blocks.get(device.index)
+    if b is None:
         return 0
-    val = int(w.item()) & 0xFFFFFFFF
-    if reset and val:
-        w.zero_()
+    val = int(b.block[0].item()) & 0xFFFFFFFF
+    if reset and (val or b.pending()):
+        b.clear()
     return val
 
 
@@ -138,9 +204,12 @@ def binding_facts(tk, tensors) -> dict:
 
 
 def _cache_for(jf):
-    cache = getattr(jf, "_b200_cache", None)
+    """The kernel cache of ``jf``: the reference's per-function dict
+    (``JITFunction._kern_cache``, runtime.py:147), so that its size means
+    what it means on the Triton path (one entry per compiled variant)."""
+    cache = getattr(jf, "_kern_cache", None)
     if cache is None:
-        cache = jf._b200_cache = {}
+        cache = jf._kern_cache = {}
     return cache
 
 
@@ -148,12 +217,26 @@ def _debug():
     return os.environ.get("TILA_DEBUG", "") == "1"
 
 
+def tir_fingerprint(tk) -> str:
+    """Hash of the typed TIR as it is now.  The reference keys its cache on
+    the generated source (runtime.py:684-696), so a kernel whose TIR was
+    edited after decoration compiles again; this key does the same without
+    generating code first."""
+    import hashlib
+    return hashlib.sha256(repr(tk.body).encode()).hexdigest()
+
+
 def compile_kernel(jf, consts, facts, num_warps, context=None) -> Compiled:
+    """The compiled kernel for a specialisation, from ``jf._kern_cache`` or
+    built.  The key follows the reference's semantic key
+    (``_triton_cache_key``, runtime.py:684-696): intrinsic registry revision,
+    function, typed Consts, debug mode, warps, Python source and TIR
+    fingerprints, binding facts, constant payloads."""
     tk = jf.tk
-    key = (tila.intrinsics.INTRINSIC_REGISTRY_SEMANTIC_REVISION, jf.source_fingerprint,
+    key = ("b200", tila.intrinsics.INTRINSIC_REGISTRY_SEMANTIC_REVISION, id(jf),
            tuple((k, "Bool" if type(v) is bool else "Int", v) for k, v in sorted(consts.items())),
-           num_warps, tuple(f.key() for f in facts.values()), _debug(),
-           tila.tir.constant_signature(tk.body))
+           _debug(), num_warps, jf.source_fingerprint, tir_fingerprint(tk),
+           tuple(f.key() for f in facts.values()), tila.tir.constant_signature(tk.body))
     cache = _cache_for(jf)
     hit = cache.get(key)
     if hit is not None:
@@ -289,6 +372,7 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
                "scalars": scalar_vals, "grid": grid, "num_warps": launcher.num_warps,
                "debug": _debug(), "backend": "b200",
                "target": asdict(target) if target is not None else None}
+    check_device_errors(device)
     with torch.cuda.device(device):
         entry = compile_kernel(jf, consts, facts, launcher.num_warps, context)
         if entry.attrs is None or entry.attrs.get("_device") != device.index:

@@ -54,21 +54,46 @@ def check_tile_library():
         subprocess.run(cmd, check=True, capture_output=True)
 
 
-def ensure_reference_install():
+REFERENCE_TREE = "tila_reference_tree"
+
+
+def ensure_reference_install(src=None):
     """Install Tila (the package this backend plugs into) into
-    ``baseline/_ref`` from a read-only source tree when it is missing."""
+    ``baseline/_ref`` from a read-only Tila source tree ``src`` (a checkout
+    with ``pyproject.toml``; default: ``$TILA_REFERENCE_SRC``) when it is
+    missing, and copy the tree's ``examples/``, ``tests/`` and ``tools/``
+    beside the package (``baseline/_ref/tila_reference_tree``).  The example
+    kernels are what the benchmark and the parity tests launch unchanged, and
+    the GPU suites under ``tests/`` (which replay failures with
+    ``tools/replay_backend.py``) are run against this backend; none of them is
+    part of the installed wheel.  Returns the install directory, or None when neither
+    an install nor a source tree is available."""
     target = ROOT / "baseline" / "_ref"
-    if (target / "tila" / "__init__.py").exists():
+    tree = target / REFERENCE_TREE
+    have_pkg = (target / "tila" / "__init__.py").exists()
+    parts = ("examples", "tests", "tools")
+    have_tree = all((tree / part).is_dir() for part in parts)
+    if have_pkg and have_tree:
         return target
-    src = Path(os.environ.get("TILA_REFERENCE_SRC", "/root/reference"))
-    if not (src / "pyproject.toml").exists():
-        return None
-    with tempfile.TemporaryDirectory() as d:
-        tmp = Path(d) / "tila_src"
-        shutil.copytree(src, tmp, ignore=shutil.ignore_patterns(".git"))
-        subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
-                        "--no-deps", "--find-links", "/opt/wheelhouse", "--target", str(target),
-                        str(tmp)], check=True, capture_output=True)
+    src = src or os.environ.get("TILA_REFERENCE_SRC")
+    if not src or not (Path(src) / "pyproject.toml").exists():
+        return target if have_pkg else None
+    src = Path(src)
+    if not have_pkg:
+        with tempfile.TemporaryDirectory() as d:
+            tmp = Path(d) / "tila_src"
+            shutil.copytree(src, tmp, ignore=shutil.ignore_patterns(".git"))
+            subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+                            "--no-deps", "--target", str(target), str(tmp)],
+                           check=True, capture_output=True)
+    if not have_tree:
+        staging = target / (REFERENCE_TREE + ".tmp")
+        shutil.rmtree(staging, ignore_errors=True)
+        for part in parts:
+            shutil.copytree(src / part, staging / part,
+                            ignore=shutil.ignore_patterns("__pycache__", "*.pyc", ".pytest_cache"))
+        shutil.rmtree(tree, ignore_errors=True)
+        os.replace(staging, tree)
     return target
 
 
@@ -81,18 +106,18 @@ def warm_cubins():
     from . import native
     f16, f32 = torch.float16, torch.float32
     cases = [
-        (W.vector_add, dict(x=torch.zeros(1 << 20), y=torch.zeros(1 << 20), out=torch.zeros(1 << 20)),
+        (W.add_kernel, dict(x=torch.zeros(1 << 20), y=torch.zeros(1 << 20), out=torch.zeros(1 << 20)),
          dict(BLOCK=1024)),
-        (W.row_softmax, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), dict(BN=1024)),
-        (W.tiled_matmul, dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16),
+        (W.softmax_kernel, dict(x=torch.zeros(8, 1000), o=torch.zeros(8, 1000)), dict(BN=1024)),
+        (W.matmul_kernel, dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16),
                               c=torch.zeros(256, 256)), dict(BM=128, BN=128, BK=64)),
         (W.attention_scores, dict(q=torch.zeros(2, 256, 64, dtype=f16), k=torch.zeros(2, 256, 64, dtype=f16),
                                   s=torch.zeros(2, 256, 256)), dict(BM=128, BN=128, BD=64)),
         (W.attention_pv, dict(p=torch.zeros(2, 256, 256), v=torch.zeros(2, 256, 64, dtype=f16),
                               o=torch.zeros(2, 256, 64)), dict(BM=128, BN=128, BD=64)),
-        (W.flash_attention, dict(q=torch.zeros(2, 256, 128, dtype=f16), k=torch.zeros(2, 256, 128, dtype=f16),
+        (W.fused_attention_kernel, dict(q=torch.zeros(2, 256, 128, dtype=f16), k=torch.zeros(2, 256, 128, dtype=f16),
                                  v=torch.zeros(2, 256, 128, dtype=f16), o=torch.zeros(2, 256, 128)),
-         dict(BM=128, BN=128, BD=128)),
+         dict(CAUSAL=0, BM=128, BN=128, BD=128)),
     ]
     names = []
     for jf, tensors, consts in cases:

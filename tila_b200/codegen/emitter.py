@@ -151,6 +151,68 @@ def _stmt_names_assigned(stmts, out=None):
     return out
 
 
+def resolve_static_ifs(tk, consts):
+    """The kernel with every ``static_if`` replaced by the branch its Const
+    values select, recursively (the statements of the taken branch take the
+    place of the ``static_if`` in the enclosing body).
+
+    A ``static_if`` is resolved per Const specialisation (tir.py:324-335); the
+    interpreter runs the selected branch in the enclosing scope
+    (interp.py:145-154), so splicing it in changes no binding.  Resolving it
+    before code generation lets the loop matchers see a loop of the taken
+    branch as a statement of the enclosing body: the non-causal loop of
+    examples/fused_attention.py:104-126 sits inside ``if CAUSAL == 1: ...
+    else:`` and is a top-level loop of the CAUSAL=0 specialisation.  A
+    condition that does not evaluate from the Consts (and from names assigned
+    once, from Consts only) keeps its ``static_if``; the emitter then decides
+    it while emitting.  The caller's kernel object is not modified."""
+    ev = tila.runtime._eval_const_operand
+    counts = {}
+
+    def count(stmts):
+        for s in stmts:
+            if isinstance(s, T_.TAssign):
+                counts[s.name] = counts.get(s.name, 0) + 1
+            elif isinstance(s, (T_.TIf, T_.TStaticIf)):
+                count(s.then_body)
+                count(s.else_body)
+            elif isinstance(s, T_.TFor):
+                counts[s.var] = counts.get(s.var, 0) + 2
+                count(s.body)
+    count(tk.body)
+    known = dict(consts)
+    changed = [False]
+
+    def walk(stmts):
+        out = []
+        for s in stmts:
+            if isinstance(s, T_.TStaticIf):
+                try:
+                    taken = bool(ev(s.cond, known))
+                except Exception:
+                    taken = None
+                if taken is None:
+                    out.append(dataclasses.replace(s, then_body=walk(s.then_body),
+                                                   else_body=walk(s.else_body)))
+                else:
+                    changed[0] = True
+                    out.extend(walk(s.then_body if taken else s.else_body))
+                continue
+            if isinstance(s, T_.TAssign) and counts.get(s.name) == 1 and s.name not in known:
+                try:
+                    known[s.name] = ev(s.value, known)
+                except Exception:
+                    pass
+            if isinstance(s, T_.TIf):
+                s = dataclasses.replace(s, then_body=walk(s.then_body), else_body=walk(s.else_body))
+            elif isinstance(s, T_.TFor):
+                s = dataclasses.replace(s, body=walk(s.body))
+            out.append(s)
+        return out
+    body = walk(tk.body)
+    return dataclasses.replace(tk, body=body) if changed[0] else tk
+
+
 class _Smem:
     """Linear plan of the kernel's dynamic shared memory."""
 
@@ -181,6 +243,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
                  entry_name=None, debug=False, versioning=True, source_map=False):
+        tk = resolve_static_ifs(tk, consts)
         self.tk = tk
         self.source_map = source_map     # annotate the output with Tila source lines
         self.versioning = versioning     # loop bodies specialised for interior tiles

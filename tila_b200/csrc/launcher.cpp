@@ -55,6 +55,9 @@ struct Driver {
                                    const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
                                    CUtensorMapFloatOOBfill) = nullptr;
+  CUresult (*MemHostAlloc)(void **, size_t, unsigned int) = nullptr;
+  CUresult (*MemHostGetDevicePointer)(CUdeviceptr *, void *, unsigned int) = nullptr;
+  CUresult (*MemFreeHost)(void *) = nullptr;
   bool ready = false;
   std::string failure;
 };
@@ -87,7 +90,10 @@ void open_driver() {
             bind(h, "cuKernelGetAttribute", g_drv.KernelGetAttribute) &&
             bind(h, "cuKernelSetAttribute", g_drv.KernelSetAttribute) &&
             bind(h, "cuLaunchKernelEx", g_drv.LaunchKernelEx) &&
-            bind(h, "cuTensorMapEncodeTiled", g_drv.TensorMapEncodeTiled);
+            bind(h, "cuTensorMapEncodeTiled", g_drv.TensorMapEncodeTiled) &&
+            bind(h, "cuMemHostAlloc", g_drv.MemHostAlloc) &&
+            bind(h, "cuMemHostGetDevicePointer_v2", g_drv.MemHostGetDevicePointer) &&
+            bind(h, "cuMemFreeHost", g_drv.MemFreeHost);
   if (!ok) {
     g_drv.failure = "libcuda.so.1 lacks a required entry point (driver too old?)";
     return;
@@ -136,6 +142,16 @@ int current_device(CUdevice *dev, char *log, size_t cap) {
 }
 
 }  // namespace
+
+// The calling thread's current CUDA context (for the no-allocation entry
+// point, which caches a device address per context); not part of the ABI.
+int tila_internal_current_context(void **ctx_out) {
+  if (ensure_driver(nullptr, 0) != TILA_OK) return TILA_ERR_DRIVER;
+  CUcontext ctx = nullptr;
+  if (g_drv.CtxGetCurrent(&ctx) != CUDA_SUCCESS) return TILA_ERR_DRIVER;
+  *ctx_out = ctx;
+  return TILA_OK;
+}
 
 extern "C" {
 
@@ -374,6 +390,35 @@ int tila_encode_tensor_map(void *tensor_map_out, int dtype, int rank,
       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return driver_error(r, "cuTensorMapEncodeTiled", log, log_cap, TILA_ERR_ARGUMENT);
   return TILA_OK;
+}
+
+int tila_host_word_alloc(uint32_t **host_out, uint64_t *device_address_out,
+                         char *log, size_t log_cap) {
+  if (host_out == nullptr || device_address_out == nullptr) return TILA_ERR_ARGUMENT;
+  int st = ensure_driver(log, log_cap);
+  if (st != TILA_OK) return st;
+  CUdevice dev;
+  st = current_device(&dev, log, log_cap);
+  if (st != TILA_OK) return st;
+  void *p = nullptr;
+  CUresult r = g_drv.MemHostAlloc(&p, 64, CU_MEMHOSTALLOC_PORTABLE | CU_MEMHOSTALLOC_DEVICEMAP);
+  if (r != CUDA_SUCCESS) return driver_error(r, "cuMemHostAlloc", log, log_cap);
+  std::memset(p, 0, 64);
+  CUdeviceptr d = 0;
+  r = g_drv.MemHostGetDevicePointer(&d, p, 0);
+  if (r != CUDA_SUCCESS) {
+    g_drv.MemFreeHost(p);
+    return driver_error(r, "cuMemHostGetDevicePointer", log, log_cap);
+  }
+  *host_out = static_cast<uint32_t *>(p);
+  *device_address_out = static_cast<uint64_t>(d);
+  return TILA_OK;
+}
+
+int tila_host_word_free(uint32_t *host) {
+  if (host == nullptr) return TILA_OK;
+  if (ensure_driver(nullptr, 0) != TILA_OK) return TILA_ERR_DRIVER;
+  return g_drv.MemFreeHost(host) == CUDA_SUCCESS ? TILA_OK : TILA_ERR_DRIVER;
 }
 
 int tila_device_info(int *sm_count, int *max_smem_optin, int *cc_major,

@@ -36,10 +36,21 @@ enum ErrorCode : u32 {
   kErrAssumption = 3,        // a ti.assume predicate was false (debug builds)
 };
 
-// Records the first error of a launch.  `err` points at a device word the
-// host reads after synchronising.
+// Records the first error of a launch.  `err` points at the launch's 16-byte
+// error block: word 0 takes (code << 24) | line of the first error; bytes
+// 8-15 hold the device address of a notification word in page-locked host
+// memory (0 = none), where the thread that recorded the error also stores it,
+// so that the host sees device errors without synchronising.
 __device__ __forceinline__ void report_error(u32 *err, u32 code, u32 where) {
-  if (err != nullptr) atomicCAS(err, 0u, (code << 24) | (where & 0xFFFFFFu));
+  if (err == nullptr) return;
+  const u32 v = (code << 24) | (where & 0xFFFFFFu);
+  if (atomicCAS(err, 0u, v) == 0u) {
+    const u64 notify = *reinterpret_cast<volatile u64 *>(err + 2);
+    if (notify != 0) {
+      *reinterpret_cast<volatile u32 *>(notify) = v;
+      __threadfence_system();
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -38,7 +38,11 @@ EXPORTED_SYMBOLS = (
     "tila_kernel_attrs_get", "tila_launch", "tila_encode_tensor_map",
     "tila_device_info", "tila_status_string", "tila_launch_noalloc",
     "tila_mg_unique_id", "tila_mg_comm_init", "tila_mg_gather", "tila_mg_comm_destroy",
+    "tila_host_word_alloc", "tila_host_word_free", "tila_noalloc_read_error",
 )
+
+#: Size of the error block every generated kernel takes (include/tila_b200.h).
+ERROR_BLOCK_BYTES = 16
 
 #: Capacity of the static scratch behind tila_launch_noalloc (include/tila_b200.h).
 NOALLOC_SCRATCH_BYTES = 256
@@ -121,6 +125,11 @@ def library() -> ctypes.CDLL:
         lib.tila_launch_noalloc.argtypes = [c_void_p, ctypes.POINTER(LaunchConfig),
                                             ctypes.POINTER(c_void_p), c_int, ctypes.c_uint32,
                                             c_char_p, c_size_t]
+        lib.tila_host_word_alloc.argtypes = [ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_uint64),
+                                             c_char_p, c_size_t]
+        lib.tila_host_word_free.argtypes = [c_void_p]
+        lib.tila_noalloc_read_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint64,
+                                                c_int, c_char_p, c_size_t]
         lib.tila_status_string.argtypes = [c_int]
         lib.tila_status_string.restype = c_char_p
         lib.tila_mg_unique_id.argtypes = [c_void_p, c_char_p, c_size_t]
@@ -320,6 +329,30 @@ def _aligned_tensor_map() -> TensorMap:
     tm = TensorMap.from_buffer(raw, offset)
     tm._keepalive = raw
     return tm
+
+
+def noalloc_read_error(stream=0, reset=True) -> int:
+    """The error word the last tila_launch_noalloc launch on the current
+    device recorded in the library's static scratch (synchronises ``stream``)."""
+    word = ctypes.c_uint32()
+    log = ctypes.create_string_buffer(1024)
+    _check(library().tila_noalloc_read_error(ctypes.byref(word), stream, int(bool(reset)), log,
+                                             len(log)), "read of the no-allocation error word", log)
+    return word.value
+
+
+def host_word_alloc():
+    """(host address, device address) of a zeroed page-locked 64-byte buffer
+    that kernels can write (needs a current CUDA context)."""
+    host, dev = ctypes.c_void_p(), ctypes.c_uint64()
+    log = ctypes.create_string_buffer(1024)
+    _check(library().tila_host_word_alloc(ctypes.byref(host), ctypes.byref(dev), log, len(log)),
+           "page-locked host word", log)
+    return host.value, dev.value
+
+
+def host_word_free(host: int) -> None:
+    _check(library().tila_host_word_free(ctypes.c_void_p(host)), "free of a page-locked host word")
 
 
 def device_info() -> dict:

@@ -17,6 +17,7 @@ Triton is never imported on the B200 path.
 
 from __future__ import annotations
 
+import dataclasses
 import os
 import struct
 
@@ -60,17 +61,43 @@ def _is_cuda_launch(tensors):
 # Every launch runs Tila's launch contracts, bounds proofs and race analysis
 # (runtime.py:726-1039, about 20 ms) before the kernel.  Those checks read
 # only the binding signature - dtypes, shapes, strides, base alignment,
-# aliasing between arguments, explicit scalar values, Consts, grid, options -
-# never buffer contents, so a launch whose signature equals that of an earlier
-# successful launch of the same kernel passes them with the same outcome.
-# Such a launch skips them and goes straight to the compiled kernel with the
-# new buffer addresses.  The previous launch's evidence (race report,
-# alignment facts, backend resources) stays valid for it.  TILA_B200_FASTPATH=0
-# runs the full checks on every launch.
+# aliasing between arguments, explicit scalar values, Consts, grid, options,
+# the kernel's TIR and the TILA_* environment switches - never buffer
+# contents, so a launch whose signature equals that of an earlier successful
+# launch of the same kernel passes them with the same outcome.  Such a launch
+# skips them and goes straight to the compiled kernel with the new buffer
+# addresses.  The previous launch's evidence (race report, alignment facts,
+# backend resources) stays valid for it.  This deviates from the reference,
+# whose cache hits do not exempt a launch from its checks
+# (docs/launch-target.md:53-54); TILA_B200_FASTPATH=0 restores that policy.
+# A launch takes the full path whenever anything the checks read may have
+# changed: any TILA_* variable (TILA_SAFETY, TILA_RACE_MAX_PAIRS,
+# TILA_PROOF_* included), a statement of the TIR replaced, or
+# ``_Launcher._execute`` patched by someone else.
 
 _FAST_MAX = 64
 fast_hits = 0        # launches that took the repeated-signature path (for tests)
-_ENV_KEYS = ("TILA_INTERP", "TILA_DEBUG", "TILA_RACE", "TILA_EFFECTS", "TILA_BACKEND_ARTIFACTS")
+
+
+def _tila_env():
+    """Every TILA_* environment switch (the checks and the code generation
+    read several of them: TILA_SAFETY, TILA_RACE*, TILA_PROOF_*, TILA_DEBUG,
+    TILA_INTERP, TILA_EFFECTS, TILA_BACKEND_ARTIFACTS, ...)."""
+    return tuple(sorted((k, v) for k, v in os.environ.items() if k.startswith("TILA_")))
+
+
+def _statements(body, out):
+    """Every statement object of the TIR, in order.  A launch whose kernel has
+    a statement replaced since the remembered launch takes the full path; an
+    expression edited in place inside a kept statement is not noticed (code
+    that edits TIR that way sets TILA_B200_FASTPATH=0)."""
+    for st in body:
+        out.append(st)
+        for name in ("body", "then_body", "else_body"):
+            sub = getattr(st, name, None)
+            if isinstance(sub, list):
+                _statements(sub, out)
+    return out
 
 
 def _pow2_div(v, cap=256):
@@ -129,9 +156,8 @@ def _fast_key(launcher, args, kwargs):
         else:
             return None      # callable grid entries take the full path
     grid = tuple(axes)
-    env = tuple(os.environ.get(k) for k in _ENV_KEYS)
     return (grid, launcher.num_warps, tuple(sorted(kwargs)), tuple(sigs), alias,
-            current_program_range(), env)
+            current_program_range(), _tila_env())
 
 
 def _remember(launcher, key, args, kwargs):
@@ -149,7 +175,30 @@ def _remember(launcher, key, args, kwargs):
     cache = launcher.jf.__dict__.setdefault("_b200_fast", {})
     if len(cache) >= _FAST_MAX:
         cache.clear()
-    cache[key] = (names, scalar_vals, stride_vals, consts, grid)
+    jf = launcher.jf
+    tir = tuple(_statements(jf.tk.body, []))
+    evidence = (getattr(jf, "last_alignment_facts", ()), getattr(jf, "last_race_report", None),
+                getattr(jf, "last_race_details", None))
+    cache[key] = (names, scalar_vals, stride_vals, consts, grid, jf.tk, tir, evidence)
+
+
+def _restore_evidence(jf, evidence):
+    """The checks' evidence of the remembered launch, as the full path would
+    leave it: alignment facts, and the race report as the race cache returns
+    it on a hit (race_policy.py:91, ``cache_status='hit'``)."""
+    facts, race, details = evidence
+    jf.last_alignment_facts = facts
+    if race is not None and getattr(race, "cache_status", None) == "miss":
+        race = dataclasses.replace(race, cache_status="hit")
+    jf.last_race_report = race
+    jf.last_race_details = details
+
+
+def _same_tir(tk, tk_then, stmts_then):
+    if tk is not tk_then:
+        return False
+    now = _statements(tk.body, [])
+    return len(now) == len(stmts_then) and all(a is b for a, b in zip(now, stmts_then))
 
 
 def install():
@@ -180,12 +229,15 @@ def install():
             key = _fast_key(self, args, kwargs)
         except Exception:
             key = None
-        if key is not None:
+        if key is not None and L._execute is _execute:
             hit = self.jf.__dict__.get("_b200_fast", {}).get(key)
+            if hit is not None and not _same_tir(self.jf.tk, hit[5], hit[6]):
+                hit = None
             if hit is not None:
                 global fast_hits
                 fast_hits += 1
-                names, scalar_vals, stride_vals, consts, grid = hit
+                names, scalar_vals, stride_vals, consts, grid = hit[:5]
+                _restore_evidence(self.jf, hit[7])
                 vals = list(args) + [kwargs[k] for k in sorted(kwargs)]
                 from . import backend
                 backend.execute(self, {n: vals[i] for n, i in names.items()}, scalar_vals,
