@@ -142,11 +142,14 @@ class Case:
     that consecutive steps read memory that is not L2-resident), the launches
     of one step, and the metadata for the JSON line."""
 
-    def __init__(self, key, world, rank, device):
+    def __init__(self, key, world, rank, device, strong=False):
         import torch
         import tila_b200
         from tila_b200 import workloads as W
         self.key, self.world, self.rank, self.device = key, world, rank, device
+        # weak scaling: the job is `world` copies of the configuration along
+        # its program axis; strong scaling: one configuration split `world` ways
+        self.mult = 1 if strong else world
         self.W, self.ti, self.torch = W, tila_b200.tila, torch
         self.tila_b200 = tila_b200
         getattr(self, f"_setup_{key}")()
@@ -166,13 +169,14 @@ class Case:
     def _setup_add(self):
         W, torch = self.W, self.torch
         n1 = 1 << 20
-        n = n1 * self.world
+        n = n1 * self.mult
         x, y = W.add_inputs(n, seed=0)
         self.host_inputs = [x, y]
         nset = self._sets(3 * 4 * n1)
         self.sets = [(self._dev(x), self._dev(y), torch.empty(n, device=self.device)) for _ in range(nset)]
         grid = (n // 1024,)
         self.axis, self.grid_axis_total = 0, grid[0]
+        self.rows_per_program = 1024
         self.launches = [lambda s: W.add_kernel[grid](s[0], s[1], s[2], BLOCK=1024)]
         self.kernels = [W.add_kernel]
         self.out_index = 2
@@ -189,13 +193,14 @@ class Case:
     def _setup_softmax(self):
         W, torch = self.W, self.torch
         m1, ncol = 8192, 1000
-        m = m1 * self.world
+        m = m1 * self.mult
         x = W.softmax_inputs(m, ncol, seed=0)
         self.host_inputs = [x]
         nset = self._sets(2 * 4 * m1 * ncol)
         self.sets = [(self._dev(x), torch.empty((m, ncol), device=self.device)) for _ in range(nset)]
         grid = (m,)
         self.axis, self.grid_axis_total = 0, m
+        self.rows_per_program = 1
         self.launches = [lambda s: W.softmax_kernel[grid](s[0], s[1], BN=1024)]
         self.kernels = [W.softmax_kernel]
         self.out_index = 1
@@ -212,7 +217,7 @@ class Case:
     def _setup_matmul(self):
         W, torch = self.W, self.torch
         m1 = 4096
-        m = m1 * self.world
+        m = m1 * self.mult
         a, b = W.matmul_inputs(m, 4096, 4096, seed=0)
         self.host_inputs = [a, b]
         nset = self._sets(2 * 4096 * 4096 * 2 + 4 * 4096 * 4096)
@@ -220,6 +225,7 @@ class Case:
                      for _ in range(nset)]
         grid = (m // 128, 4096 // 128)
         self.axis, self.grid_axis_total = 0, grid[0]
+        self.rows_per_program = 128
         self.launches = [lambda s: W.matmul_kernel[grid](s[0], s[1], s[2], BM=128, BN=128, BK=64)]
         self.kernels = [W.matmul_kernel]
         self.out_index = 2
@@ -239,7 +245,7 @@ class Case:
     def _setup_unfused_attention(self):
         W, torch = self.W, self.torch
         bh1, l, d = 128, 1024, 64
-        bh = bh1 * self.world
+        bh = bh1 * self.mult
         q, k, v = W.attention_inputs(bh, l, d, seed=0)
         self.host_inputs = [q, k, v]
         qg, kg, vg = self._dev(q), self._dev(k), self._dev(v)
@@ -250,6 +256,7 @@ class Case:
         g1, g2, g3 = (l // 128, l // 128, bh), (bh * l,), (l // 128, bh)
         # shard axes: scores by heads (axis 2), softmax by rows (axis 0), pv by heads (axis 1)
         self.multi_shard = [(2, bh), (0, bh * l), (1, bh)]
+        self.grid_axis_total, self.rows_per_program = bh, 1     # the output O: one head per program
         self.launches = [
             lambda st: W.attention_scores[g1](st[0], st[1], st[3], 0.125, BM=128, BN=128, BD=64),
             lambda st: W.softmax_kernel[g2](st[3].view(bh * l, l), st[4].view(bh * l, l), BN=1024),
@@ -287,13 +294,14 @@ class Case:
     def _setup_fused_attention(self):
         W, torch = self.W, self.torch
         bh1, l, d = 128, 4096, 128
-        bh = bh1 * self.world
+        bh = bh1 * self.mult
         q, k, v = W.attention_inputs(bh, l, d, seed=0)
         self.host_inputs = [q, k, v]
         self.sets = [(self._dev(q), self._dev(k), self._dev(v),
                       torch.empty((bh, l, d), device=self.device))]
         grid = (l // 128, bh)
         self.axis, self.grid_axis_total = 1, bh
+        self.rows_per_program = 1
         scale = d ** -0.5
         self.launches = [lambda s: W.fused_attention_kernel[grid](s[0], s[1], s[2], s[3], scale,
                                                            CAUSAL=0, BM=128, BN=128, BD=128)]
@@ -314,13 +322,14 @@ class Case:
     def _setup_fused_attention_causal(self):
         W, torch = self.W, self.torch
         bh1, l, d = 128, 4096, 128
-        bh = bh1 * self.world
+        bh = bh1 * self.mult
         q, k, v = W.attention_inputs(bh, l, d, seed=0)
         self.host_inputs = [q, k, v]
         self.sets = [(self._dev(q), self._dev(k), self._dev(v),
                       torch.empty((bh, l, d), device=self.device))]
         grid = (l // 128, bh)
         self.axis, self.grid_axis_total = 1, bh
+        self.rows_per_program = 1
         scale = d ** -0.5
         # 8 warps: one program per CTA, each row's 128 scores split over two
         # thread halves; two such CTAs share an SM (faster here than pairing
@@ -347,6 +356,12 @@ class Case:
         if getattr(self, "multi_shard", None):
             return [(ax, *self._shard(total)) for ax, total in self.multi_shard]
         return [(self.axis, *self._shard(self.grid_axis_total))] * len(self.launches)
+
+    def gather_rows(self, out):
+        """Leading rows of ``out`` each rank's programs write (the program
+        split of the output's launch, times the rows one program writes)."""
+        from tila_b200.multigpu import shard_rows
+        return shard_rows(self.grid_axis_total, self.rows_per_program, out.shape[0], self.world)
 
     def prepare(self):
         """Launch every step once through the public API (compiling and
@@ -470,8 +485,14 @@ def run_ours(args, world, rank, device, keys):
         if world > 1:
             out = case.sets[0][case.out_index]
             gather_ms = _gather(out, case, world, rank, device)
+        # every timed launch wrote its device errors (bounded-wait timeouts)
+        # into the error block; a run with one is not a measurement
+        errors = case.tila_b200.read_device_errors(device)
+        if errors:
+            from tila_b200.backend import describe_error
+            raise RuntimeError(f"{key}: a timed launch recorded a device error: {describe_error(errors)}")
         entry = {"metric": name, "value": round(value, 3), "unit": unit, "ms_per_step": round(ms_step, 5),
-                 "steps": K, "gpu_launches": K * len(case.launches),
+                 "steps": K, "gpu_launches": K * len(case.launches), "device_errors": 0,
                  "roofline": roof, "config": case.config, "clocks": clocks.summary(),
                  "dtype": case.dtype}
         if key == "unfused_attention":
@@ -488,10 +509,58 @@ def run_ours(args, world, rank, device, keys):
             entry["e2e"] = _e2e(case, args, world, rank, device)
         if rank == 0 and world == 1 and not args.no_cpu:
             entry["cpu_baseline"] = cpu_baseline(key, repeats=1)
+        if gather_ms is not None:
+            # the same steps followed by the gather (weak scaling, the gather
+            # measured above; device times added)
+            entry["with_gather"] = {
+                "value": round(case.units_per_rank * world / ((ms_step + gather_ms) * 1e-3) / scale, 3),
+                "ms_per_step": round(ms_step + gather_ms, 5)}
         results[key] = entry
         del case
         torch.cuda.empty_cache()
+        if world > 1:
+            entry["strong"] = _strong(key, args, world, rank, device)
+            torch.cuda.empty_cache()
     return results
+
+
+def _strong(key, args, world, rank, device):
+    """Strong scaling: the configuration itself (not N copies) split N ways.
+    Each timed step is this rank's share of the launches followed by the NCCL
+    all-gather (C ABI) that leaves the whole output on every rank; device
+    time of K steps with CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from tila_b200.multigpu import gather_leading
+    case = Case(key, world, rank, device, strong=True)
+    case.prepare()
+    comm = _communicator(world, rank, device)
+
+    def step(i):
+        case.step(i)
+        out = case.sets[i % len(case.sets)][case.out_index]
+        gather_leading(out, world, rank, rows=case.gather_rows(out), comm=comm)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize(device)
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    name, unit, scale = case.metric_unit
+    res = {"value": round(case.units_per_rank / (ms * 1e-3) / scale, 3), "unit": unit,
+           "ms_per_step": round(ms, 5), "steps": args.steps, "gather_included": True,
+           "split": f"{case.grid_axis_total} programs of axis {case.axis if not getattr(case, 'multi_shard', None) else 'per launch'} over {world} ranks"}
+    del case
+    return res
 
 
 W_ROOF = {"add": "hbm", "softmax": "hbm", "matmul": "tensor", "unfused_attention": "hbm",
@@ -516,12 +585,13 @@ def _gather(out, case, world, rank, device):
     import torch.distributed as dist
     from tila_b200.multigpu import gather_leading
     comm = _communicator(world, rank, device)
-    gather_leading(out, world, rank, comm=comm)     # first call sets up NCCL's buffers
+    rows = case.gather_rows(out)
+    gather_leading(out, world, rank, rows=rows, comm=comm)     # first call sets up NCCL's buffers
     dist.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    gather_leading(out, world, rank, comm=comm)
+    gather_leading(out, world, rank, rows=rows, comm=comm)
     e1.record()
     torch.cuda.synchronize(device)
     t = torch.tensor([e0.elapsed_time(e1)], device=device)
@@ -746,7 +816,8 @@ def main():
                                l2="inputs rotated across buffer sets larger than L2"),
                 "roofline": head["roofline"], "clocks": head["clocks"],
                 "gpu_launches": head["gpu_launches"]}
-        for k in ("e2e", "cpu_baseline", "gather_ms", "hbm_gbs"):
+        for k in ("e2e", "cpu_baseline", "gather_ms", "with_gather", "strong", "hbm_gbs",
+                  "device_errors"):
             if k in head:
                 line[k] = head[k]
         line["workloads"] = {k: v for k, v in res.items() if k != keys[0]}

@@ -195,6 +195,28 @@ def test_program_range_shards_reproduce_the_full_launch(world):
     assert torch.equal(c_part, c_full)
 
 
+def test_program_shards_write_the_rows_shard_rows_names():
+    """3 matmul tile rows of 128 on 2 ranks (programs [0, 2) and [2, 3)): each
+    rank's launch writes exactly the rows multigpu.shard_rows gives it (0-255
+    and 256-383, not a split of the 384 rows), which is what gather_leading
+    collects."""
+    from tila_b200.multigpu import shard, shard_rows
+    a, b = W.matmul_inputs(384, 256, 128, seed=15)
+    ag, bg = _cuda(a), _cuda(b)
+    full = torch.zeros((384, 256), device="cuda")
+    W.matmul_kernel[(3, 2)](ag, bg, full, BM=128, BN=128, BK=64)
+    rows = shard_rows(3, 128, 384, 2)
+    assert rows == [(0, 256), (256, 384)]
+    for rank, (lo, hi) in enumerate(rows):
+        part = torch.full_like(full, float("nan"))
+        with shard(0, 3, 2, rank):
+            W.matmul_kernel[(3, 2)](ag, bg, part, BM=128, BN=128, BK=64)
+        _no_device_errors()
+        written = ~torch.isnan(part).all(dim=1)
+        assert written.nonzero().flatten().tolist() == list(range(lo, hi))
+        assert torch.equal(part[lo:hi], full[lo:hi])
+
+
 def test_repeated_signature_launches_skip_checks_and_use_new_buffers():
     """A second launch with the same binding signature takes the cached path
     (no re-checking) and reads and writes the new tensors; a different

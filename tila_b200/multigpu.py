@@ -72,22 +72,51 @@ class Communicator:
             self.handle = None
 
 
-def gather_leading(out, world: int, rank: int, group=None, comm: Communicator = None):
+def shard_rows(programs: int, rows_per_program: int, rows: int, world: int):
+    """Leading-dimension rows of the output that each rank's programs write
+    when ``programs`` programs of the sharded axis are split by
+    :func:`shard_range` and program p writes rows
+    ``[p * rows_per_program, (p + 1) * rows_per_program)`` (clipped to
+    ``rows``): one per rank, contiguous, covering ``[0, rows)``.  Example: 3
+    matmul tile rows of 128 on 2 GPUs -> programs [0, 2) and [2, 3) -> rows
+    [0, 256) and [256, 384)."""
+    out = []
+    for r in range(world):
+        lo, hi = shard_range(programs, world, r)
+        out.append((min(lo * rows_per_program, rows), min(hi * rows_per_program, rows)))
+    if out and (out[0][0] != 0 or out[-1][1] != rows):
+        raise ValueError(f"{programs} programs of {rows_per_program} rows do not cover {rows} rows")
+    return out
+
+
+def gather_leading(out, world: int, rank: int, rows=None, group=None, comm: Communicator = None):
     """All-gather the leading-dimension shards of ``out`` in place.
 
-    Rank r owns rows ``shard_range(out.shape[0], world, r)`` of ``out``; after
-    the call every rank holds the full tensor.  Shards may differ in size by
-    one row; they are padded to the largest shard for the collective, which
-    runs through ``comm`` (the C-ABI NCCL communicator) when given, else
-    through ``torch.distributed``.
+    ``rows[r]`` is the ``[lo, hi)`` range of leading rows that rank r wrote
+    (:func:`shard_rows` computes it from the program split); the ranges are
+    contiguous, in rank order, and cover ``out``.  Without ``rows`` the rows
+    are split by :func:`shard_range` (right when each program of the sharded
+    axis writes one leading row).  After the call every rank holds the full
+    tensor.  With ``comm`` (the C-ABI NCCL communicator), a contiguous ``out``
+    and equal shards, the ranks' shards are gathered straight into ``out``
+    (each rank's own rows are its send buffer); otherwise shards are padded
+    to the largest one for the collective, which runs through ``comm`` or
+    ``torch.distributed``.
     """
     import torch
     import torch.distributed as dist
     n = out.shape[0]
-    ranges = [shard_range(n, world, r) for r in range(world)]
-    width = max(hi - lo for lo, hi in ranges)
+    ranges = [tuple(r) for r in rows] if rows is not None else [shard_range(n, world, r) for r in range(world)]
+    if len(ranges) != world or ranges[0][0] != 0 or ranges[-1][1] != n or \
+            any(b != c for (_, b), (c, _) in zip(ranges, ranges[1:])) or any(b < a for a, b in ranges):
+        raise ValueError(f"row ranges {ranges} do not partition {n} rows over {world} ranks")
+    sizes = [b - a for a, b in ranges]
     lo, hi = ranges[rank]
-    send = torch.zeros((width,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
+    if comm is not None and out.is_contiguous() and len(set(sizes)) == 1:
+        comm.all_gather(out[lo:hi], out)
+        return out
+    width = max(sizes)
+    send = torch.empty((width,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
     send[: hi - lo] = out[lo:hi]
     if comm is not None:
         flat = torch.empty((world,) + tuple(send.shape), dtype=out.dtype, device=out.device)
@@ -97,6 +126,6 @@ def gather_leading(out, world: int, rank: int, group=None, comm: Communicator = 
         recv = [torch.empty_like(send) for _ in range(world)]
         dist.all_gather(recv, send, group=group)
     for r, (a, b) in enumerate(ranges):
-        if r != rank:
+        if r != rank and b > a:
             out[a:b] = recv[r][: b - a]
     return out
