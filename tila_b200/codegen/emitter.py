@@ -183,9 +183,15 @@ def resolve_static_ifs(tk, consts):
     known = dict(consts)
     changed = [False]
 
-    def walk(stmts):
+    def walk(stmts, top=False):
         out = []
         for s in stmts:
+            if top and out and isinstance(out[-1], T_.TReturn):
+                # a return spliced in at the top level ends the program: what
+                # follows it never runs (and may not even have matching shapes,
+                # being typed for the branch that does not return)
+                changed[0] = True
+                break
             if isinstance(s, T_.TStaticIf):
                 try:
                     taken = bool(ev(s.cond, known))
@@ -196,7 +202,7 @@ def resolve_static_ifs(tk, consts):
                                                    else_body=walk(s.else_body)))
                 else:
                     changed[0] = True
-                    out.extend(walk(s.then_body if taken else s.else_body))
+                    out.extend(walk(s.then_body if taken else s.else_body, top))
                 continue
             if isinstance(s, T_.TAssign) and counts.get(s.name) == 1 and s.name not in known:
                 try:
@@ -209,7 +215,7 @@ def resolve_static_ifs(tk, consts):
                 s = dataclasses.replace(s, body=walk(s.body))
             out.append(s)
         return out
-    body = walk(tk.body)
+    body = walk(tk.body, top=True)
     return dataclasses.replace(tk, body=body) if changed[0] else tk
 
 
@@ -752,6 +758,16 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     def e_TCast(self, x):
         v = self.value(x.operand)
         dst = x.dtype
+        op = x.operand
+        if DT.is_int(dst) and v.kind == "scalar" and type(v.const) is int and (
+                isinstance(op, T_.TLit) and type(op.value) is int
+                or isinstance(op, T_.TName) and op.name in self.consts
+                or isinstance(op, (T_.TBin, T_.TUna)) and getattr(op, "staged", False)):
+            # an integer literal, Const or staged constant converts by its exact
+            # value modulo 2^bits, not through the dtype the literal carries
+            # (cast[i64](-4294967296) is -4294967296; lowering.py:506-510 folds
+            # the same way before the tensor conversion)
+            return Val("scalar", dst, expr=DT.int_literal(dst, v.const), const=v.const)
         if v.kind == "scalar":
             return Val("scalar", dst, expr=DT.convert(v.dt, dst, v.expr))
         if v.kind == "func":
@@ -847,6 +863,14 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             self.fail(f"unsupported unary op {op}")
         return self.combine(dt, shape, [v], mk)
 
+    @staticmethod
+    def _has_effects(node):
+        """``node`` contains an atomic or a memory load (evaluating it is observable)."""
+        from .pipeline import _walk
+        found = [False]
+        _walk(node, lambda n: found.__setitem__(0, found[0] or isinstance(n, (T_.TAtomicAdd, T_.TLoad))))
+        return found[0]
+
     def e_TBin(self, x):
         dt, shape, is_ptr = self.vt_info(x.vt)
         op = x.op
@@ -859,6 +883,23 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                 return Val("scalar", D.bool_, expr="false", const=False)
             if op == "or" and l.const:
                 return Val("scalar", D.bool_, expr="true", const=True)
+        if op in ("and", "or") and l.kind == "scalar" and not shape and self._has_effects(x.right):
+            # Python's short circuit: the right operand (an atomic, a load)
+            # runs only when the left one does not decide the result.  The
+            # left operand is uniform, so every thread takes the same branch.
+            v = self.fresh("sc")
+            self.emit(f"bool {v} = ({l.expr});")
+            self.emit(f"if ({'' if op == 'and' else '!'}{v}) {{")
+            self.indent += 1
+            saved_conv = dict(self.conv_cache)      # values made inside the block stay there
+            r = self.value(x.right)
+            if r.kind != "scalar":
+                self.fail("short-circuit operand is not a scalar", getattr(x, "line", 0))
+            self.emit(f"{v} = ({r.expr});")
+            self.conv_cache = saved_conv
+            self.indent -= 1
+            self.emit("}")
+            return Val("scalar", D.bool_, expr=v)
         r = self.value(x.right)
         if is_ptr:
             self.fail("pointer arithmetic tiles are not supported yet")
@@ -2224,7 +2265,7 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
     def _declare_merged(self, names, ends):
         storage = {}
         for n in names:
-            a, b = ends
+            a, b = ends[0][n], ends[1][n]
             cur = self.env[n]
             proto = self._carried_val(cur, a if a.kind == "reg" else b, n)
             var = self.fresh(f"m_{n}")

@@ -57,14 +57,27 @@ __device__ __forceinline__ void report_error(u32 *err, u32 code, u32 where) {
 // dtype semantics
 // ---------------------------------------------------------------------------
 
+// f16 <-> f32 with NumPy's NaN handling (npy_halfbits_to_floatbits and
+// npy_floatbits_to_halfbits): a NaN keeps its sign and the top bits of its
+// payload, so a half value that only moves through f32 (a copy, a reshape)
+// comes back bit for bit.
 __device__ __forceinline__ float h2f(u16 h) {
   float f;
   asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  if ((h & 0x7FFFu) > 0x7C00u)
+    f = __uint_as_float((static_cast<u32>(h & 0x8000u) << 16) | 0x7F800000u |
+                        (static_cast<u32>(h & 0x3FFu) << 13));
   return f;
 }
 __device__ __forceinline__ u16 f2h(float f) {
   u16 h;
   asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  const u32 b = __float_as_uint(f);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) {
+    u32 r = 0x7C00u + ((b & 0x7FFFFFu) >> 13);
+    if (r == 0x7C00u) r += 1u;               // a payload below the kept bits stays a NaN
+    h = static_cast<u16>(((b >> 16) & 0x8000u) | r);
+  }
   return h;
 }
 __device__ __forceinline__ u16 d2h(double d) {
@@ -75,9 +88,17 @@ __device__ __forceinline__ u16 d2h(double d) {
 __device__ __forceinline__ float bf2f(u16 h) {
   return __uint_as_float(static_cast<u32>(h) << 16);
 }
+// f32 -> bf16, round to nearest even; a NaN keeps its sign and the top bits of
+// its payload (a bf16 value that only moves through f32 comes back bit for bit).
 __device__ __forceinline__ u16 f2bf(float f) {
   u16 h;
   asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  const u32 b = __float_as_uint(f);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) {
+    u32 r = b >> 16;
+    if ((r & 0x7Fu) == 0u) r |= 0x40u;      // a payload below the kept bits stays a NaN
+    h = static_cast<u16>(r);
+  }
   return h;
 }
 __device__ __forceinline__ u16 d2bf(double d) {
