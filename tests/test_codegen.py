@@ -75,12 +75,41 @@ def test_reference_fused_attention_takes_two_program_plan(causal):
     """examples/fused_attention.py puts each of its loops inside ``if CAUSAL
     == 1: ... else:``; the static if is resolved per specialisation before
     the loop matchers run, so at 128x128 tiles the loop of the taken branch
-    gets the two-programs-per-CTA plan (256 threads, one 128-row program per
-    warpgroup)."""
+    runs two 128-row programs per CTA.  The non-causal loop (same trip count
+    for both programs) gets the warp-specialised form: two softmax
+    warpgroups plus a producer warpgroup that issues every copy and MMA;
+    the causal one keeps the hand-off between the two programs."""
     q = torch.zeros(2, 512, 128, dtype=f16)
     spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
                CAUSAL=causal, BM=128, BN=128, BD=128)
-    assert spec.fuse == {0: 2} and spec.threads == 256 and spec.tmem_cols == 512
+    assert spec.fuse == {0: 2} and spec.tmem_cols == 512
+    if causal:
+        assert spec.threads == 256 and spec.launch_regs == 0
+    else:
+        assert spec.threads == 384 and spec.launch_regs == 168
+        assert "tila::reg_alloc<232>()" in spec.source and "tila::reg_dealloc<40>()" in spec.source
+
+
+def test_warp_specialised_kernel_register_budget(tmp_path):
+    """The warpgroups of the warp-specialised kernel trade registers within
+    the pool the CTA is launched with (384 threads x 168): ptxas must give the
+    kernel exactly 168 registers per thread at launch."""
+    import re
+    import shutil
+    import subprocess
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    q = torch.zeros(2, 512, 128, dtype=f16)
+    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+               CAUSAL=0, BM=128, BN=128, BD=128)
+    cu = tmp_path / "ws.cu"
+    cu.write_text(spec.source)
+    from tila_b200 import build
+    out = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-Xptxas", "-v",
+                          f"-I{build.PKG / 'csrc' / 'tile'}", "-c", str(cu), "-o", str(tmp_path / "ws.o")],
+                         capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr[-2000:]
+    regs = re.findall(r"Used (\d+) registers", out.stderr)
+    assert regs and int(regs[-1]) == spec.launch_regs == 168
 
 
 def test_static_if_resolution_leaves_kernel_untouched():

@@ -292,6 +292,13 @@ def preflight(entry: Compiled, context) -> dict:
     if spec.threads > attrs["max_threads_per_block"]:
         raise _failure(RuntimeError("threads"), "resources", spec.source, context,
                        resource=("threads", spec.threads, attrs["max_threads_per_block"]))
+    if spec.launch_regs and attrs["registers_per_thread"] != spec.launch_regs:
+        # the kernel's warpgroups trade registers (setmaxnreg) within a pool of
+        # threads x launch registers; any other count could leave a warpgroup
+        # waiting for registers that do not exist, so it is never launched
+        raise _failure(RuntimeError("registers"), "resources", spec.source, context,
+                       resource=("registers per thread at launch", spec.launch_regs,
+                                 attrs["registers_per_thread"]))
     return {"shared_bytes": spec.smem_bytes + attrs["static_smem_bytes"],
             "shared_limit_bytes": limit + attrs["static_smem_bytes"],
             "threads": spec.threads, "max_threads": attrs["max_threads_per_block"],

@@ -33,6 +33,7 @@ into the TMEM-row layout.
 
 from __future__ import annotations
 
+import os
 import re
 
 import dataclasses
@@ -47,6 +48,7 @@ from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_pr
                       source_slot_map)
 from .fused import FusedContractionMixin
 from .mma import AsyncLoopMixin, MmaMixin
+from .wspec import WS_REGS_CONSUMER, WS_REGS_LAUNCH, WS_REGS_PRODUCER, WS_THREADS, WarpSpecMixin
 
 T_ = tila.tir
 TY = tila.types
@@ -124,6 +126,9 @@ class KernelSpec:
     fp_contract: bool = False
     # Tila lines of the ti.assume checks compiled in (TILA_DEBUG=1 builds)
     assume_lines: list = field(default_factory=list)
+    # registers per thread the kernel must have been given at launch (kernels
+    # that move registers between warpgroups with setmaxnreg); 0 = any
+    launch_regs: int = 0
 
 
 # ---------------------------------------------------------------------------
@@ -244,13 +249,18 @@ class _Smem:
 # the emitter
 # ---------------------------------------------------------------------------
 
-class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
+class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMixin):
     MAX_SCRATCH = 96 * 1024
 
     def __init__(self, tk, consts: dict, buffers: dict, num_warps: int = 4,
-                 entry_name=None, debug=False, versioning=True, source_map=False):
+                 entry_name=None, debug=False, versioning=True, source_map=False, ws=None):
         tk = resolve_static_ifs(tk, consts)
         self.tk = tk
+        self._num_warps = num_warps
+        # warp-specialised attention loop (see wspec.py): None, or the plan the
+        # first generation found ({"q": name of the loop's one-shot operand})
+        self._ws = dict(ws) if ws else None
+        self._ws_found = None
         self.source_map = source_map     # annotate the output with Tila source lines
         self.versioning = versioning     # loop bodies specialised for interior tiles
         self.consts = dict(consts)
@@ -2365,6 +2375,19 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
         wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
               and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3
               and not self._assume_lines)
+        if wg and self._ws_found is not None and self._ws is None \
+                and os.environ.get("TILA_B200_WS", "1") != "0":
+            # the loop has the flash-attention shape: generate the
+            # warp-specialised kernel instead (this pass's plan is the fallback)
+            try:
+                return KernelEmitter(self.tk, self.consts, self.buffers, num_warps=self._num_warps,
+                                     entry_name=self.entry, debug=self.debug,
+                                     versioning=self.versioning, source_map=self.source_map,
+                                     ws=self._ws_found).generate()
+            except CodegenError:
+                pass
+        if self._ws is not None and not wg:
+            self.fail("warp-specialised loop: two programs per CTA do not fit")
         if wg:
             self.fuse = {0: 2}
         for ax in sorted(self.fuse or {}):
@@ -2375,6 +2398,9 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
             params.append(("tensormap", tm["param"], tm))
         threads = 2 * self.T if wg else self.T
         cta_cols = 2 * self.tmem_cols if wg else self.tmem_cols
+        if self._ws is not None:
+            return self._ws_generate(sig, params, per_prog, body, scratch_off, red_off, scratch_col,
+                                     cta_cols)
         out = ['#include "tila_tile.cuh"', ""]
         # f32 exp2: tensor-core kernels (compared within a tolerance, compiled
         # with multiply-add contraction) use the flush-to-zero form, which
@@ -2508,6 +2534,106 @@ class KernelEmitter(FusedContractionMixin, AsyncLoopMixin, MmaMixin):
                           assume_lines=list(self._assume_lines),
                           tmem_cols=self.tmem_cols,
                           tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
+
+
+def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, scratch_col, cta_cols):
+    """Kernel text of the warp-specialised two-program kernel (wspec.py):
+    warpgroups 0 and 1 run the consumer body of programs 2 * blockIdx.x + w,
+    thread 256 the producer."""
+    from .mma import WG_ACQUIRE, WG_RELEASE, WG_TRIPS, WG_TURNS
+    from .wspec import RING
+    ring_off = -(-(2 * per_prog) // 1024) * 1024
+    kp, vp = self._ws["k"], self._ws["v"]
+    ring_bytes = RING * sum(c["plan"].nbox * max(c["plan"].outer_extent, 128) * 128 for c in (kp, vp))
+    bars_off = ring_off + ring_bytes
+    prod, nbars, _ = self.ws_producer(per_prog, ring_off, bars_off, scratch_col)
+    dead_off = bars_off + 8 * nbars
+    total = dead_off + 16
+    if total > 232448:
+        self.fail(f"warp-specialised kernel needs {total} bytes of shared memory")
+    out = ['#include "tila_tile.cuh"', "",
+           "#define tila_exp2_f32 tila::" + ("exp2_ftz" if self.uses_mma else "exp2_fast"), "",
+           f'extern "C" __global__ void __launch_bounds__({WS_THREADS}, 1) {self.entry}(',
+           ",\n".join("    " + x for x in sig) + ") {"]
+    e = out.append
+    e("  extern __shared__ __align__(1024) unsigned char tila_smem_all[];")
+    e("  // warpgroups 0 and 1: programs 2*blockIdx.x + w (softmax side); thread 256 (warpgroup 2): copies and MMAs")
+    e("  const bool tila_producer = threadIdx.x >= 256;")
+    e("  const int tila_wg = tila_producer ? 0 : (int)(threadIdx.x >> 7);")
+    e("  const int tid = threadIdx.x & 127;")
+    e(f"  unsigned char* const tila_smem = tila_smem_all + tila_wg * {per_prog};")
+    e("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + tila_wg + pid_off_0);")
+    e("  const bool tila_live = !tila_producer && (tila::i32)(blockIdx.x * 2 + tila_wg) < launch_0;")
+    e("  const tila::i32 pid_1 = (tila::i32)(blockIdx.y + pid_off_1);")
+    e("  const tila::i32 pid_2 = (tila::i32)(blockIdx.z + pid_off_2);")
+    e("  (void)pid_0; (void)pid_1; (void)pid_2;")
+    e("  const tila::u32 tila_sb4 = tila::smem_u32(tila_smem) >> 4; (void)tila_sb4;")
+    e("  tila::u64* tila_mma_bar = reinterpret_cast<tila::u64*>(tila_smem);")
+    e("  tila::u32* tila_tmem_slot = reinterpret_cast<tila::u32*>(tila_smem_all + 8);")
+    e(f"  volatile int& tila_dead = *reinterpret_cast<volatile int*>(tila_smem_all + {dead_off});")
+    e(f"  unsigned char* tila_scratch = tila_smem + {scratch_off};")
+    e("  (void)tila_scratch; (void)tila_mma_bar; (void)tila_tmem_slot;")
+    if self.smem.red:
+        e(f"  unsigned char* const tila_red = tila_smem + {red_off};")
+        e(f"  constexpr tila::u32 tila_red_half = {self.smem.red};")
+        e("  tila::u32 tila_rsel = 0;")
+    e("  tila::u32 tila_mma_phase = 0; (void)tila_mma_phase;")
+    for v in self._phase_vars:
+        e(f"  tila::u32 {v} = 0;")
+    q = self._ws["q_load"]
+    per_region = [(0, 1), (q["bar_off"], 1), (self._ws["acc_bar"], 1), (self._ws["p_full"], 128)]
+    per_region += [(o, 1) for o in self._need_barrier_init]
+    inits = " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem_all + {w * per_prog + o}), {c});"
+                     for w in range(2) for o, c in per_region)
+    inits += " " + " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem_all + {bars_off + 8 * i}), 1);"
+                            for i in range(nbars))
+    e(f"  if (threadIdx.x == 0) {{ {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
+    for tm in self.tensor_maps:
+        e(f"  if (threadIdx.x == 0) tila::tma_prefetch_desc(&{tm['param']});")
+    if self._prefetch:
+        e("  if (tila_live) {")
+        for code in self._prefetch:
+            out.extend("    " + ln for ln in code.split("\n"))
+        e("  }")
+    e("  tila::grid_dep_wait();")
+    e("  tila::grid_dep_release();")
+    e(f"  if (threadIdx.x < 32) tila::tmem_alloc(tila_tmem_slot, {cta_cols});")
+    e("  tila::tc_fence_before();")
+    e("  __syncthreads();")
+    e("  tila::tc_fence_after();")
+    e(f"  const tila::u32 tila_tmem = *tila_tmem_slot + (tila::u32)(tila_wg * {self.tmem_cols});")
+    e(f"  const tila::u32 tila_tmem_scratch_col = {scratch_col}; (void)tila_tmem_scratch_col;")
+    e("  if (tila_producer) {")
+    e(f"    tila::reg_dealloc<{WS_REGS_PRODUCER}>();")
+    e("    if (threadIdx.x == 256) {")
+    e("    const tila::u32 tila_tmem_base = *tila_tmem_slot;")
+    out.extend("  " + ln for ln in prod)
+    e("    }")
+    e("    __syncwarp();   // the producer warp reconverges before the final barrier")
+    e("  } else {")
+    e(f"  tila::reg_alloc<{WS_REGS_CONSUMER}>();")
+    e("  do {")
+    e("    if (!tila_live) break;")
+    for line in body:
+        st = line.strip()
+        if st in (WG_ACQUIRE, WG_RELEASE) or st.startswith((WG_TRIPS, WG_TURNS)):
+            continue
+        out.append(line.replace("__syncthreads();", "tila::wg_sync(tila_wg);"))
+    e("  } while (0);")
+    e("  }")
+    e("  tila::tc_fence_before();")
+    e("  __syncthreads();")
+    e(f"  if (threadIdx.x < 32) tila::tmem_dealloc(*tila_tmem_slot, {cta_cols});")
+    e("}")
+    src = "\n".join(out) + "\n"
+    self.fuse = {0: 2}
+    tmem_cols = cta_cols
+    return KernelSpec(self.entry, src, WS_THREADS, max(total, 233472 // 2 - 1024 + 1), params,
+                      fp_contract=True, assume_lines=list(self._assume_lines), tmem_cols=tmem_cols,
+                      tensor_maps=list(self.tensor_maps), fuse={0: 2}, launch_regs=WS_REGS_LAUNCH)
+
+
+KernelEmitter._ws_generate = _ws_generate_impl
 
 
 class _PackedBin:

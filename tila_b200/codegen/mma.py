@@ -146,6 +146,8 @@ class MmaMixin:
         coords = [self.value(c) for c in x.coords]
         if any(c.kind not in ("scalar", "func") for c in coords):
             return None
+        if self._ws is not None and assigned_name == self._ws["q"]:
+            return self.ws_oneshot(x, assigned_name, plan, coords)
         size = plan.nbox * max(plan.outer_extent, 128) * 128
         off = self.smem.alloc(size, 1024)
         bar_off = self.smem.alloc(8, 8)
@@ -213,6 +215,8 @@ class MmaMixin:
     def e_TDot(self, x):
         dt, shape, _ = self.vt_info(x.vt)
         ctx = self.actx
+        if ctx is not None and getattr(ctx, "ws", False) and x.acc is None:
+            return self.ws_sync_dot(x)
         # In an asynchronous loop whose synchronous dot reads two TMA tiles,
         # that dot's MMAs for the next iteration are issued right behind the
         # accumulating dot (see emit_async_acc_dot); tila_s_pre records it.
@@ -645,6 +649,8 @@ class AsyncLoopMixin:
         al = match_async_loop(s, self.pdefs, is_tma, is_smem, carried, acc_ok, is_cast_tma)
         if al is None:
             return None
+        if self._ws is not None:
+            return self.ws_loop_setup(s, start, end, stepv, al)
         # B operands must be laid out for an N that the instruction accepts
         for name, dot in al.accs.items():
             _, (M, N), _ = self.vt_info(dot.vt)
@@ -740,6 +746,7 @@ class AsyncLoopMixin:
                 self.emit(f"const tila::i64 tila_trip_{k} = ((tila::i64)({end.expr}) > (tila::i64)({start.expr})) ? "
                           f"((tila::i64)({end.expr}) - (tila::i64)({start.expr}) + {stepv - 1}) / {stepv} : 0;")
                 self.emit(f"{WG_TRIPS} {k}")
+        self.ws_detect(s, al, ctx)
         self.actx = ctx
         return ctx
 
@@ -904,7 +911,7 @@ class AsyncLoopMixin:
     def _emit_loop_copies(self, ctx, names, iter_value):
         """tid 0 issues the TMA copies of ``names`` for loop value ``iter_value``;
         every thread marks them not yet waited for."""
-        if not names:
+        if not names or getattr(ctx, "ws", False):
             return
         saved = dict(self.env)
         self.emit("{")
@@ -974,6 +981,8 @@ class AsyncLoopMixin:
         """acc = dot(a, b, acc=acc) with acc in TMEM: issue and leave pending."""
         from .emitter import Val
         ctx = self.actx
+        if getattr(ctx, "ws", False):
+            return self.ws_acc_dot(x, name)
         a = ctx.accs[name]
         N = a["N"]
         # the previous accumulation and any TS operand reader must be finished
@@ -1168,9 +1177,11 @@ class AsyncLoopMixin:
             self.emit(f"{WG_TURNS} {ctx.turns}")
         for name in ctx.accs:
             self.emit_acc_wait(name, release=False)
+        if getattr(ctx, "ws", False):
+            self.ws_finish(ctx)
         # all loop copies were consumed (the last iteration issues none)
         spans = [(int(x["base"]), x["plan"].nbox * max(x["plan"].outer_extent, 128) * 128)
-                 for x in ctx.loads.values()]
+                 for x in ctx.loads.values() if x["base"] is not None]
         if spans:
             lo = min(b for b, _ in spans)
             hi = max(b + n for b, n in spans)

@@ -1,0 +1,421 @@
+"""Warp-specialised lowering of the online-softmax attention loop.
+
+Applies to the asynchronous accumulator loops that already run two programs
+per CTA (one per warpgroup, see ``AsyncLoopMixin._pingpong_ok``) when the loop
+has exactly the flash-attention shape: one synchronous dot ``S = dot(Q, K)``
+whose A operand is a one-shot TMA tile loaded before the loop and whose B
+operand is an in-loop TMA tile, and one accumulating dot
+``acc = dot(cast[f16](P), V, acc=acc)`` with V an in-loop TMA tile, the same
+trip count for both programs (examples/fused_attention.py:104-126, the
+CAUSAL=0 loop).
+
+The CTA then has three roles instead of two programs that each issue their own
+copies and MMAs:
+
+* warpgroups 0 and 1 run programs ``2 * blockIdx.x + w`` as before, but only
+  the CUDA-core part of each iteration: wait for S in tensor memory, compute
+  the softmax update, rescale the accumulator in place, store P (f16) into
+  tensor memory and arrive on the program's "P ready" barrier;
+* one producer thread (256, in the third warpgroup, whose other warps idle)
+  loads both programs' Q
+  tiles once and streams K and V through a two-stage ring shared by the two
+  programs (each tile crosses L2 once per CTA instead of once per program),
+  and issues every ``tcgen05.mma``: for each program in turn P@V of iteration
+  j, then S of iteration j + 1, so the tensor pipe always holds the other
+  program's work while one program is in its softmax;
+* the two softmax warpgroups are no longer serialised by a hand-off: both
+  run concurrently (two warps per SM sub-partition during the exponentials).
+
+Barriers (all waits bounded, see ``tila::mbar_wait``): per program the S
+barrier (``tila_mma_bar``, committed by the producer after S), the
+accumulator barrier (committed after P@V) and the "P ready" barrier (128
+consumer arrivals); per ring stage K/V "full" (TMA transaction count) and
+"empty" (committed after the MMAs that read the stage).  ``tcgen05.mma``
+operations of one thread execute in issue order, so S(j + 1), issued after
+P@V(j), overwrites the tensor-memory columns that P@V(j) reads only after
+that MMA consumed them, and a consumer that has waited for S(j + 1) knows that
+P@V(j) is complete.
+
+The producer's code is built from the same TMA plans, descriptors and
+coordinate expressions as the consumer's would be; a coordinate that depends
+on anything but the program ids, kernel parameters and the loop variable makes
+the kernel fall back to the two-program lowering.
+"""
+
+from __future__ import annotations
+
+import re
+
+from .._reference import tila
+
+T_ = tila.tir
+D = tila.dtypes
+
+WS_THREADS = 384           # two consumer warpgroups + the producer warpgroup
+RING = 2                   # stages of the K and V rings
+# Register budgets.  __launch_bounds__(384, 1) gives every thread 168 registers
+# at launch (65536 / 384 rounded down to a multiple of 8), a pool of
+# 384 x 168 = 64512.  The producer warpgroup gives back all but 40 and the two
+# consumer warpgroups take 232 each: 128 x 40 + 256 x 232 = 64512, exactly the
+# pool, so reg_alloc never waits for registers that do not exist.  The host
+# refuses to launch the kernel unless ptxas allocated exactly WS_REGS_LAUNCH.
+WS_REGS_LAUNCH = 168
+WS_REGS_PRODUCER = 40
+WS_REGS_CONSUMER = 232
+assert 128 * WS_REGS_PRODUCER + 256 * WS_REGS_CONSUMER <= WS_THREADS * WS_REGS_LAUNCH
+assert WS_REGS_LAUNCH == (65536 // WS_THREADS) // 8 * 8
+
+_IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")
+_ALLOWED = {"pid_0", "pid_1", "pid_2", "tila_pit", "int", "long", "unsigned", "float", "double",
+            "true", "false", "LL", "ULL", "u", "ull"}
+
+
+def _portable(expr: str) -> bool:
+    """``expr`` reads only program ids, kernel parameters, the producer's loop
+    variable, literals and tila:: helpers (so it means the same in the
+    producer warp as in a consumer)."""
+    stripped = re.sub(r"tila::[A-Za-z0-9_:<>]+", " ", expr)
+    stripped = re.sub(r"\b(0x[0-9a-fA-F]+|\d+)[uUlL]*\b", " ", stripped)
+    for ident in _IDENT.findall(stripped):
+        if ident in _ALLOWED or ident.startswith(("p_", "nprog_", "pid_off_")):
+            continue
+        return False
+    return True
+
+
+class WarpSpecMixin:
+    """Mixed into :class:`tila_b200.codegen.emitter.KernelEmitter`."""
+
+    # -- first pass: is the loop of the warp-specialised shape? ------------------
+
+    def ws_detect(self, s, al, ctx):
+        """Record the one-shot operand of the loop's synchronous dot when the
+        two-program loop has the flash-attention shape (see module doc)."""
+        from .pipeline import _walk
+        if not getattr(ctx, "pingpong", False) or ctx.turns is not None:
+            return
+        if al.cast_loads or len(al.loads) != 2 or len(al.accs) != 1:
+            return
+        (acc_name, acc_dot), = al.accs.items()
+        if not (isinstance(acc_dot.a, T_.TCast) and isinstance(acc_dot.a.operand, T_.TName)
+                and acc_dot.a.operand.name not in al.loads):
+            return
+        syncs = []
+        for st in s.body:
+            _walk(st.value, lambda n: syncs.append(n) if isinstance(n, T_.TDot) and n.acc is None else None)
+        if len(syncs) != 1:
+            return
+        sd = syncs[0]
+        if not (isinstance(sd.a, T_.TName) and isinstance(sd.b, T_.TName) and sd.b.name in al.loads
+                and sd.b.name != acc_dot.b.name):
+            return
+        q = self.env.get(sd.a.name)
+        op = getattr(q, "smem", None)
+        if q is None or q.kind != "smem" or op is None or op.bar is None or not op.nbytes:
+            return
+        if len(self.uses.get(sd.a.name, [])) != 1:
+            return
+        _, (M, N), _ = self.vt_info(sd.vt)
+        if M != 128 or self.vt_info(acc_dot.vt)[1][0] != 128:
+            return
+        self._ws_found = {"q": sd.a.name}
+
+    # -- second pass: the consumer side --------------------------------------------
+
+    def ws_oneshot(self, x, assigned_name, plan, coords):
+        """The Q tile: shared memory and a barrier in the program's region; the
+        producer copies it, the consumers never touch it."""
+        size = plan.nbox * max(plan.outer_extent, 128) * 128
+        off = self.smem.alloc(size, 1024)
+        bar_off = self.smem.alloc(8, 8)
+        coords_if = self._tma_coords(plan, coords)
+        if not all(_portable(c) for c in coords_if):
+            self.fail("warp-specialised loop: the Q copy depends on program-local values")
+        self._ws["q_load"] = dict(plan=plan, coords=coords_if, off=off, bar_off=bar_off, size=size)
+        self.tensor_map_param(plan)        # a kernel parameter of the producer's copies
+        from .mma import SmemOperand
+        dt, shape, _ = self.vt_info(x.vt)
+        v = self._smem_val(dt, shape, SmemOperand(plan, str(off), None, "0u", None, nbytes=size))
+        return v
+
+    def ws_loop_setup(self, s, start, end, stepv, al):
+        from .emitter import Val
+        from .layouts import TmemRows
+        from .mma import AsyncCtx, SmemOperand
+        from .pipeline import _walk
+        ws = self._ws
+        if "q_load" not in ws or ws.get("loop_done"):
+            self.fail("warp-specialised loop: unexpected loop structure")
+        ws["loop_done"] = True
+        self.uses_mma = True
+        self.uses_tmem = True
+        ctx = AsyncCtx(al, s.var, stepv, f"(tila::i64)({end.expr})", {}, {})
+        ctx.body = s.body
+        ctx.cast_loads = set()
+        ctx.p_early_after = self._early_p_points(s.body, al)
+        ctx.p_early = False
+        ctx.pingpong = False
+        ctx.turns = None
+        ctx.ws = True
+        (acc_name, acc_dot), = al.accs.items()
+        syncs = []
+        for st in s.body:
+            _walk(st.value, lambda n: syncs.append(n) if isinstance(n, T_.TDot) and n.acc is None else None)
+        sd = syncs[0]
+        if sd.a.name != ws["q"]:
+            self.fail("warp-specialised loop: unexpected synchronous dot")
+        k_name, v_name = sd.b.name, acc_dot.b.name
+        for name, ld in al.loads.items():
+            ctx.loads[name] = dict(plan=self.tma_plan(ld), node=ld, base=None, bar=None,
+                                   phase=None, flag=None)
+        _, (M, N), _ = self.vt_info(acc_dot.vt)
+        col = self.tmem_alloc_cols(N)
+        self._loop_acc_cols.add((str(col), N))
+        bar_off = self.smem.alloc(8, 8)
+        ctx.accs[acc_name] = dict(col=col, N=N, bar_off=bar_off,
+                                  bar=f"reinterpret_cast<tila::u64*>(tila_smem + {bar_off})",
+                                  phase=self._tma_state_var(f"tila_ph_{bar_off}"),
+                                  pend=self._tma_state_var(f"tila_p_{bar_off}"),
+                                  releases=[], dot=acc_dot)
+        p_full = self.smem.alloc(8, 8)
+        ctx.p_full_off = p_full
+        K_pv = self.vt_info(acc_dot.a.vt)[1][1]
+        self.tmem_scratch_need = max(self.tmem_scratch_need, K_pv // 2)
+        # the accumulator's initial value into tensor memory
+        pre = self.env[acc_name]
+        lay = TmemRows((128, N), self.T)
+        if pre.kind == "tmem":
+            pre = self.tmem_to_reg(pre)
+        if pre.dt.name != "f32":
+            pre = self.coerce(pre, D.f32)
+        if pre.kind == "scalar":
+            pre = self.materialize_elementwise(D.f32, (128, N), [pre], lambda e: e[0], layout=lay)
+        pre = self.materialize(pre, lay)
+        self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {col} + ((tid & 96u) << 16), {pre.name});")
+        self.emit(f"// warp-specialised loop over {s.var}: S from the producer warp, P handed back "
+                  f"through tensor memory, {acc_name} accumulated in tensor memory")
+        a = ctx.accs[acc_name]
+        self.emit(f"{a['phase']} = 0u; {a['pend']} = 0u;")
+        self.env[acc_name] = Val("tmem", D.f32, (128, N), tmem_col=str(col))
+        # producer templates: TMA copies of K and V for loop value tila_pit
+        saved_env, saved_lines, saved_indent = dict(self.env), self.lines, self.indent
+        self.lines, self.indent = [], 0
+        try:
+            self._functional_prefix(ctx, "tila_pit")
+            copies = {}
+            for name in (k_name, v_name):
+                x = ctx.loads[name]
+                coords = [self.value(c) for c in x["node"].coords]
+                copies[name] = dict(plan=x["plan"], coords=self._tma_coords(x["plan"], coords))
+                self.tensor_map_param(x["plan"])
+            stray = [ln for ln in self.lines if ln.strip()]
+        finally:
+            self.env, self.lines, self.indent = saved_env, saved_lines, saved_indent
+        if stray or not all(_portable(c) for cp in copies.values() for c in cp["coords"]):
+            self.fail("warp-specialised loop: K/V copies depend on program-local values")
+        for e in (start.expr, end.expr):
+            if not _portable(e):
+                self.fail("warp-specialised loop: loop bounds depend on program-local values")
+        # MMA templates (@QB@, @KB@, @VB@: byte offsets in the CTA's shared memory)
+        q = ws["q_load"]
+        qv = self._smem_val(D.f16, q["plan"].shape, SmemOperand(q["plan"], "@QB@"))
+        kv = self._smem_val(D.f16, copies[k_name]["plan"].shape, SmemOperand(copies[k_name]["plan"], "@KB@"))
+        vv = self._smem_val(D.f16, copies[v_name]["plan"].shape, SmemOperand(copies[v_name]["plan"], "@VB@"))
+        _, (Ms, Ns), _ = self.vt_info(sd.vt)
+        Ks = q["plan"].shape[1] if q["plan"].inner == 1 else q["plan"].shape[0]
+        Npad = max(16, Ns)
+        self.tmem_scratch_need = max(self.tmem_scratch_need, Npad)
+        s_mma = []
+        a_mn = self._operand_desc(qv, "A", 0)[1]
+        b_mn = self._operand_desc(kv, "B", 0)[1]
+        for kk in range(Ks // 16):
+            da, _ = self._operand_desc(qv, "A", kk)
+            db, _ = self._operand_desc(kv, "B", kk)
+            s_mma.append(f"tila::mma_f16_ss(@TM@ + @SCOL@, {da}, {db}, "
+                         f"tila::idesc_f16_f32(128, {Npad}, {a_mn}, {b_mn}), {'1u' if kk else '0u'});")
+        pv_mma = []
+        vb_mn = self._operand_desc(vv, "B", 0)[1]
+        for kk in range(K_pv // 16):
+            db, _ = self._operand_desc(vv, "B", kk)
+            pv_mma.append(f"tila::mma_f16_ts(@TM@ + {col}, @TM@ + @SCOL@ + {kk * 8}, {db}, "
+                          f"tila::idesc_f16_f32(128, {N}, 0, {vb_mn}), 1u);")
+        ws.update(k=copies[k_name], v=copies[v_name], s_mma=s_mma, pv_mma=pv_mma,
+                  start=start.expr, end=end.expr, step=stepv, acc_bar=bar_off, p_full=p_full,
+                  acc_col=col)
+        self._wg_candidate = True
+        self.actx = ctx
+        return ctx
+
+    def ws_sync_dot(self, x):
+        """S = dot(Q, K) of the warp-specialised loop: the producer issued it
+        and commits it to tila_mma_bar; read it from tensor memory."""
+        from .emitter import Val
+        dt, (M, N), _ = self.vt_info(x.vt)
+        if dt.name != "f32" or not (isinstance(x.a, T_.TName) and x.a.name == self._ws["q"]):
+            self.fail("warp-specialised loop: unexpected synchronous dot")
+        self.uses_mma = True
+        self.uses_tmem = True
+        self.tmem_scratch_need = max(self.tmem_scratch_need, max(16, N))
+        self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
+        self.emit("tila_mma_phase ^= 1u;")
+        self.emit("tila::tc_fence_after();")
+        reg = self.tmem_to_reg(Val("tmem", D.f32, (M, N), tmem_col="tila_tmem_scratch_col"))
+        self.emit("tila::tc_fence_before();")
+        return reg
+
+    def ws_acc_dot(self, x, name):
+        """acc = dot(cast[f16](P), V, acc=acc): store P into tensor memory and
+        hand it to the producer, which issues P@V and commits it to the
+        accumulator barrier."""
+        from .emitter import Val
+        from .layouts import TmemRows
+        ctx = self.actx
+        a = ctx.accs[name]
+        N = a["N"]
+        self.wait_all_accs(release=False)
+        acc = self.env[name]
+        if acc.kind != "tmem":
+            lay = TmemRows((128, N), self.T)
+            accv = acc if acc.dt.name == "f32" else self.coerce(acc, D.f32)
+            accv = self.materialize(accv, lay) if not (accv.kind == "reg" and accv.layout == lay) else accv
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {a['col']} + ((tid & 96u) << 16), {accv.name});")
+        if ctx.p_early:
+            ctx.p_early = False
+        else:
+            pv = self.value(x.a.operand)
+            if pv.kind == "smem":
+                self.fail("warp-specialised loop: P must be a register tile")
+            self._store_p(pv, ctx)
+        self.emit("tila::tmem_wait_st();")
+        self.emit("tila::tc_fence_before();")
+        self.emit(f"tila::mbar_arrive(reinterpret_cast<tila::u64*>(tila_smem + {ctx.p_full_off}));")
+        self.emit(f"{a['pend']} = 1u;")
+        v = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
+        v.pending = name
+        return v
+
+    def ws_finish(self, ctx):
+        """After the loop: the Q tile is dead (its last reader, S of the last
+        iteration, completed before the final P@V); its shared memory can stage
+        the epilogue's stores."""
+        q = self._ws["q_load"]
+        self._free_smem.append((q["off"], q["size"]))
+
+    # -- assembly ------------------------------------------------------------------
+
+    def ws_producer(self, per_prog, ring_off, bars_off, scratch_col):
+        """Code of the producer thread (threadIdx.x == 256)."""
+        ws = self._ws
+        kp, vp = ws["k"], ws["v"]
+        kbytes = kp["plan"].nbox * max(kp["plan"].outer_extent, 128) * 128
+        vbytes = vp["plan"].nbox * max(vp["plan"].outer_extent, 128) * 128
+        kring = [ring_off + i * kbytes for i in range(RING)]
+        vring = [ring_off + RING * kbytes + i * vbytes for i in range(RING)]
+        bar = lambda i: f"reinterpret_cast<tila::u64*>(tila_smem_all + {bars_off + 8 * i})"
+        k_full = [bar(i) for i in range(RING)]
+        k_empty = [bar(RING + i) for i in range(RING)]
+        v_full = [bar(2 * RING + i) for i in range(RING)]
+        v_empty = [bar(3 * RING + i) for i in range(RING)]
+        region = lambda w, off: f"reinterpret_cast<tila::u64*>(tila_smem_all + {w * per_prog + off})"
+        q = ws["q_load"]
+        L = []
+        e = L.append
+
+        def tma(plan, coords, dst, barx, ind="      "):
+            for b in range(plan.nbox):
+                cs = list(coords)
+                if b:
+                    cs[0] = f"({cs[0]} + {plan.box_elems * b})"
+                tm = self.tensor_map_param(plan)
+                e(f"{ind}tila::tma_load_{plan.rank}d(tila_smem_all + {dst} + {b * plan.box_bytes}, &{tm}, {barx}, {', '.join(cs)});")
+
+        def wait(barx, parity):
+            e(f"      if (!tila::mbar_wait({barx}, {parity}, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+
+        def mmas(lines, w, qb=None, kb=None, vb=None):
+            for ln in lines:
+                ln = ln.replace("@TM@", f"(tila_tmem_base + {w} * {self.tmem_cols})").replace("@SCOL@", str(scratch_col))
+                if qb is not None:
+                    ln = ln.replace("@QB@", str(qb))
+                if kb is not None:
+                    ln = ln.replace("@KB@", kb)
+                if vb is not None:
+                    ln = ln.replace("@VB@", vb)
+                e("      " + ln)
+
+        e("    // producer: Q tiles, the shared K/V ring and every tcgen05.mma of both programs")
+        e("    const tila::u32 tila_sb4 = tila::smem_u32(tila_smem_all) >> 4;")
+        e("    const bool tila_live_w[2] = {(tila::i32)(blockIdx.x * 2) < launch_0, "
+          "(tila::i32)(blockIdx.x * 2 + 1) < launch_0};")
+        e(f"    const tila::i64 tila_lo = (tila::i64)({ws['start']}), tila_hi = (tila::i64)({ws['end']});")
+        step = ws["step"]
+        e(f"    const tila::i64 tila_n = tila_hi > tila_lo ? (tila_hi - tila_lo + {step - 1}) / {step} : 0;")
+        e("    {")
+        for w in range(2):
+            e(f"    if (tila_live_w[{w}]) {{")
+            e(f"      const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + {w} + pid_off_0);")
+            e(f"      tila::mbar_arrive_expect_tx({region(w, q['bar_off'])}, {q['plan'].bytes}u);")
+            tma(q["plan"], q["coords"], w * per_prog + q["off"], region(w, q["bar_off"]))
+            e("    }")
+        e("    }")
+
+        def load(jexpr, cond, ind):
+            """TMA copies of K and V of iteration ``jexpr`` into stage jexpr & 1."""
+            e(f"{ind}if ({cond}) {{")
+            e(f"{ind}  const tila::i64 lj_ = {jexpr};")
+            e(f"{ind}  const tila::i32 tila_pit = (tila::i32)(tila_lo + lj_ * {step});")
+            e(f"{ind}  (void)tila_pit;")
+            for name, cp, full, base in (("K", kp, k_full, kring), ("V", vp, v_full, vring)):
+                for st in range(RING):
+                    e(f"{ind}  if ((lj_ & 1) == {st}) {{  // {name} into stage {st}")
+                    e(f"{ind}    tila::mbar_arrive_expect_tx({full[st]}, {cp['plan'].bytes}u);")
+                    tma(cp["plan"], cp["coords"], base[st], full[st], ind + "    ")
+                    e(f"{ind}  }}")
+            e(f"{ind}}}")
+        load("0", "tila_n > 0", "    ")
+        load("1", "tila_n > 1", "    ")
+        e("    if (tila_n > 0) {")
+        for w in range(2):
+            e(f"      if (tila_live_w[{w}]) {{")
+            e(f"        if (!tila::mbar_wait({region(w, q['bar_off'])}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+            e("      }")
+        wait(k_full[0], "0u")
+        e("      tila::tc_fence_after();")
+        for w in range(2):
+            e(f"      if (tila_live_w[{w}]) {{")
+            mmas(ws["s_mma"], w, qb=w * per_prog + q["off"], kb=str(kring[0]))
+            e(f"        tila::mma_commit({region(w, 0)});")
+            e("      }")
+        e(f"      tila::mma_commit({k_empty[0]});")
+        e("    }")
+        e("    for (tila::i64 j = 0; j < tila_n; ++j) {")
+        e("      const int st = (int)(j & 1), nx = (int)((j + 1) & 1);")
+        e("      const tila::u32 par = (tila::u32)((j >> 1) & 1), npar = (tila::u32)(((j + 1) >> 1) & 1);")
+        e("      const bool more = j + 1 < tila_n;")
+        e(f"      if (!tila::mbar_wait(st ? {v_full[1]} : {v_full[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+        e(f"      if (more && !tila::mbar_wait(nx ? {k_full[1]} : {k_full[0]}, npar, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+        e(f"      const tila::u32 vb = st ? {vring[1]}u : {vring[0]}u;")
+        e(f"      const tila::u32 kb = nx ? {kring[1]}u : {kring[0]}u;")
+        for w in range(2):
+            e(f"      if (tila_live_w[{w}]) {{")
+            e(f"        if (!tila::mbar_wait({region(w, ws['p_full'])}, (tila::u32)(j & 1), tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+            e("        tila::tc_fence_after();")
+            mmas(ws["pv_mma"], w, vb="vb")
+            e(f"        tila::mma_commit({region(w, ws['acc_bar'])});")
+            e("        if (more) {")
+            mmas(ws["s_mma"], w, qb=w * per_prog + q["off"], kb="kb")
+            e(f"          tila::mma_commit({region(w, 0)});")
+            e("        }")
+            e("      }")
+        e(f"      if (more) tila::mma_commit(nx ? {k_empty[1]} : {k_empty[0]});")
+        e(f"      tila::mma_commit(st ? {v_empty[1]} : {v_empty[0]});")
+        e("      if (j + 2 < tila_n) {")
+        e("        // stage st is free once S(j) (K) and P@V(j) (V) are done")
+        e(f"        if (!tila::mbar_wait(st ? {k_empty[1]} : {k_empty[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+        e(f"        if (!tila::mbar_wait(st ? {v_empty[1]} : {v_empty[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+        load("j + 2", "true", "        ")
+        e("      }")
+        e("    }")
+        e("  tila_producer_end: ;")
+        nbars = 4 * RING
+        return L, nbars, kbytes * RING + vbytes * RING

@@ -544,6 +544,20 @@ __device__ __forceinline__ void bulk_wait_read_n() {
 // tcgen05: tensor memory and the 5th-generation tensor core
 // ---------------------------------------------------------------------------
 
+// Per-warpgroup register budgets (setmaxnreg): executed by every thread of a
+// warpgroup.  reg_dealloc returns registers to the CTA's pool; reg_alloc waits
+// until the pool (threads at launch x registers per thread at launch) holds
+// enough free registers, so the budgets of all warpgroups must add up to at
+// most that total.
+template <u32 N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <u32 N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Allocates `ncols` (power of two >= 32) TMEM columns; executed by one whole
 // warp.  The base address is written to *slot (shared memory).
 __device__ __forceinline__ void tmem_alloc(u32 *slot, u32 ncols) {
