@@ -44,6 +44,7 @@ the kernel fall back to the two-program lowering.
 
 from __future__ import annotations
 
+import os
 import re
 
 from .._reference import tila
@@ -118,7 +119,7 @@ class WarpSpecMixin:
         _, (M, N), _ = self.vt_info(sd.vt)
         if M != 128 or self.vt_info(acc_dot.vt)[1][0] != 128:
             return
-        self._ws_found = {"q": sd.a.name}
+        self._ws_found = {"q": sd.a.name, "token": os.environ.get("TILA_B200_WS_TOKEN", "0") == "1"}
 
     # -- second pass: the consumer side --------------------------------------------
 
@@ -259,6 +260,9 @@ class WarpSpecMixin:
         self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
         self.emit("tila_mma_phase ^= 1u;")
         self.emit("tila::tc_fence_after();")
+        if self._ws.get("token"):
+            from .mma import WG_ACQUIRE
+            self.emit(WG_ACQUIRE)
         reg = self.tmem_to_reg(Val("tmem", D.f32, (M, N), tmem_col="tila_tmem_scratch_col"))
         self.emit("tila::tc_fence_before();")
         return reg
@@ -288,6 +292,9 @@ class WarpSpecMixin:
             self._store_p(pv, ctx)
         self.emit("tila::tmem_wait_st();")
         self.emit("tila::tc_fence_before();")
+        if self._ws.get("token"):
+            from .mma import WG_RELEASE
+            self.emit(WG_RELEASE)
         self.emit(f"tila::mbar_arrive(reinterpret_cast<tila::u64*>(tila_smem + {ctx.p_full_off}));")
         self.emit(f"{a['pend']} = 1u;")
         v = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
@@ -304,7 +311,7 @@ class WarpSpecMixin:
     # -- assembly ------------------------------------------------------------------
 
     def ws_producer(self, per_prog, ring_off, bars_off, scratch_col):
-        """Code of the producer thread (threadIdx.x == 256)."""
+        """Code of the two producer threads: (copy thread 256, MMA thread 288)."""
         ws = self._ws
         kp, vp = ws["k"], ws["v"]
         kbytes = kp["plan"].nbox * max(kp["plan"].outer_extent, 128) * 128
@@ -343,43 +350,49 @@ class WarpSpecMixin:
                     ln = ln.replace("@VB@", vb)
                 e("      " + ln)
 
-        e("    // producer: Q tiles, the shared K/V ring and every tcgen05.mma of both programs")
-        e("    const tila::u32 tila_sb4 = tila::smem_u32(tila_smem_all) >> 4;")
-        e("    const bool tila_live_w[2] = {(tila::i32)(blockIdx.x * 2) < launch_0, "
-          "(tila::i32)(blockIdx.x * 2 + 1) < launch_0};")
-        e(f"    const tila::i64 tila_lo = (tila::i64)({ws['start']}), tila_hi = (tila::i64)({ws['end']});")
         step = ws["step"]
-        e(f"    const tila::i64 tila_n = tila_hi > tila_lo ? (tila_hi - tila_lo + {step - 1}) / {step} : 0;")
-        e("    {")
+        head = ["    const bool tila_live_w[2] = {(tila::i32)(blockIdx.x * 2) < launch_0, "
+                "(tila::i32)(blockIdx.x * 2 + 1) < launch_0};",
+                f"    const tila::i64 tila_lo = (tila::i64)({ws['start']}), tila_hi = (tila::i64)({ws['end']});",
+                f"    const tila::i64 tila_n = tila_hi > tila_lo ? (tila_hi - tila_lo + {step - 1}) / {step} : 0;"]
+
+        # -- copy thread (threadIdx.x == 256): Q once, then K and V of every
+        #    iteration into stage j & 1 as soon as the MMAs that read the
+        #    stage's previous tile are done (empty barrier of that use)
+        e("    // copies: both programs' Q tiles, then K and V through the two-stage ring")
+        L.extend(head)
         for w in range(2):
             e(f"    if (tila_live_w[{w}]) {{")
             e(f"      const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + {w} + pid_off_0);")
             e(f"      tila::mbar_arrive_expect_tx({region(w, q['bar_off'])}, {q['plan'].bytes}u);")
             tma(q["plan"], q["coords"], w * per_prog + q["off"], region(w, q["bar_off"]))
             e("    }")
+        e("    for (tila::i64 j = 0; j < tila_n; ++j) {")
+        e("      const tila::u32 up = (tila::u32)(((j >> 1) - 1) & 1);   // parity of the stage's previous use")
+        e(f"      const tila::i32 tila_pit = (tila::i32)(tila_lo + j * {step});")
+        e("      (void)tila_pit;")
+        for name, cp, full, empty, base in (("K", kp, k_full, k_empty, kring), ("V", vp, v_full, v_empty, vring)):
+            for st in range(RING):
+                e(f"      if ((j & 1) == {st}) {{  // {name} of iteration j into stage {st}")
+                e(f"        if (j >= 2 && !tila::mbar_wait({empty[st]}, up, tila_err, __LINE__, &tila_dead)) goto tila_copy_end;")
+                e(f"        tila::mbar_arrive_expect_tx({full[st]}, {cp['plan'].bytes}u);")
+                tma(cp["plan"], cp["coords"], base[st], full[st], "        ")
+                e("      }")
         e("    }")
+        e("  tila_copy_end: ;")
+        copy_lines = list(L)
+        L.clear()
 
-        def load(jexpr, cond, ind):
-            """TMA copies of K and V of iteration ``jexpr`` into stage jexpr & 1."""
-            e(f"{ind}if ({cond}) {{")
-            e(f"{ind}  const tila::i64 lj_ = {jexpr};")
-            e(f"{ind}  const tila::i32 tila_pit = (tila::i32)(tila_lo + lj_ * {step});")
-            e(f"{ind}  (void)tila_pit;")
-            for name, cp, full, base in (("K", kp, k_full, kring), ("V", vp, v_full, vring)):
-                for st in range(RING):
-                    e(f"{ind}  if ((lj_ & 1) == {st}) {{  // {name} into stage {st}")
-                    e(f"{ind}    tila::mbar_arrive_expect_tx({full[st]}, {cp['plan'].bytes}u);")
-                    tma(cp["plan"], cp["coords"], base[st], full[st], ind + "    ")
-                    e(f"{ind}  }}")
-            e(f"{ind}}}")
-        load("0", "tila_n > 0", "    ")
-        load("1", "tila_n > 1", "    ")
+        # -- MMA thread (threadIdx.x == 288): per program P@V(j), then S(j+1)
+        e("    // MMAs: S = Q K^T and O += P V of both programs, in issue order per program")
+        e("    const tila::u32 tila_sb4 = tila::smem_u32(tila_smem_all) >> 4;")
+        L.extend(head)
         e("    if (tila_n > 0) {")
         for w in range(2):
             e(f"      if (tila_live_w[{w}]) {{")
-            e(f"        if (!tila::mbar_wait({region(w, q['bar_off'])}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+            e(f"        if (!tila::mbar_wait({region(w, q['bar_off'])}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
             e("      }")
-        wait(k_full[0], "0u")
+        e(f"      if (!tila::mbar_wait({k_full[0]}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
         e("      tila::tc_fence_after();")
         for w in range(2):
             e(f"      if (tila_live_w[{w}]) {{")
@@ -392,13 +405,13 @@ class WarpSpecMixin:
         e("      const int st = (int)(j & 1), nx = (int)((j + 1) & 1);")
         e("      const tila::u32 par = (tila::u32)((j >> 1) & 1), npar = (tila::u32)(((j + 1) >> 1) & 1);")
         e("      const bool more = j + 1 < tila_n;")
-        e(f"      if (!tila::mbar_wait(st ? {v_full[1]} : {v_full[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
-        e(f"      if (more && !tila::mbar_wait(nx ? {k_full[1]} : {k_full[0]}, npar, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+        e(f"      if (!tila::mbar_wait(st ? {v_full[1]} : {v_full[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
+        e(f"      if (more && !tila::mbar_wait(nx ? {k_full[1]} : {k_full[0]}, npar, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
         e(f"      const tila::u32 vb = st ? {vring[1]}u : {vring[0]}u;")
         e(f"      const tila::u32 kb = nx ? {kring[1]}u : {kring[0]}u;")
         for w in range(2):
             e(f"      if (tila_live_w[{w}]) {{")
-            e(f"        if (!tila::mbar_wait({region(w, ws['p_full'])}, (tila::u32)(j & 1), tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
+            e(f"        if (!tila::mbar_wait({region(w, ws['p_full'])}, (tila::u32)(j & 1), tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
             e("        tila::tc_fence_after();")
             mmas(ws["pv_mma"], w, vb="vb")
             e(f"        tila::mma_commit({region(w, ws['acc_bar'])});")
@@ -407,15 +420,10 @@ class WarpSpecMixin:
             e(f"          tila::mma_commit({region(w, 0)});")
             e("        }")
             e("      }")
+        e("      // stage frees: K of iteration j + 1 once both S(j + 1) are done, V of j once both P@V(j) are")
         e(f"      if (more) tila::mma_commit(nx ? {k_empty[1]} : {k_empty[0]});")
         e(f"      tila::mma_commit(st ? {v_empty[1]} : {v_empty[0]});")
-        e("      if (j + 2 < tila_n) {")
-        e("        // stage st is free once S(j) (K) and P@V(j) (V) are done")
-        e(f"        if (!tila::mbar_wait(st ? {k_empty[1]} : {k_empty[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
-        e(f"        if (!tila::mbar_wait(st ? {v_empty[1]} : {v_empty[0]}, par, tila_err, __LINE__, &tila_dead)) goto tila_producer_end;")
-        load("j + 2", "true", "        ")
-        e("      }")
         e("    }")
-        e("  tila_producer_end: ;")
+        e("  tila_mma_end: ;")
         nbars = 4 * RING
-        return L, nbars, kbytes * RING + vbytes * RING
+        return (copy_lines, list(L)), nbars, kbytes * RING + vbytes * RING
