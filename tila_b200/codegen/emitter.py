@@ -48,7 +48,7 @@ from .layouts import (Blocked, Derived, Layout, TmemRows, dedupe_owner, owner_pr
                       source_slot_map)
 from .fused import FusedContractionMixin
 from .mma import AsyncLoopMixin, MmaMixin
-from .wspec import WS_REGS_CONSUMER, WS_REGS_LAUNCH, WS_REGS_PRODUCER, WS_THREADS, WarpSpecMixin
+from .wspec import WarpSpecMixin, ws_budget
 
 T_ = tila.tir
 TY = tila.types
@@ -1614,7 +1614,7 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
             ring = None
             base = self._store_staging(size, allocate=False)
         boxes = None
-        if base is None and lay.groups == 1 and len(self._box_slots(16384, 4)) >= 2:
+        if base is None and (lay.groups == 1 or lay.cpg % 32 == 0) and len(self._box_slots(16384, 4)) >= 2:
             # freed operand buffers hold at least two boxes: stage through them
             # instead of a new allocation (less shared memory per CTA)
             boxes = self._box_slots(16384, 4)
@@ -1683,12 +1683,19 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
             if b >= k:
                 self.emit(f"if (tid == 0) tila::bulk_wait_read_n<{k - 1}>();")
                 self.emit("__syncthreads();")
+            # the box's 32 columns belong to one thread group (lay.groups
+            # groups of 128 threads hold lay.cpg columns of every row each)
+            g, c0 = divmod(32 * b, lay.cpg) if lay.groups > 1 else (0, 32 * b)
+            if lay.groups > 1:
+                self.emit(f"if ((tid >> 7) == {g}) {{")
             self.emit("#pragma unroll")
-            self.emit(f"for (int r = {32 * b}; r < {32 * b + 32}; r += 4) {{")
+            self.emit(f"for (int r = {c0}; r < {c0 + 32}; r += 4) {{")
             self.emit(f"  *reinterpret_cast<float4*>(tila_smem + {slot} + row_ * 128 + "
                       f"((((r % 32) / 4) ^ (row_ & 7)) * 16)) = "
                       f"make_float4({value.name}[r], {value.name}[r + 1], {value.name}[r + 2], {value.name}[r + 3]);")
             self.emit("}")
+            if lay.groups > 1:
+                self.emit("}")
             self.emit("tila::fence_proxy_async_smem();")
             self.emit("__syncthreads();")
             cs = list(origin)
@@ -2375,8 +2382,11 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         wg = (self._wg_candidate and not self.fuse and self.T == 128 and self.uses_tmem
               and self.tmem_cols <= 256 and 2 * per_prog + 64 <= 232448 and self._uneven_loops <= 3
               and not self._assume_lines)
-        if wg and self._ws_found is not None and self._ws is None \
-                and os.environ.get("TILA_B200_WS", "1") != "0":
+        # the warp-specialised form also takes programs of 8 warps (one per
+        # pair of warpgroups), which the two-program hand-off does not
+        ws_fit = (self._ws_found is not None and not self.fuse and self.T in (128, 256)
+                  and self.uses_tmem and self.tmem_cols <= 256 and not self._assume_lines)
+        if ws_fit and self._ws is None and os.environ.get("TILA_B200_WS", "1") != "0":
             # the loop has the flash-attention shape: generate the
             # warp-specialised kernel instead (this pass's plan is the fallback)
             try:
@@ -2386,8 +2396,10 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
                                      ws=self._ws_found).generate()
             except CodegenError:
                 pass
-        if self._ws is not None and not wg:
-            self.fail("warp-specialised loop: two programs per CTA do not fit")
+        if self._ws is not None:
+            if not (self.T in (128, 256) and self.uses_tmem and self.tmem_cols <= 256 and not self.fuse):
+                self.fail("warp-specialised loop: two programs per CTA do not fit")
+            wg = True
         if wg:
             self.fuse = {0: 2}
         for ax in sorted(self.fuse or {}):
@@ -2542,6 +2554,8 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     thread 256 the producer."""
     from .mma import WG_ACQUIRE, WG_RELEASE, WG_TRIPS, WG_TURNS
     from .wspec import RING
+    T = self.T
+    threads, launch_regs, regs_producer, regs_consumer = ws_budget(T)
     ring_off = -(-(2 * per_prog) // 1024) * 1024
     kp, vp = self._ws["k"], self._ws["v"]
     ring_bytes = RING * sum(c["plan"].nbox * max(c["plan"].outer_extent, 128) * 128 for c in (kp, vp))
@@ -2554,14 +2568,14 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
         self.fail(f"warp-specialised kernel needs {total} bytes of shared memory")
     out = ['#include "tila_tile.cuh"', "",
            "#define tila_exp2_f32 tila::" + ("exp2_ftz" if self.uses_mma else "exp2_fast"), "",
-           f'extern "C" __global__ void __launch_bounds__({WS_THREADS}, 1) {self.entry}(',
+           f'extern "C" __global__ void __launch_bounds__({threads}, 1) {self.entry}(',
            ",\n".join("    " + x for x in sig) + ") {"]
     e = out.append
     e("  extern __shared__ __align__(1024) unsigned char tila_smem_all[];")
     e("  // warpgroups 0 and 1: programs 2*blockIdx.x + w (softmax side); warpgroup 2: thread 256 copies, thread 288 issues the MMAs")
-    e("  const bool tila_producer = threadIdx.x >= 256;")
-    e("  const int tila_wg = tila_producer ? 0 : (int)(threadIdx.x >> 7);")
-    e("  const int tid = threadIdx.x & 127;")
+    e(f"  const bool tila_producer = threadIdx.x >= {2 * T};")
+    e(f"  const int tila_wg = tila_producer ? 0 : (int)(threadIdx.x / {T});")
+    e(f"  const int tid = threadIdx.x & {T - 1};")
     e(f"  unsigned char* const tila_smem = tila_smem_all + tila_wg * {per_prog};")
     e("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + tila_wg + pid_off_0);")
     e("  const bool tila_live = !tila_producer && (tila::i32)(blockIdx.x * 2 + tila_wg) < launch_0;")
@@ -2586,13 +2600,13 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     for v in self._phase_vars:
         e(f"  tila::u32 {v} = 0;")
     q = self._ws["q_load"]
-    per_region = [(0, 1), (q["bar_off"], 1), (self._ws["acc_bar"], 1), (self._ws["p_full"], 128)]
+    per_region = [(0, 1), (q["bar_off"], 1), (self._ws["acc_bar"], 1), (self._ws["p_full"], T)]
     per_region += [(o, 1) for o in self._need_barrier_init]
     inits = " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem_all + {w * per_prog + o}), {c});"
                      for w in range(2) for o, c in per_region)
     inits += " " + " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem_all + {bars_off + 8 * i}), 1);"
                             for i in range(nbars))
-    inits += " tila::mbar_init(&tila_tok[0], 128); tila::mbar_init(&tila_tok[1], 128);"
+    inits += f" tila::mbar_init(&tila_tok[0], {T}); tila::mbar_init(&tila_tok[1], {T});"
     e(f"  if (threadIdx.x == 0) {{ {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
     for tm in self.tensor_maps:
         e(f"  if (threadIdx.x == 0) tila::tma_prefetch_desc(&{tm['param']});")
@@ -2610,17 +2624,17 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     e(f"  const tila::u32 tila_tmem = *tila_tmem_slot + (tila::u32)(tila_wg * {self.tmem_cols});")
     e(f"  const tila::u32 tila_tmem_scratch_col = {scratch_col}; (void)tila_tmem_scratch_col;")
     e("  if (tila_producer) {")
-    e(f"    tila::reg_dealloc<{WS_REGS_PRODUCER}>();")
+    e(f"    tila::reg_dealloc<{regs_producer}>();")
     copy_lines, mma_lines = prod
-    e("    if (threadIdx.x == 256) {")
+    e(f"    if (threadIdx.x == {2 * T}) {{")
     out.extend("  " + ln for ln in copy_lines)
-    e("    } else if (threadIdx.x == 288) {")
+    e(f"    }} else if (threadIdx.x == {2 * T + 32}) {{")
     e("    const tila::u32 tila_tmem_base = *tila_tmem_slot;")
     out.extend("  " + ln for ln in mma_lines)
     e("    }")
     e("    __syncwarp();   // each producer warp reconverges before the final barrier")
     e("  } else {")
-    e(f"  tila::reg_alloc<{WS_REGS_CONSUMER}>();")
+    e(f"  tila::reg_alloc<{regs_consumer}>();")
     e("  do {")
     e("    if (!tila_live) break;")
     # the optional hand-off between the two softmax warpgroups (TILA_B200_WS_TOKEN=1)
@@ -2633,7 +2647,7 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
         if st.startswith((WG_TRIPS, WG_TURNS)):
             continue
         line = line.replace(WG_ACQUIRE, acquire).replace(WG_RELEASE, release)
-        out.append(line.replace("__syncthreads();", "tila::wg_sync(tila_wg);"))
+        out.append(line.replace("__syncthreads();", f"tila::wg_sync_n(tila_wg, {T});"))
     e("  } while (0);")
     e("  }")
     e("  tila::tc_fence_before();")
@@ -2643,9 +2657,9 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     src = "\n".join(out) + "\n"
     self.fuse = {0: 2}
     tmem_cols = cta_cols
-    return KernelSpec(self.entry, src, WS_THREADS, max(total, 233472 // 2 - 1024 + 1), params,
+    return KernelSpec(self.entry, src, threads, max(total, 233472 // 2 - 1024 + 1), params,
                       fp_contract=True, assume_lines=list(self._assume_lines), tmem_cols=tmem_cols,
-                      tensor_maps=list(self.tensor_maps), fuse={0: 2}, launch_regs=WS_REGS_LAUNCH)
+                      tensor_maps=list(self.tensor_maps), fuse={0: 2}, launch_regs=launch_regs)
 
 
 KernelEmitter._ws_generate = _ws_generate_impl

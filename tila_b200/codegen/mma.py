@@ -746,7 +746,7 @@ class AsyncLoopMixin:
                 self.emit(f"const tila::i64 tila_trip_{k} = ((tila::i64)({end.expr}) > (tila::i64)({start.expr})) ? "
                           f"((tila::i64)({end.expr}) - (tila::i64)({start.expr}) + {stepv - 1}) / {stepv} : 0;")
                 self.emit(f"{WG_TRIPS} {k}")
-        self.ws_detect(s, al, ctx)
+        self.ws_detect(s, start, al, ctx)
         self.actx = ctx
         return ctx
 
@@ -834,7 +834,7 @@ class AsyncLoopMixin:
                 return off
         return self.smem.alloc(size, 1024)
 
-    def _pingpong_ok(self, s, start, al):
+    def _pingpong_ok(self, s, start, al, any_T=False):
         """Two programs of grid axis 0 may share a CTA, one per warpgroup,
         handing the CUDA-core phase of each iteration back and forth, when
         both are sure to run the same iterations: the loop is a top-level
@@ -842,7 +842,7 @@ class AsyncLoopMixin:
         on program_id(0), and each iteration has exactly one synchronous and
         one accumulating dot."""
         from .pipeline import _walk
-        if self.T != 128 or id(s) not in {id(st) for st in self.tk.body}:
+        if (self.T != 128 and not any_T) or id(s) not in {id(st) for st in self.tk.body}:
             return False
         has_return = [False]
         for st in self.tk.body:

@@ -52,19 +52,28 @@ from .._reference import tila
 T_ = tila.tir
 D = tila.dtypes
 
-WS_THREADS = 384           # two consumer warpgroups + the producer warpgroup
 RING = 2                   # stages of the K and V rings
-# Register budgets.  __launch_bounds__(384, 1) gives every thread 168 registers
-# at launch (65536 / 384 rounded down to a multiple of 8), a pool of
-# 384 x 168 = 64512.  The producer warpgroup gives back all but 40 and the two
-# consumer warpgroups take 232 each: 128 x 40 + 256 x 232 = 64512, exactly the
-# pool, so reg_alloc never waits for registers that do not exist.  The host
-# refuses to launch the kernel unless ptxas allocated exactly WS_REGS_LAUNCH.
-WS_REGS_LAUNCH = 168
-WS_REGS_PRODUCER = 40
-WS_REGS_CONSUMER = 232
-assert 128 * WS_REGS_PRODUCER + 256 * WS_REGS_CONSUMER <= WS_THREADS * WS_REGS_LAUNCH
-assert WS_REGS_LAUNCH == (65536 // WS_THREADS) // 8 * 8
+
+
+def ws_budget(T):
+    """(threads, registers per thread at launch, producer, consumer registers)
+    of the warp-specialised kernel whose programs have T threads.
+
+    The CTA is two programs of T threads plus the producer warpgroup.
+    ``__launch_bounds__(threads, 1)`` gives every thread 65536 / threads
+    registers at launch, rounded down to a multiple of 8; that times the
+    thread count is the pool the warpgroups trade in (setmaxnreg).  The
+    producer gives back all but its share, the consumers take theirs, and the
+    shares add up to at most the pool, so reg_alloc never waits for
+    registers that do not exist.  The host refuses to launch the kernel
+    unless ptxas allocated exactly the launch count."""
+    threads = 2 * T + 128
+    launch = (65536 // threads) // 8 * 8
+    producer, consumer = {128: (56, 224), 256: (24, 112)}[T]
+    assert 128 * producer + 2 * T * consumer <= threads * launch
+    assert producer <= launch <= consumer and producer % 8 == 0 and consumer % 8 == 0
+    return threads, launch, producer, consumer
+
 
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")
 _ALLOWED = {"pid_0", "pid_1", "pid_2", "tila_pit", "int", "long", "unsigned", "float", "double",
@@ -89,11 +98,14 @@ class WarpSpecMixin:
 
     # -- first pass: is the loop of the warp-specialised shape? ------------------
 
-    def ws_detect(self, s, al, ctx):
+    def ws_detect(self, s, start, al, ctx):
         """Record the one-shot operand of the loop's synchronous dot when the
-        two-program loop has the flash-attention shape (see module doc)."""
+        loop has the flash-attention shape (see module doc) and both programs
+        of a CTA run the same trip count; programs of 4 or 8 warps."""
         from .pipeline import _walk
-        if not getattr(ctx, "pingpong", False) or ctx.turns is not None:
+        if self.T not in (128, 256) or not self._pingpong_ok(s, start, al, any_T=True):
+            return
+        if any(node is not None and not self._pid0_free(node) for node in (s.start, s.end)):
             return
         if al.cast_loads or len(al.loads) != 2 or len(al.accs) != 1:
             return
@@ -192,7 +204,8 @@ class WarpSpecMixin:
         if pre.kind == "scalar":
             pre = self.materialize_elementwise(D.f32, (128, N), [pre], lambda e: e[0], layout=lay)
         pre = self.materialize(pre, lay)
-        self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {col} + ((tid & 96u) << 16), {pre.name});")
+        goff = f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else ""
+        self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {col}{goff} + ((tid & 96u) << 16), {pre.name});")
         self.emit(f"// warp-specialised loop over {s.var}: S from the producer warp, P handed back "
                   f"through tensor memory, {acc_name} accumulated in tensor memory")
         a = ctx.accs[acc_name]
@@ -282,7 +295,8 @@ class WarpSpecMixin:
             lay = TmemRows((128, N), self.T)
             accv = acc if acc.dt.name == "f32" else self.coerce(acc, D.f32)
             accv = self.materialize(accv, lay) if not (accv.kind == "reg" and accv.layout == lay) else accv
-            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {a['col']} + ((tid & 96u) << 16), {accv.name});")
+            goff = f" + (tid >> 7) * {lay.cpg}" if lay.groups > 1 else ""
+            self.emit(f"tila::tmem_store_row<{lay.nreg}>(tila_tmem + {a['col']}{goff} + ((tid & 96u) << 16), {accv.name});")
         if ctx.p_early:
             ctx.p_early = False
         else:

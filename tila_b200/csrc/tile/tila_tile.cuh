@@ -441,6 +441,12 @@ __device__ __forceinline__ void wg_sync(int wg) {
   asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
 }
 
+// Barrier of the `n` threads of program `wg` (named barrier 1 + wg) in kernels
+// that run one program per group of n threads.
+__device__ __forceinline__ void wg_sync_n(int wg, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ u64 globaltimer_ns() {
   u64 t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
