@@ -86,8 +86,26 @@ def test_reference_fused_attention_takes_two_program_plan(causal):
     if causal:
         assert spec.threads == 256 and spec.launch_regs == 0
     else:
-        assert spec.threads == 384 and spec.launch_regs == 168
-        assert "tila::reg_alloc<232>()" in spec.source and "tila::reg_dealloc<40>()" in spec.source
+        from tila_b200.codegen.wspec import ws_budget
+        threads, launch, producer, consumer = ws_budget(128)
+        assert spec.threads == threads == 384 and spec.launch_regs == launch == 168
+        assert f"tila::reg_alloc<{consumer}>()" in spec.source
+        assert f"tila::reg_dealloc<{producer}>()" in spec.source
+
+
+def test_warp_specialised_budgets_fit_the_launch_pool():
+    """Every warpgroup's setmaxnreg share adds up to at most the registers the
+    CTA is launched with (threads x launch registers), for 4- and 8-warp
+    programs; 8-warp programs run 2 x 256 consumers and a producer warpgroup."""
+    from tila_b200.codegen.wspec import ws_budget
+    for T in (128, 256):
+        threads, launch, producer, consumer = ws_budget(T)
+        assert threads == 2 * T + 128 and launch == (65536 // threads) // 8 * 8
+        assert 128 * producer + 2 * T * consumer <= threads * launch
+    q = torch.zeros(2, 512, 128, dtype=f16)
+    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+               8, CAUSAL=0, BM=128, BN=128, BD=128)
+    assert spec.threads == 640 and spec.launch_regs == 96 and spec.fuse == {0: 2}
 
 
 def test_warp_specialised_kernel_register_budget(tmp_path):
@@ -110,6 +128,14 @@ def test_warp_specialised_kernel_register_budget(tmp_path):
     assert out.returncode == 0, out.stderr[-2000:]
     regs = re.findall(r"Used (\d+) registers", out.stderr)
     assert regs and int(regs[-1]) == spec.launch_regs == 168
+    spec8 = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+                8, CAUSAL=0, BM=128, BN=128, BD=128)
+    cu.write_text(spec8.source)
+    out = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-Xptxas", "-v",
+                          f"-I{build.PKG / 'csrc' / 'tile'}", "-c", str(cu), "-o", str(tmp_path / "ws.o")],
+                         capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert int(re.findall(r"Used (\d+) registers", out.stderr)[-1]) == spec8.launch_regs == 96
 
 
 def test_static_if_resolution_leaves_kernel_untouched():
