@@ -2562,8 +2562,7 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     bars_off = ring_off + ring_bytes
     prod, nbars, _ = self.ws_producer(per_prog, ring_off, bars_off, scratch_col)
     dead_off = bars_off + 8 * nbars
-    tok_off = dead_off + 16
-    total = tok_off + 16
+    total = dead_off + 16
     if total > 232448:
         self.fail(f"warp-specialised kernel needs {total} bytes of shared memory")
     out = ['#include "tila_tile.cuh"', "",
@@ -2579,10 +2578,6 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     e(f"  unsigned char* const tila_smem = tila_smem_all + tila_wg * {per_prog};")
     e("  const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + tila_wg + pid_off_0);")
     e("  const bool tila_live = !tila_producer && (tila::i32)(blockIdx.x * 2 + tila_wg) < launch_0;")
-    e("  const bool tila_partner_live = (tila::i32)(blockIdx.x * 2 + (tila_wg ^ 1)) < launch_0;")
-    e(f"  tila::u64* const tila_tok = reinterpret_cast<tila::u64*>(tila_smem_all + {tok_off});")
-    e("  tila::u32 tila_tok_ph = 0, tila_tok_n = 0;")
-    e("  (void)tila_partner_live; (void)tila_tok; (void)tila_tok_ph; (void)tila_tok_n;")
     e("  const tila::i32 pid_1 = (tila::i32)(blockIdx.y + pid_off_1);")
     e("  const tila::i32 pid_2 = (tila::i32)(blockIdx.z + pid_off_2);")
     e("  (void)pid_0; (void)pid_1; (void)pid_2;")
@@ -2606,7 +2601,6 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
                      for w in range(2) for o, c in per_region)
     inits += " " + " ".join(f"tila::mbar_init(reinterpret_cast<tila::u64*>(tila_smem_all + {bars_off + 8 * i}), 1);"
                             for i in range(nbars))
-    inits += f" tila::mbar_init(&tila_tok[0], {T}); tila::mbar_init(&tila_tok[1], {T});"
     e(f"  if (threadIdx.x == 0) {{ {inits} tila::mbar_fence_init(); tila_dead = 0; }}")
     for tm in self.tensor_maps:
         e(f"  if (threadIdx.x == 0) tila::tma_prefetch_desc(&{tm['param']});")
@@ -2637,16 +2631,10 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     e(f"  tila::reg_alloc<{regs_consumer}>();")
     e("  do {")
     e("    if (!tila_live) break;")
-    # the optional hand-off between the two softmax warpgroups (TILA_B200_WS_TOKEN=1)
-    acquire = ("if (tila_partner_live && (tila_wg == 1 || tila_tok_n > 0)) { "
-               "tila::mbar_wait(&tila_tok[tila_wg], tila_tok_ph, tila_err, __LINE__, &tila_dead); "
-               "tila_tok_ph ^= 1u; } ++tila_tok_n;")
-    release = "if (tila_partner_live) tila::mbar_arrive(&tila_tok[tila_wg ^ 1]);"
     for line in body:
         st = line.strip()
-        if st.startswith((WG_TRIPS, WG_TURNS)):
+        if st in (WG_ACQUIRE, WG_RELEASE) or st.startswith((WG_TRIPS, WG_TURNS)):
             continue
-        line = line.replace(WG_ACQUIRE, acquire).replace(WG_RELEASE, release)
         out.append(line.replace("__syncthreads();", f"tila::wg_sync_n(tila_wg, {T});"))
     e("  } while (0);")
     e("  }")

@@ -44,7 +44,6 @@ the kernel fall back to the two-program lowering.
 
 from __future__ import annotations
 
-import os
 import re
 
 from .._reference import tila
@@ -131,7 +130,7 @@ class WarpSpecMixin:
         _, (M, N), _ = self.vt_info(sd.vt)
         if M != 128 or self.vt_info(acc_dot.vt)[1][0] != 128:
             return
-        self._ws_found = {"q": sd.a.name, "token": os.environ.get("TILA_B200_WS_TOKEN", "0") == "1"}
+        self._ws_found = {"q": sd.a.name}
 
     # -- second pass: the consumer side --------------------------------------------
 
@@ -273,9 +272,6 @@ class WarpSpecMixin:
         self.emit("tila::mbar_wait(tila_mma_bar, tila_mma_phase, tila_err, __LINE__, &tila_dead);")
         self.emit("tila_mma_phase ^= 1u;")
         self.emit("tila::tc_fence_after();")
-        if self._ws.get("token"):
-            from .mma import WG_ACQUIRE
-            self.emit(WG_ACQUIRE)
         reg = self.tmem_to_reg(Val("tmem", D.f32, (M, N), tmem_col="tila_tmem_scratch_col"))
         self.emit("tila::tc_fence_before();")
         return reg
@@ -306,9 +302,6 @@ class WarpSpecMixin:
             self._store_p(pv, ctx)
         self.emit("tila::tmem_wait_st();")
         self.emit("tila::tc_fence_before();")
-        if self._ws.get("token"):
-            from .mma import WG_RELEASE
-            self.emit(WG_RELEASE)
         self.emit(f"tila::mbar_arrive(reinterpret_cast<tila::u64*>(tila_smem + {ctx.p_full_off}));")
         self.emit(f"{a['pend']} = 1u;")
         v = Val("tmem", D.f32, (128, N), tmem_col=str(a["col"]))
