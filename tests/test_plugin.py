@@ -89,3 +89,39 @@ def test_build_cli_writes_cuda_tir_and_source_map(tmp_path):
     ref = tmp_path / "ref"
     assert tila_cli.main(["build", str(src), "-o", str(ref)]) == 0
     assert (out / "kernel.tir.txt").read_text() == (ref / "kernel.tir.txt").read_text()
+
+
+def test_build_cli_emits_the_launch_time_tensor_core_plan(tmp_path):
+    """The build-time facts (contiguous, 16-byte aligned rows) give the
+    reference matmul example the TMA ring and tcgen05 MMAs a launch gets."""
+    from tila_b200._reference import reference_tree
+    from tila_b200.__main__ import main
+    src = reference_tree() / "examples" / "matmul.py"
+    assert main(["build", str(src), "-o", str(tmp_path), "--const", "BM=128", "--const", "BN=128",
+                 "--const", "BK=64"]) == 0
+    cu = (tmp_path / "matmul_kernel.cu").read_text()
+    assert "tila::tma_load_2d(" in cu and "tila::mma_f16_ss(" in cu
+
+
+def test_repeated_signature_key_follows_every_tila_switch(monkeypatch):
+    """The repeated-signature path keys on every TILA_* variable (TILA_SAFETY,
+    TILA_RACE_MAX_PAIRS and TILA_PROOF_* included): flipping one makes the
+    next launch run the full checks."""
+    monkeypatch.setenv("TILA_SAFETY", "strict")
+    before = plugin._tila_env()
+    monkeypatch.setenv("TILA_SAFETY", "warn")
+    assert plugin._tila_env() != before
+    for name in ("TILA_RACE_MAX_PAIRS", "TILA_PROOF_TIMEOUT_MS"):
+        key = plugin._tila_env()
+        monkeypatch.setenv(name, "7")
+        assert plugin._tila_env() != key
+
+
+def test_replaced_statement_invalidates_the_repeated_signature_path():
+    from dataclasses import replace
+    jf = ti.jit(W.add_kernel.fn)
+    stmts = tuple(plugin._statements(jf.tk.body, []))
+    assert plugin._same_tir(jf.tk, jf.tk, stmts)
+    store = jf.tk.body[-1]
+    jf.tk.body[-1] = replace(store)
+    assert not plugin._same_tir(jf.tk, jf.tk, stmts)

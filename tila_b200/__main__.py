@@ -20,17 +20,23 @@ import sys
 
 
 def _default_facts(tk):
-    """Binding facts for build-time code: contiguous, 16-byte aligned."""
+    """Binding facts for build-time code: contiguous, 16-byte aligned buffers
+    whose row strides are multiples of 16 bytes - the bindings the
+    benchmarked kernels receive, so f16/f32 buffers of rank 2 and more get
+    the TMA/tcgen05 plans that such a launch gets (backend.binding_facts)."""
     from .codegen.emitter import BufferInfo
     out = {}
     for p in list(tk.buffers) + list(tk.ptr_params):
         dt = p.vtype.elem
         rank = len(getattr(p.vtype, "dims", ()) or ()) or 1
+        is_ptr = p in tk.ptr_params
         out[p.name] = BufferInfo(name=p.name, dtype=dt, rank=rank, unit_last=True,
-                                 stride_div=(1,) * rank, base_align=16,
+                                 stride_div=(16,) * (rank - 1) + (1,), base_align=16,
                                  writable=p.vtype.access is not None and
                                  getattr(p.vtype.access, "name", "") != "READ_ONLY",
-                                 is_ptr=p in tk.ptr_params, tma_ok=False)
+                                 is_ptr=is_ptr,
+                                 tma_ok=(not is_ptr and rank >= 2 and dt is not None
+                                         and dt.name in ("f16", "f32")))
     return out
 
 
