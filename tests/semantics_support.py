@@ -286,3 +286,25 @@ def kernel(idx_buf: ti.Buffer[ti.i32, (N,), ti.ReadOnly],
     v = ti.load(data, idx)
     ti.store(out, offs, v, mask=m)
 ''')
+
+
+def expand3_program(directory):
+    """expand of 2-D tiles (x[None, :] and x[:, None] insert a unit axis at 0
+    and 1) broadcast against 3-D tiles built by chained expands."""
+    return load_source(directory, "sem_expand3", '''import tila as ti
+
+
+@ti.jit
+def kernel(x: ti.Buffer[ti.f32, (4, 8), ti.ReadOnly],
+           o0: ti.Buffer[ti.f32, (2, 4, 8), ti.WriteOnly],
+           o1: ti.Buffer[ti.f32, (4, 2, 8), ti.WriteOnly]):
+    r = ti.arange(0, 4)
+    c = ti.arange(0, 8)
+    k = ti.arange(0, 2)
+    t = ti.load(x, (r[:, None], c[None, :]))
+    kf = ti.cast[ti.f32](k)
+    ti.store(o0, (k[:, None][:, None], r[:, None][None, :], c[None, :][None, :]),
+             t[None, :] + kf[:, None][:, None])
+    ti.store(o1, (r[:, None][:, None], k[:, None][None, :], c[None, :][None, :]),
+             t[:, None] * 2.0 + kf[:, None][None, :])
+''')

@@ -280,6 +280,15 @@ def test_rank3_tiles_compile(tmp_path):
             native.compile_spec(spec)
 
 
+def test_expand_of_rank2_tiles_compiles(tmp_path):
+    """x[None, :] and x[:, None] on 2-D tiles insert a unit axis at 0 and 1;
+    chained expands of 1-D aranges give 3-D index tiles."""
+    import semantics_support as S
+    k = S.expand3_program(tmp_path)
+    spec = gen(k, dict(x=torch.zeros(4, 8), o0=torch.zeros(2, 4, 8), o1=torch.zeros(4, 2, 8)))
+    native.compile_spec(spec)
+
+
 def test_assume_checks_only_in_debug_builds(tmp_path):
     """ti.assume is free normally; with debug checks each false lane records
     its line and the program stops before the access it guards."""

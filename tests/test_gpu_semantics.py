@@ -382,6 +382,22 @@ def test_rank3_tiles_match_interpreter(tmp_path, op, axis):
         np.testing.assert_allclose(got, cpu, rtol=1e-5, atol=1e-6)
 
 
+def test_expand_of_rank2_tiles_matches_interpreter(tmp_path):
+    """Unit axes inserted at 0 and 1 of a (4, 8) tile broadcast against 3-D
+    index tiles (src/tila/interp.py:305-307 expand semantics), bit-exact."""
+    k = S.expand3_program(tmp_path)
+    x = np.random.default_rng(7).standard_normal((4, 8)).astype(np.float32)
+    c0, c1 = np.zeros((2, 4, 8), np.float32), np.zeros((4, 2, 8), np.float32)
+    k[(1,)](x, c0, c1)
+    g0, g1 = torch.zeros(2, 4, 8, device="cuda"), torch.zeros(4, 2, 8, device="cuda")
+    k[(1,)](torch.from_numpy(x).cuda(), g0, g1)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    np.testing.assert_array_equal(g0.cpu().numpy(), c0)
+    np.testing.assert_array_equal(g1.cpu().numpy(), c1)
+    np.testing.assert_array_equal(c0[1], x + 1.0)
+
+
 @pytest.mark.parametrize("dtype", ["f16", "bf16", "f64"])
 @pytest.mark.parametrize("op", ["sum", "max"])
 @pytest.mark.parametrize("axis", [0, 1])

@@ -734,16 +734,22 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
 
     def e_TExpand(self, x):
         v = self.value(x.operand)
-        if v.kind == "scalar" or len(v.shape) != 1:
-            self.fail("expand is supported on 1-D tiles only")
-        n = v.shape[0]
-        shape = (n, 1) if x.axis == 1 else (1, n)
+        if v.kind == "scalar":
+            self.fail("expand of a scalar")
+        ax = int(x.axis)
+        if ax < 0:
+            ax += len(v.shape) + 1
+        if not 0 <= ax <= len(v.shape):
+            self.fail(f"expand axis {x.axis} out of range")
+        shape = tuple(v.shape[:ax]) + (1,) + tuple(v.shape[ax:])
+        if v.kind == "tmem":
+            v = self.tmem_to_reg(v)
         if v.kind == "func":
-            if x.axis == 1:
-                return Val("func", v.dt, shape, fn=lambda idx, f=v.fn: f((idx[0],)), zero=v.zero)
-            return Val("func", v.dt, shape, fn=lambda idx, f=v.fn: f((idx[1],)), zero=v.zero)
+            # the inserted unit axis carries no index
+            return Val("func", v.dt, shape, fn=lambda idx, f=v.fn, a=ax: f(tuple(idx[:a]) + tuple(idx[a + 1:])),
+                       zero=v.zero)
         if v.kind == "reg":
-            lay = Derived(v.layout, ("expand", x.axis), shape, tuple(range(v.layout.nreg)))
+            lay = Derived(v.layout, ("expand", ax), shape, tuple(range(v.layout.nreg)))
             return Val("reg", v.dt, shape, name=v.name, layout=lay)
         self.fail("expand of this value kind is not supported")
 
@@ -2071,6 +2077,7 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         end = self.value(s.end)
         step = self.value(s.step)
         if step.const is None:
+            # the checker admits only compile-time steps >= 1 (TILA-TYPE-025)
             self.fail("loop step must be a compile-time constant", s.line)
         stepv = int(step.const)
         if stepv == 0:
