@@ -308,3 +308,28 @@ def kernel(x: ti.Buffer[ti.f32, (4, 8), ti.ReadOnly],
     ti.store(o1, (r[:, None][:, None], k[:, None][None, :], c[None, :][None, :]),
              t[:, None] * 2.0 + kf[:, None][None, :])
 ''')
+
+
+def ptr_tile_program(directory):
+    """Pointer tiles bound to names: a 1-D tile (p = x + i) and a 2-D tile
+    built from an expanded index (x + r[:, None] * 8 + c[None, :])."""
+    return load_source(directory, "sem_ptr_tiles", '''import tila as ti
+N = ti.Dim("N")
+
+
+@ti.jit
+def kernel(x: ti.ReadPtr[ti.f32, N], out: ti.WritePtr[ti.f32, N], out2: ti.WritePtr[ti.f32, N]):
+    i = ti.program_id(0) * 64 + ti.arange(0, 64)
+    ok = i < N
+    p = x + i
+    q = out + i
+    v = ti.load(p, mask=ok, other=0)
+    ti.store(q, v * 3.0, mask=ok)
+    r = ti.program_id(0) * 8 + ti.arange(0, 8)
+    c = ti.arange(0, 8)
+    j = r[:, None] * 8 + c[None, :]
+    ok2 = j < N
+    p2 = x + j
+    w = ti.load(p2, mask=ok2, other=0)
+    ti.store(out2 + j, w + 1.0, mask=ok2)
+''')

@@ -289,6 +289,15 @@ def test_expand_of_rank2_tiles_compiles(tmp_path):
     native.compile_spec(spec)
 
 
+def test_named_pointer_tiles_compile(tmp_path):
+    """Pointer tiles bound to names (1-D and 2-D) lower to masked loads and
+    stores through the Ptr parameters."""
+    import semantics_support as S
+    k = S.ptr_tile_program(tmp_path)
+    spec = gen(k, dict(x=torch.zeros(300), out=torch.zeros(300), out2=torch.zeros(300)))
+    native.compile_spec(spec)
+
+
 def test_assume_checks_only_in_debug_builds(tmp_path):
     """ti.assume is free normally; with debug checks each false lane records
     its line and the program stops before the access it guards."""
