@@ -331,10 +331,10 @@ class Case:
         self.axis, self.grid_axis_total = 1, bh
         self.rows_per_program = 1
         scale = d ** -0.5
-        # 8 warps: one program per CTA, each row's 128 scores split over two
-        # thread halves; two such CTAs share an SM (faster here than pairing
-        # the programs of uneven trip counts in one CTA)
-        causal = W.fused_attention_kernel[grid].with_options(num_warps=8)
+        # 4 warps per program: the warp-specialised form, two programs per CTA
+        # whose two loops (below the diagonal, then the diagonal tile) walk
+        # one stream of K/V tiles of per-program length
+        causal = W.fused_attention_kernel[grid].with_options(num_warps=4)
         self.launches = [lambda s: causal(s[0], s[1], s[2], s[3], scale, CAUSAL=1, BM=128, BN=128, BD=128)]
         self.kernels = [W.fused_attention_kernel]
         self.out_index = 3
@@ -344,7 +344,7 @@ class Case:
         self.metric_unit = ("f16 TFLOPS", "TFLOP/s", 1e12)
         self.dtype = "f16 in, f32 accumulate"
         self.config = {"workload": "fused_attention_causal", "batch": 4, "heads": 32, "seq": l,
-                       "head_dim": d, "BM": 128, "BN": 128, "causal": True, "num_warps": 8,
+                       "head_dim": d, "BM": 128, "BN": 128, "causal": True, "num_warps": 4,
                        "flop_count": "half of the non-causal 4*BH*L^2*D"}
         self.e2e_call = lambda xs: (grid, xs, lambda: torch.empty((bh, l, d), device=self.device),
                                     lambda args, out: causal(*args, out, scale, CAUSAL=1,

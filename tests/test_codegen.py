@@ -75,22 +75,21 @@ def test_reference_fused_attention_takes_two_program_plan(causal):
     """examples/fused_attention.py puts each of its loops inside ``if CAUSAL
     == 1: ... else:``; the static if is resolved per specialisation before
     the loop matchers run, so at 128x128 tiles the loop of the taken branch
-    runs two 128-row programs per CTA.  The non-causal loop (same trip count
-    for both programs) gets the warp-specialised form: two softmax
-    warpgroups plus a producer warpgroup that issues every copy and MMA;
-    the causal one keeps the hand-off between the two programs."""
+    runs two 128-row programs per CTA in the warp-specialised form: two
+    softmax warpgroups plus a producer warpgroup that issues every copy and
+    MMA.  With CAUSAL=1 the below-diagonal loop and the diagonal loop form
+    one chain over the K/V tiles, and the two programs of a CTA run
+    different numbers of iterations (the producer counts them per program)."""
     q = torch.zeros(2, 512, 128, dtype=f16)
     spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
                CAUSAL=causal, BM=128, BN=128, BD=128)
     assert spec.fuse == {0: 2} and spec.tmem_cols == 512
-    if causal:
-        assert spec.threads == 256 and spec.launch_regs == 0
-    else:
-        from tila_b200.codegen.wspec import ws_budget
-        threads, launch, producer, consumer = ws_budget(128)
-        assert spec.threads == threads == 384 and spec.launch_regs == launch == 168
-        assert f"tila::reg_alloc<{consumer}>()" in spec.source
-        assert f"tila::reg_dealloc<{producer}>()" in spec.source
+    from tila_b200.codegen.wspec import ws_budget
+    threads, launch, producer, consumer = ws_budget(128)
+    assert spec.threads == threads == 384 and spec.launch_regs == launch == 168
+    assert f"tila::reg_alloc<{consumer}>()" in spec.source
+    assert f"tila::reg_dealloc<{producer}>()" in spec.source
+    assert "tila_nw[1]" in spec.source and "kErrSchedule" in spec.source
 
 
 def test_warp_specialised_budgets_fit_the_launch_pool():

@@ -81,6 +81,8 @@ ERROR_CODES = {
        "partner warpgroup never arrived); the program stopped early and its outputs are incomplete",
     2: "tensor memory allocation failed",
     3: "a ti.assume predicate was false (TILA_DEBUG=1 build)",
+    4: "the loops of a warp-specialised kernel did not cover one contiguous range of iterations "
+       "at run time (a loop ended before it started); the kernel's outputs are incomplete",
 }
 
 

@@ -2391,16 +2391,17 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
               and not self._assume_lines)
         # the warp-specialised form also takes programs of 8 warps (one per
         # pair of warpgroups), which the two-program hand-off does not
-        ws_fit = (self._ws_found is not None and not self.fuse and self.T in (128, 256)
+        found = self.ws_ready() if self._ws is None else None
+        ws_fit = (found is not None and not self.fuse and self.T in (128, 256)
                   and self.uses_tmem and self.tmem_cols <= 256 and not self._assume_lines)
-        if ws_fit and self._ws is None and os.environ.get("TILA_B200_WS", "1") != "0":
-            # the loop has the flash-attention shape: generate the
+        if ws_fit and os.environ.get("TILA_B200_WS", "1") != "0":
+            # the loops have the flash-attention shape: generate the
             # warp-specialised kernel instead (this pass's plan is the fallback)
             try:
                 return KernelEmitter(self.tk, self.consts, self.buffers, num_warps=self._num_warps,
                                      entry_name=self.entry, debug=self.debug,
                                      versioning=self.versioning, source_map=self.source_map,
-                                     ws=self._ws_found).generate()
+                                     ws=found).generate()
             except CodegenError:
                 pass
         if self._ws is not None:

@@ -746,7 +746,7 @@ class AsyncLoopMixin:
                 self.emit(f"const tila::i64 tila_trip_{k} = ((tila::i64)({end.expr}) > (tila::i64)({start.expr})) ? "
                           f"((tila::i64)({end.expr}) - (tila::i64)({start.expr}) + {stepv - 1}) / {stepv} : 0;")
                 self.emit(f"{WG_TRIPS} {k}")
-        self.ws_detect(s, start, al, ctx)
+        self.ws_detect(s, start, end, stepv, al, ctx)
         self.actx = ctx
         return ctx
 

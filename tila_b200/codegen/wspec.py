@@ -44,6 +44,8 @@ the kernel fall back to the two-program lowering.
 
 from __future__ import annotations
 
+import dataclasses
+import math
 import re
 
 from .._reference import tila
@@ -68,7 +70,7 @@ def ws_budget(T):
     unless ptxas allocated exactly the launch count."""
     threads = 2 * T + 128
     launch = (65536 // threads) // 8 * 8
-    producer, consumer = {128: (56, 224), 256: (24, 112)}[T]
+    producer, consumer = {128: (64, 216), 256: (24, 112)}[T]
     assert 128 * producer + 2 * T * consumer <= threads * launch
     assert producer <= launch <= consumer and producer % 8 == 0 and consumer % 8 == 0
     return threads, launch, producer, consumer
@@ -77,6 +79,37 @@ def ws_budget(T):
 _IDENT = re.compile(r"[A-Za-z_][A-Za-z0-9_]*")
 _ALLOWED = {"pid_0", "pid_1", "pid_2", "tila_pit", "int", "long", "unsigned", "float", "double",
             "true", "false", "LL", "ULL", "u", "ull"}
+
+
+def _multiple_of(em, node, depth=0):
+    """A positive integer that provably divides the value of TIR expression
+    ``node`` in every program (1 when nothing is known; 0 stands for the
+    value 0, which every integer divides)."""
+    if depth > 24 or node is None:
+        return 1
+    if isinstance(node, T_.TLit) and isinstance(node.value, int) and not isinstance(node.value, bool):
+        return abs(node.value)
+    if isinstance(node, T_.TName):
+        c = em.consts.get(node.name)
+        if isinstance(c, int) and not isinstance(c, bool):
+            return abs(c)
+        d = em.pdefs.resolve(node)
+        return 1 if d is node else _multiple_of(em, d, depth + 1)
+    if isinstance(node, T_.TCast):
+        return _multiple_of(em, node.operand, depth + 1)
+    if isinstance(node, T_.TBin):
+        a, b = _multiple_of(em, node.left, depth + 1), _multiple_of(em, node.right, depth + 1)
+        if node.op == "*":
+            return a * b
+        if node.op in ("+", "-"):
+            return math.gcd(a, b)
+    return 1
+
+
+def _plan_key(plan):
+    """A TMA plan without its TIR coordinate nodes (compared by value)."""
+    return tuple((f.name, getattr(plan, f.name)) for f in dataclasses.fields(plan)
+                 if f.name not in ("coords", "coord_nodes"))
 
 
 def _portable(expr: str) -> bool:
@@ -97,40 +130,88 @@ class WarpSpecMixin:
 
     # -- first pass: is the loop of the warp-specialised shape? ------------------
 
-    def ws_detect(self, s, start, al, ctx):
-        """Record the one-shot operand of the loop's synchronous dot when the
-        loop has the flash-attention shape (see module doc) and both programs
-        of a CTA run the same trip count; programs of 4 or 8 warps."""
+    def ws_detect(self, s, start, end, stepv, al, ctx):
+        """First pass: record the loops of the warp-specialised shape.
+
+        A kernel qualifies when its asynchronous accumulator loops form one
+        chain of flash-attention-shaped loops (module doc) over the same
+        one-shot Q tile: each loop starts where the previous one ends, with
+        the same step, so that for every program the loops walk one
+        contiguous range of K/V tiles from a start that is the same for both
+        programs of a CTA (examples/fused_attention.py: one loop with
+        CAUSAL=0, the below-diagonal loop and the diagonal loop with
+        CAUSAL=1).  The two programs may run different numbers of
+        iterations; the producer serves the longer one."""
+        q = self._ws_loop_shape(s, start, al)
+        if getattr(self, "_ws_bad", False):
+            return
+        if q is None:
+            self._ws_bad, self._ws_found = True, None
+            return
+        loop = dict(start=start.expr, end=end.expr, step=int(stepv),
+                    even=all(n is None or self._pid0_free(n) for n in (s.start, s.end)))
+        found = self._ws_found
+        if found is None:
+            if s.start is not None and not self._pid0_free(s.start):
+                self._ws_bad = True
+                return
+            self._ws_found = {"q": q, "loops": [loop]}
+            self._ws_last_loop = s
+            return
+        prev, prev_node = found["loops"][-1], self._ws_last_loop
+        whole = _multiple_of(self, prev_node.start) if prev_node.start is not None else 0
+        whole = math.gcd(whole, _multiple_of(self, prev_node.end))
+        if (q != found["q"] or loop["step"] != prev["step"] or loop["start"] != prev["end"]
+                or whole % loop["step"]):
+            self._ws_bad, self._ws_found = True, None
+            return
+        found["loops"].append(loop)
+        self._ws_last_loop = s
+
+    def _ws_loop_shape(self, s, start, al):
+        """The name of the one-shot Q tile when loop ``s`` has the
+        flash-attention shape, else None."""
         from .pipeline import _walk
         if self.T not in (128, 256) or not self._pingpong_ok(s, start, al, any_T=True):
-            return
-        if any(node is not None and not self._pid0_free(node) for node in (s.start, s.end)):
-            return
+            return None
         if al.cast_loads or len(al.loads) != 2 or len(al.accs) != 1:
-            return
+            return None
         (acc_name, acc_dot), = al.accs.items()
         if not (isinstance(acc_dot.a, T_.TCast) and isinstance(acc_dot.a.operand, T_.TName)
                 and acc_dot.a.operand.name not in al.loads):
-            return
+            return None
         syncs = []
         for st in s.body:
             _walk(st.value, lambda n: syncs.append(n) if isinstance(n, T_.TDot) and n.acc is None else None)
         if len(syncs) != 1:
-            return
+            return None
         sd = syncs[0]
         if not (isinstance(sd.a, T_.TName) and isinstance(sd.b, T_.TName) and sd.b.name in al.loads
                 and sd.b.name != acc_dot.b.name):
-            return
+            return None
         q = self.env.get(sd.a.name)
         op = getattr(q, "smem", None)
         if q is None or q.kind != "smem" or op is None or op.bar is None or not op.nbytes:
-            return
-        if len(self.uses.get(sd.a.name, [])) != 1:
-            return
+            return None
         _, (M, N), _ = self.vt_info(sd.vt)
         if M != 128 or self.vt_info(acc_dot.vt)[1][0] != 128:
-            return
-        self._ws_found = {"q": sd.a.name}
+            return None
+        return sd.a.name
+
+    def ws_ready(self):
+        """The recorded chain may run warp-specialised: Q is read by the
+        chain's dots only."""
+        f = self._ws_found
+        if f is None or getattr(self, "_ws_bad", False):
+            return None
+        if len(self.uses.get(f["q"], [])) != len(f["loops"]):
+            return None
+        # 8-warp programs keep the one-loop, equal-trip form: with uneven
+        # trip counts their producer spills and the one-program-per-CTA plan
+        # is faster (742 against 688 TFLOP/s for causal attention)
+        if self.T == 256 and (len(f["loops"]) > 1 or not f["loops"][0]["even"]):
+            return None
+        return f
 
     # -- second pass: the consumer side --------------------------------------------
 
@@ -156,9 +237,13 @@ class WarpSpecMixin:
         from .mma import AsyncCtx, SmemOperand
         from .pipeline import _walk
         ws = self._ws
-        if "q_load" not in ws or ws.get("loop_done"):
+        chain = ws.get("loops") or [dict(start=start.expr, end=end.expr, step=int(stepv))]
+        k = ws.get("loops_seen", 0)
+        if ("q_load" not in ws or k >= len(chain) or chain[k]["start"] != start.expr
+                or chain[k]["end"] != end.expr or chain[k]["step"] != int(stepv)):
             self.fail("warp-specialised loop: unexpected loop structure")
-        ws["loop_done"] = True
+        ws["loops"] = chain
+        ws["loops_seen"] = k + 1
         self.uses_mma = True
         self.uses_tmem = True
         ctx = AsyncCtx(al, s.var, stepv, f"(tila::i64)({end.expr})", {}, {})
@@ -180,6 +265,8 @@ class WarpSpecMixin:
         for name, ld in al.loads.items():
             ctx.loads[name] = dict(plan=self.tma_plan(ld), node=ld, base=None, bar=None,
                                    phase=None, flag=None)
+        if k > 0:
+            return self._ws_loop_continue(s, ctx, acc_name, acc_dot, k_name, v_name)
         _, (M, N), _ = self.vt_info(acc_dot.vt)
         col = self.tmem_alloc_cols(N)
         self._loop_acc_cols.add((str(col), N))
@@ -211,23 +298,9 @@ class WarpSpecMixin:
         self.emit(f"{a['phase']} = 0u; {a['pend']} = 0u;")
         self.env[acc_name] = Val("tmem", D.f32, (128, N), tmem_col=str(col))
         # producer templates: TMA copies of K and V for loop value tila_pit
-        saved_env, saved_lines, saved_indent = dict(self.env), self.lines, self.indent
-        self.lines, self.indent = [], 0
-        try:
-            self._functional_prefix(ctx, "tila_pit")
-            copies = {}
-            for name in (k_name, v_name):
-                x = ctx.loads[name]
-                coords = [self.value(c) for c in x["node"].coords]
-                copies[name] = dict(plan=x["plan"], coords=self._tma_coords(x["plan"], coords))
-                self.tensor_map_param(x["plan"])
-            stray = [ln for ln in self.lines if ln.strip()]
-        finally:
-            self.env, self.lines, self.indent = saved_env, saved_lines, saved_indent
-        if stray or not all(_portable(c) for cp in copies.values() for c in cp["coords"]):
-            self.fail("warp-specialised loop: K/V copies depend on program-local values")
-        for e in (start.expr, end.expr):
-            if not _portable(e):
+        copies = self._ws_kv_copies(ctx, k_name, v_name)
+        for loop in chain:
+            if not (_portable(loop["start"]) and _portable(loop["end"])):
                 self.fail("warp-specialised loop: loop bounds depend on program-local values")
         # MMA templates (@QB@, @KB@, @VB@: byte offsets in the CTA's shared memory)
         q = ws["q_load"]
@@ -253,9 +326,54 @@ class WarpSpecMixin:
             pv_mma.append(f"tila::mma_f16_ts(@TM@ + {col}, @TM@ + @SCOL@ + {kk * 8}, {db}, "
                           f"tila::idesc_f16_f32(128, {N}, 0, {vb_mn}), 1u);")
         ws.update(k=copies[k_name], v=copies[v_name], s_mma=s_mma, pv_mma=pv_mma,
-                  start=start.expr, end=end.expr, step=stepv, acc_bar=bar_off, p_full=p_full,
-                  acc_col=col)
+                  step=stepv, acc_bar=bar_off, p_full=p_full, acc_col=col,
+                  acc_entry=ctx.accs[acc_name], acc_name=acc_name)
         self._wg_candidate = True
+        self.actx = ctx
+        return ctx
+
+    def _ws_kv_copies(self, ctx, k_name, v_name):
+        """TMA plans and coordinates of the loop's K and V copies for loop
+        value ``tila_pit`` (the producer's); they must read nothing but the
+        program ids, kernel parameters and the loop value, and not depend on
+        program_id(0): both programs of the CTA share the stream."""
+        saved_env, saved_lines, saved_indent = dict(self.env), self.lines, self.indent
+        self.lines, self.indent = [], 0
+        try:
+            self._functional_prefix(ctx, "tila_pit")
+            copies = {}
+            for name in (k_name, v_name):
+                x = ctx.loads[name]
+                coords = [self.value(c) for c in x["node"].coords]
+                copies[name] = dict(plan=x["plan"], coords=self._tma_coords(x["plan"], coords))
+                self.tensor_map_param(x["plan"])
+            stray = [ln for ln in self.lines if ln.strip()]
+        finally:
+            self.env, self.lines, self.indent = saved_env, saved_lines, saved_indent
+        if stray or not all(_portable(c) and not re.search(r"\bpid_0\b", c)
+                            for cp in copies.values() for c in cp["coords"]):
+            self.fail("warp-specialised loop: K/V copies depend on program-local values")
+        return copies
+
+    def _ws_loop_continue(self, s, ctx, acc_name, acc_dot, k_name, v_name):
+        """A later loop of the chain: the accumulator, its barriers and phase
+        variables and the producer's templates carry over from the first loop
+        (its iterations continue the same stream of K/V tiles and MMAs)."""
+        from .emitter import Val
+        ws = self._ws
+        if acc_name != ws["acc_name"] or self.vt_info(acc_dot.vt)[1][1] != ws["acc_entry"]["N"]:
+            self.fail("warp-specialised loop: the loops accumulate into different tiles")
+        copies = self._ws_kv_copies(ctx, k_name, v_name)
+        for cur, first in ((copies[k_name], ws["k"]), (copies[v_name], ws["v"])):
+            if cur["coords"] != first["coords"] or _plan_key(cur["plan"]) != _plan_key(first["plan"]):
+                self.fail("warp-specialised loop: the loops copy different K/V tiles")
+        pre = self.env.get(acc_name)
+        if pre is None or pre.kind != "tmem" or str(pre.tmem_col) != str(ws["acc_col"]):
+            self.fail("warp-specialised loop: the accumulator left tensor memory between the loops")
+        ctx.accs[acc_name] = dict(ws["acc_entry"], dot=acc_dot)
+        ctx.p_full_off = ws["p_full"]
+        self.emit(f"// warp-specialised loop over {s.var} (continues the previous loop's stream)")
+        self.env[acc_name] = Val("tmem", D.f32, (128, ws["acc_entry"]["N"]), tmem_col=str(ws["acc_col"]))
         self.actx = ctx
         return ctx
 
@@ -309,10 +427,13 @@ class WarpSpecMixin:
         return v
 
     def ws_finish(self, ctx):
-        """After the loop: the Q tile is dead (its last reader, S of the last
-        iteration, completed before the final P@V); its shared memory can stage
-        the epilogue's stores."""
-        q = self._ws["q_load"]
+        """After the last loop of the chain: the Q tile is dead (its last
+        reader, S of the last iteration, completed before the final P@V); its
+        shared memory can stage the epilogue's stores."""
+        ws = self._ws
+        if ws["loops_seen"] < len(ws["loops"]):
+            return
+        q = ws["q_load"]
         self._free_smem.append((q["off"], q["size"]))
 
     # -- assembly ------------------------------------------------------------------
@@ -358,10 +479,27 @@ class WarpSpecMixin:
                 e("      " + ln)
 
         step = ws["step"]
+        # per program w: its iterations over the chain of loops (bounds
+        # evaluated with its own program id), which must walk one contiguous
+        # range from the first loop's start (that start is the same for both
+        # programs, so the shorter program's tiles are a prefix of the other's)
         head = ["    const bool tila_live_w[2] = {(tila::i32)(blockIdx.x * 2) < launch_0, "
                 "(tila::i32)(blockIdx.x * 2 + 1) < launch_0};",
-                f"    const tila::i64 tila_lo = (tila::i64)({ws['start']}), tila_hi = (tila::i64)({ws['end']});",
-                f"    const tila::i64 tila_n = tila_hi > tila_lo ? (tila_hi - tila_lo + {step - 1}) / {step} : 0;"]
+                f"    const tila::i64 tila_lo = (tila::i64)({ws['loops'][0]['start']});",
+                "    tila::i64 tila_nw[2] = {0, 0};",
+                "    bool tila_chain_ok = true;"]
+        for w in range(2):
+            head.append(f"    if (tila_live_w[{w}]) {{")
+            head.append(f"      const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + {w} + pid_off_0); (void)pid_0;")
+            head.append("      tila::i64 pos_ = tila_lo;")
+            for loop in ws["loops"]:
+                head.append(f"      {{ const tila::i64 s_ = (tila::i64)({loop['start']}), e_ = (tila::i64)({loop['end']});")
+                head.append(f"        const tila::i64 t_ = e_ > s_ ? (e_ - s_ + {step - 1}) / {step} : 0;")
+                head.append(f"        if (t_ > 0 && s_ != pos_) tila_chain_ok = false;")
+                head.append(f"        tila_nw[{w}] += t_; if (t_ > 0) pos_ = s_ + t_ * {step}; }}")
+            head.append("    }")
+        head.append("    if (!tila_chain_ok) tila_nw[0] = tila_nw[1] = 0;")
+        head.append("    const tila::i64 tila_n = tila_nw[0] > tila_nw[1] ? tila_nw[0] : tila_nw[1];")
 
         # -- copy thread (threadIdx.x == 256): Q once, then K and V of every
         #    iteration into stage j & 1 as soon as the MMAs that read the
@@ -369,7 +507,9 @@ class WarpSpecMixin:
         e("    // copies: both programs' Q tiles, then K and V through the two-stage ring")
         L.extend(head)
         for w in range(2):
-            e(f"    if (tila_live_w[{w}]) {{")
+            # (a program with no iterations never waits for its Q tile, so
+            # none is copied: its epilogue reuses that shared memory)
+            e(f"    if (tila_nw[{w}] > 0) {{")
             e(f"      const tila::i32 pid_0 = (tila::i32)(blockIdx.x * 2 + {w} + pid_off_0);")
             e(f"      tila::mbar_arrive_expect_tx({region(w, q['bar_off'])}, {q['plan'].bytes}u);")
             tma(q["plan"], q["coords"], w * per_prog + q["off"], region(w, q["bar_off"]))
@@ -390,19 +530,21 @@ class WarpSpecMixin:
         copy_lines = list(L)
         L.clear()
 
-        # -- MMA thread (threadIdx.x == 288): per program P@V(j), then S(j+1)
+        # -- MMA thread: per iteration j and program w (while j < its trip
+        #    count) P@V(j), then S(j+1) into the columns P@V(j) has just read
         e("    // MMAs: S = Q K^T and O += P V of both programs, in issue order per program")
         e("    const tila::u32 tila_sb4 = tila::smem_u32(tila_smem_all) >> 4;")
         L.extend(head)
+        e("    if (!tila_chain_ok) { tila::report_error(tila_err, tila::kErrSchedule, __LINE__); tila_dead = 1; }")
         e("    if (tila_n > 0) {")
         for w in range(2):
-            e(f"      if (tila_live_w[{w}]) {{")
+            e(f"      if (tila_nw[{w}] > 0) {{")
             e(f"        if (!tila::mbar_wait({region(w, q['bar_off'])}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
             e("      }")
         e(f"      if (!tila::mbar_wait({k_full[0]}, 0u, tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
         e("      tila::tc_fence_after();")
         for w in range(2):
-            e(f"      if (tila_live_w[{w}]) {{")
+            e(f"      if (tila_nw[{w}] > 0) {{")
             mmas(ws["s_mma"], w, qb=w * per_prog + q["off"], kb=str(kring[0]))
             e(f"        tila::mma_commit({region(w, 0)});")
             e("      }")
@@ -417,17 +559,17 @@ class WarpSpecMixin:
         e(f"      const tila::u32 vb = st ? {vring[1]}u : {vring[0]}u;")
         e(f"      const tila::u32 kb = nx ? {kring[1]}u : {kring[0]}u;")
         for w in range(2):
-            e(f"      if (tila_live_w[{w}]) {{")
+            e(f"      if (j < tila_nw[{w}]) {{")
             e(f"        if (!tila::mbar_wait({region(w, ws['p_full'])}, (tila::u32)(j & 1), tila_err, __LINE__, &tila_dead)) goto tila_mma_end;")
             e("        tila::tc_fence_after();")
             mmas(ws["pv_mma"], w, vb="vb")
             e(f"        tila::mma_commit({region(w, ws['acc_bar'])});")
-            e("        if (more) {")
+            e(f"        if (j + 1 < tila_nw[{w}]) {{")
             mmas(ws["s_mma"], w, qb=w * per_prog + q["off"], kb="kb")
             e(f"          tila::mma_commit({region(w, 0)});")
             e("        }")
             e("      }")
-        e("      // stage frees: K of iteration j + 1 once both S(j + 1) are done, V of j once both P@V(j) are")
+        e("      // stage frees: K of iteration j + 1 once the S(j + 1) that read it are done, V of j once the P@V(j) are")
         e(f"      if (more) tila::mma_commit(nx ? {k_empty[1]} : {k_empty[0]});")
         e(f"      tila::mma_commit(st ? {v_empty[1]} : {v_empty[0]});")
         e("    }")

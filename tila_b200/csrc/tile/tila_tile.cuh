@@ -34,6 +34,7 @@ enum ErrorCode : u32 {
   kErrMbarrierTimeout = 1,   // a bounded mbarrier wait gave up
   kErrTmemAlloc = 2,         // tensor memory allocation failed
   kErrAssumption = 3,        // a ti.assume predicate was false (debug builds)
+  kErrSchedule = 4,          // a warp-specialised loop chain was not contiguous at run time
 };
 
 // Records the first error of a launch.  `err` points at the launch's 16-byte
