@@ -92,6 +92,43 @@ def test_reference_fused_attention_takes_two_program_plan(causal):
     assert "tila_nw[1]" in spec.source and "kErrSchedule" in spec.source
 
 
+def test_heavy_first_cta_order_is_a_bijection():
+    """The causal kernel renumbers its CTAs heaviest-first within groups of
+    heads (wspec.cta_order_prelude); the prelude, evaluated here for grids
+    whose head count is and is not a multiple of the group, maps the
+    dispatch order onto every CTA exactly once."""
+    import re
+    from tila_b200.codegen.wspec import CTA_GROUP, cta_order_prelude
+    q = torch.zeros(2, 512, 128, dtype=f16)
+    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+               CAUSAL=1, BM=128, BN=128, BD=128)
+    assert cta_order_prelude(True) in spec.source
+    body = spec.source.split(cta_order_prelude(True), 1)[1]
+    assert "blockIdx" not in body
+    src = cta_order_prelude(True)
+    stmts = re.findall(r"const (?:unsigned|bool) ([^;]*);", src)
+
+    def run(lin, X, Y, Z):
+        env = dict(gridDim=None)
+        vals = {"gridDim.x": X, "gridDim.y": Y, "gridDim.z": Z, "blockIdx.x": lin % X,
+                "blockIdx.y": (lin // X) % Y, "blockIdx.z": lin // (X * Y)}
+        for st in stmts:
+            for decl in re.split(r",\s*(?=tila_)", st):
+                name, expr = decl.split("=", 1)
+                e = expr
+                for k, v in sorted(vals.items(), key=lambda kv: -len(kv[0])):
+                    e = re.sub(r"\b" + re.escape(k) + r"\b", str(v), e)
+                e = e.replace("u", "").replace("/", "//").replace("?", " if ").replace(":", " else ")
+                e = re.sub(r"(.*) if (.*) else (.*)", r"(\2) if (\1) else (\3)", e)
+                vals[name.strip()] = int(eval(e))
+        return vals["tila_bx"], vals["tila_by"], vals["tila_bz"]
+    for X, Y, Z in [(16, 128, 1), (4, CTA_GROUP + 3, 1), (3, 5, 2), (1, 1, 1)]:
+        seen = {run(lin, X, Y, Z) for lin in range(X * Y * Z)}
+        assert len(seen) == X * Y * Z and all(0 <= a < X and 0 <= b < Y and 0 <= c < Z for a, b, c in seen)
+    # the first CTAs dispatched run the heaviest (last) axis-0 position
+    assert run(0, 16, 128, 1)[0] == 15
+
+
 def test_warp_specialised_budgets_fit_the_launch_pool():
     """Every warpgroup's setmaxnreg share adds up to at most the registers the
     CTA is launched with (threads x launch registers), for 4- and 8-warp

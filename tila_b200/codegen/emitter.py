@@ -2651,6 +2651,12 @@ def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, s
     e(f"  if (threadIdx.x < 32) tila::tmem_dealloc(*tila_tmem_slot, {cta_cols});")
     e("}")
     src = "\n".join(out) + "\n"
+    if self._ws.get("heavy_last") is not None:
+        from .wspec import cta_order_prelude
+        decl = "  extern __shared__ __align__(1024) unsigned char tila_smem_all[];\n"
+        head, body = src.split(decl, 1)
+        body = body.replace("blockIdx.x", "tila_bx").replace("blockIdx.y", "tila_by").replace("blockIdx.z", "tila_bz")
+        src = head + decl + cta_order_prelude(self._ws["heavy_last"]) + body
     self.fuse = {0: 2}
     tmem_cols = cta_cols
     return KernelSpec(self.entry, src, threads, max(total, 233472 // 2 - 1024 + 1), params,

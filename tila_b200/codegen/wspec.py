@@ -106,6 +106,58 @@ def _multiple_of(em, node, depth=0):
     return 1
 
 
+def _eval_at_pid0(em, node, pid0, depth=0):
+    """Value of integer TIR expression ``node`` with program_id(0) = pid0,
+    when it is built from that id, Consts and literals only (else None)."""
+    if depth > 24 or node is None:
+        return None
+    if isinstance(node, T_.TPid):
+        return pid0 if node.axis == 0 else None
+    if isinstance(node, T_.TLit) and isinstance(node.value, int) and not isinstance(node.value, bool):
+        return node.value
+    if isinstance(node, T_.TName):
+        c = em.consts.get(node.name)
+        if isinstance(c, int) and not isinstance(c, bool):
+            return c
+        d = em.pdefs.resolve(node)
+        return None if d is node else _eval_at_pid0(em, d, pid0, depth + 1)
+    if isinstance(node, T_.TCast):
+        return _eval_at_pid0(em, node.operand, pid0, depth + 1)
+    if isinstance(node, T_.TBin) and node.op in ("+", "-", "*"):
+        a = _eval_at_pid0(em, node.left, pid0, depth + 1)
+        b = _eval_at_pid0(em, node.right, pid0, depth + 1)
+        if a is None or b is None:
+            return None
+        return a + b if node.op == "+" else a - b if node.op == "-" else a * b
+    return None
+
+
+# heads (grid axes 1 and 2) per group of the heavy-first CTA order
+CTA_GROUP = 8
+
+
+def cta_order_prelude(heavy_last):
+    """Kernel prologue that renumbers the CTAs of a grid whose programs' work
+    grows (``heavy_last``) or shrinks along axis 0: CTAs are dispatched in
+    linear order, and the renumbering hands out, for every group of
+    CTA_GROUP positions along axes 1 and 2, the heaviest axis-0 position
+    first.  The long CTAs then start early (no tail of long CTAs on a few
+    SMs) while the CTAs running at one time share a few groups' tiles in
+    L2.  A bijection of the grid; programs compute what they computed."""
+    bx = "tila_X - 1u - tila_q" if heavy_last else "tila_q"
+    return f"""  // CTA order: heaviest axis-0 position first within groups of {CTA_GROUP} positions along axes 1-2
+  const unsigned tila_X = gridDim.x, tila_YZ = gridDim.y * gridDim.z;
+  const unsigned tila_lin = blockIdx.x + tila_X * (blockIdx.y + gridDim.y * blockIdx.z);
+  const unsigned tila_full = tila_YZ / {CTA_GROUP}u * {CTA_GROUP}u;
+  const bool tila_in_full = tila_lin < tila_full * tila_X;
+  const unsigned tila_gs = tila_in_full ? {CTA_GROUP}u : tila_YZ - tila_full;
+  const unsigned tila_base = tila_in_full ? tila_lin / ({CTA_GROUP}u * tila_X) * {CTA_GROUP}u : tila_full;
+  const unsigned tila_r = tila_in_full ? tila_lin % ({CTA_GROUP}u * tila_X) : tila_lin - tila_full * tila_X;
+  const unsigned tila_q = tila_r / tila_gs, tila_h = tila_base + tila_r % tila_gs;
+  const unsigned tila_bx = {bx}, tila_by = tila_h % gridDim.y, tila_bz = tila_h / gridDim.y;
+"""
+
+
 def _plan_key(plan):
     """A TMA plan without its TIR coordinate nodes (compared by value)."""
     return tuple((f.name, getattr(plan, f.name)) for f in dataclasses.fields(plan)
@@ -211,6 +263,14 @@ class WarpSpecMixin:
         # is faster (742 against 688 TFLOP/s for causal attention)
         if self.T == 256 and (len(f["loops"]) > 1 or not f["loops"][0]["even"]):
             return None
+        # programs whose trip counts grow or shrink with program_id(0): the
+        # CTAs are renumbered heaviest-first (see cta_order_prelude)
+        f["heavy_last"] = None
+        if not all(loop["even"] for loop in f["loops"]):
+            last = self._ws_last_loop
+            n0, n1 = _eval_at_pid0(self, last.end, 0), _eval_at_pid0(self, last.end, 1)
+            if n0 is not None and n1 is not None and n0 != n1:
+                f["heavy_last"] = n1 > n0
         return f
 
     # -- second pass: the consumer side --------------------------------------------
