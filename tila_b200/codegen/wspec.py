@@ -1,13 +1,17 @@
 """Warp-specialised lowering of the online-softmax attention loop.
 
 Applies to the asynchronous accumulator loops that already run two programs
-per CTA (one per warpgroup, see ``AsyncLoopMixin._pingpong_ok``) when the loop
-has exactly the flash-attention shape: one synchronous dot ``S = dot(Q, K)``
-whose A operand is a one-shot TMA tile loaded before the loop and whose B
-operand is an in-loop TMA tile, and one accumulating dot
-``acc = dot(cast[f16](P), V, acc=acc)`` with V an in-loop TMA tile, the same
-trip count for both programs (examples/fused_attention.py:104-126, the
-CAUSAL=0 loop).
+per CTA (one per warpgroup, see ``AsyncLoopMixin._pingpong_ok``) when the
+loops have exactly the flash-attention shape: one synchronous dot
+``S = dot(Q, K)`` whose A operand is a one-shot TMA tile loaded before the
+loop and whose B operand is an in-loop TMA tile, and one accumulating dot
+``acc = dot(cast[f16](P), V, acc=acc)`` with V an in-loop TMA tile.  The
+kernel may have one such loop or a chain of them in which every loop starts
+where the previous one ends (examples/fused_attention.py:104-126, the
+CAUSAL=0 loop; 62-103, the CAUSAL=1 loops below and on the diagonal); in
+every program the chain then walks one contiguous range of K/V tiles from a
+start that both programs of a CTA share, so the shorter program's tiles are
+a prefix of the longer one's.
 
 The CTA then has three roles instead of two programs that each issue their own
 copies and MMAs:
@@ -16,15 +20,19 @@ copies and MMAs:
   the CUDA-core part of each iteration: wait for S in tensor memory, compute
   the softmax update, rescale the accumulator in place, store P (f16) into
   tensor memory and arrive on the program's "P ready" barrier;
-* one producer thread (256, in the third warpgroup, whose other warps idle)
-  loads both programs' Q
-  tiles once and streams K and V through a two-stage ring shared by the two
-  programs (each tile crosses L2 once per CTA instead of once per program),
-  and issues every ``tcgen05.mma``: for each program in turn P@V of iteration
-  j, then S of iteration j + 1, so the tensor pipe always holds the other
-  program's work while one program is in its softmax;
-* the two softmax warpgroups are no longer serialised by a hand-off: both
-  run concurrently (two warps per SM sub-partition during the exponentials).
+* a copy thread (first thread of the third warpgroup) loads both programs'
+  Q tiles once and streams K and V through a two-stage ring shared by the
+  two programs (each tile crosses L2 once per CTA instead of once per
+  program), as many tiles as the longer program needs;
+* an MMA thread (first thread of the next warp) issues every
+  ``tcgen05.mma``: per iteration, for each program that still runs, P@V of
+  iteration j, then S of iteration j + 1, so the tensor pipe holds the other
+  program's work while one program is in its softmax.  Each program's
+  iterations are counted from its own program id (``tila_nw``); a run-time
+  check of the chain's contiguity records ``kErrSchedule`` if it fails;
+* the two softmax warpgroups are not serialised by a hand-off: both run
+  concurrently; ``setmaxnreg`` moves registers from the producer warpgroup
+  to them (``ws_budget``).
 
 Barriers (all waits bounded, see ``tila::mbar_wait``): per program the S
 barrier (``tila_mma_bar``, committed by the producer after S), the
@@ -36,10 +44,15 @@ P@V(j), overwrites the tensor-memory columns that P@V(j) reads only after
 that MMA consumed them, and a consumer that has waited for S(j + 1) knows that
 P@V(j) is complete.
 
+When the programs' trip counts grow (or shrink) with program_id(0), the CTAs
+are renumbered so that the heaviest start first within groups of CTA_GROUP
+positions along the other grid axes (``cta_order_prelude``).
+
 The producer's code is built from the same TMA plans, descriptors and
 coordinate expressions as the consumer's would be; a coordinate that depends
-on anything but the program ids, kernel parameters and the loop variable makes
-the kernel fall back to the two-program lowering.
+on anything but the program ids, kernel parameters and the loop variable, or
+K/V coordinates that depend on program_id(0), make the kernel fall back to
+the two-program lowering.
 """
 
 from __future__ import annotations
