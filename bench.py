@@ -740,7 +740,7 @@ def cpu_baseline(key, repeats=1):
     dt = (time.perf_counter() - t0) / repeats
     return {"value": units / dt / scale, "unit": unit, "cores": cores, "kind": "reference",
             "sample": f"Tila NumPy interpreter, {sample}; {repeats} run(s) of "
-                      f"{dt:.3f} s on {os.cpu_count()} host cores"}
+                      f"{dt:.3f} s, {cores} thread(s) of {os.cpu_count()} host cores"}
 
 
 # ---------------------------------------------------------------------------
