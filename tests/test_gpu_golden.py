@@ -58,3 +58,20 @@ def test_causal_flash_attention_128_tiles(l, d, warps):
     assert tila_b200.read_device_errors() == 0
     ref = restate.attention_f64(q, k, v, causal=True)
     assert restate.rel_frobenius(o.cpu().numpy(), ref) <= 2e-3
+
+
+def test_causal_flash_attention_heavy_first_order():
+    """11 heads at L=1000: the heavy-first CTA numbering of the causal kernel
+    covers one full group of 8 heads and a partial group of 3; every query
+    block of every head is computed once (eight blocks, the last partial)."""
+    q, k, v = W.attention_inputs(11, 1000, 128, seed=23)
+    o = torch.full(q.shape, float("nan"), dtype=torch.float32, device="cuda")
+    W.fused_attention_kernel[(-(-1000 // 128), 11)](
+        _cuda(q), _cuda(k), _cuda(v), o, 128 ** -0.5, CAUSAL=1, BM=128, BN=128, BD=128)
+    torch.cuda.synchronize()
+    assert tila_b200.read_device_errors() == 0
+    got = o.cpu().numpy()
+    assert np.isfinite(got).all()
+    for h in (0, 7, 8, 10):
+        ref = restate.attention_f64(q[h:h + 1], k[h:h + 1], v[h:h + 1], causal=True)
+        assert restate.rel_frobenius(got[h:h + 1], ref) <= 2e-3
