@@ -42,9 +42,50 @@ def test_matmul_uses_tma_ring_and_tcgen05():
     spec = gen(W.matmul_kernel, t, BM=128, BN=128, BK=64)
     # a 2 x 2 block of programs per CTA sharing A and B tiles, N = 256 MMAs
     assert "2x2 programs per CTA" in spec.source and spec.fuse == {0: 2, 1: 2}
+    assert not spec.persistent
     assert "tma_load_2d" in spec.source and "idesc_f16_f32(128, 256" in spec.source
     assert len(spec.tensor_maps) == 3          # A, B loads and the C store
     assert spec.tmem_cols == 512 and spec.smem_bytes <= 227 * 1024
+
+
+def test_matmul_persistent_form_is_opt_in(monkeypatch):
+    """TILA_B200_STREAMK=1 gives the persistent contraction (K loops split
+    evenly over one CTA per SM when there are more tiles than SMs), with its
+    workspace and flag arguments; it compiles."""
+    monkeypatch.setenv("TILA_B200_STREAMK", "1")
+    t = dict(a=torch.zeros(256, 256, dtype=f16), b=torch.zeros(256, 256, dtype=f16), c=torch.zeros(256, 256))
+    spec = gen(W.matmul_kernel, t, BM=128, BN=128, BK=64)
+    assert "2x2-program tiles" in spec.source and spec.fuse == {0: 2, 1: 2}
+    assert spec.persistent and {"skws", "skflags"} <= {k for k, _, _ in spec.params}
+    native.compile_spec(spec)
+
+
+def test_streamk_split_covers_every_unit_once():
+    """The persistent contraction's split (CTA b takes units [T b / P,
+    T (b + 1) / P)) with P = #SMs and more tiles than SMs: every (tile, K
+    step) unit is computed exactly once; a CTA's pieces are an optional
+    high-K part first, whole tiles, an optional low-K part last; and every
+    parked high-K part is finished by the previous CTA."""
+    for tiles, kn, P in [(256, 64, 148), (149, 64, 148), (1000, 7, 148), (300, 1, 148)]:
+        total = tiles * kn
+        seen = {}
+        for b in range(P):
+            u0, u1 = total * b // P, total * (b + 1) // P
+            assert u1 - u0 >= kn
+            pieces, p = [], u0
+            while p < u1:
+                t, ka = divmod(p, kn)
+                end = min((t + 1) * kn, u1)
+                pieces.append((t, ka, end - t * kn))
+                for u in range(p, end):
+                    seen[u] = seen.get(u, 0) + 1
+                p = end
+            kinds = ["park" if ka > 0 else "fin" if kb < kn else "full" for _, ka, kb in pieces]
+            assert "park" not in kinds[1:] and "fin" not in kinds[:-1]
+            if kinds[-1] == "fin":
+                nxt = total * (b + 1) // P
+                assert nxt % kn and nxt // kn == pieces[-1][0]     # CTA b + 1 parks this tile
+        assert len(seen) == total and set(seen.values()) == {1}
 
 
 def test_matmul_strided_falls_back_to_register_staging():

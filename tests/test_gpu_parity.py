@@ -271,3 +271,24 @@ def test_batched_matmul_contraction_ring(tmp_path, shape):
     got = c.cpu().numpy()
     for h in range(bsz):
         assert np.all(np.abs(got[h] - restate.matmul_f64(a[h], b[h])) <= restate.matmul_bound(a[h], b[h]))
+
+
+@pytest.mark.parametrize("k", [320, 4096])
+def test_matmul_persistent_split_matches_f64(monkeypatch, k):
+    """The opt-in persistent contraction (TILA_B200_STREAMK=1) at 4096 x 4096
+    outputs: 256 tiles of 2 x 2 programs on one CTA per SM, K loops split
+    evenly, tiles parked by one CTA and finished by the previous one (with
+    K = 320 nearly every CTA does both).  Every element within the K*eps_f32
+    bound of the f64 product."""
+    monkeypatch.setenv("TILA_B200_STREAMK", "1")
+    kernel = ti.jit(W.matmul_kernel.fn)
+    a, b = W.matmul_inputs(4096, 4096, k, seed=29)
+    c = torch.zeros((4096, 4096), dtype=torch.float32, device="cuda")
+    kernel[(32, 32)](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)
+    _no_device_errors()
+    from tila_b200.backend import last_launch
+    assert last_launch(kernel).entry.spec.persistent and last_launch(kernel).grid[0] < 256
+    rows = np.random.default_rng(k).choice(4096, 256, replace=False)
+    got = c.cpu().numpy()[rows]
+    want = restate.matmul_f64(a[rows], b)
+    assert np.all(np.abs(got - want) <= restate.matmul_bound(a[rows], b))

@@ -138,6 +138,7 @@ def check_device_errors(device=None) -> None:
     word = b.pending()
     if word:
         b.clear()
+        _reset_streamk_flags(torch.device("cuda", idx))
         raise TilaError("TILA-TARGET-005", "a kernel launched earlier on this device failed",
                         Loc(word & 0xFFFFFF),
                         details=[f"device: cuda:{idx}", f"error: {describe_error(word)}"],
@@ -156,6 +157,7 @@ def read_device_errors(device=None, reset=True) -> int:
     val = int(b.block[0].item()) & 0xFFFFFFFF
     if reset and (val or b.pending()):
         b.clear()
+        _reset_streamk_flags(device)
     return val
 
 
@@ -331,7 +333,7 @@ def _tensor_map(t, info):
     return tm
 
 
-def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word, launch_grid):
+def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word, launch_grid, extra=None):
     args = []
     for kind, name, ct in entry.spec.params:
         if kind in ("buffer", "ptr"):
@@ -358,6 +360,8 @@ def pack_args(entry: Compiled, tk, tensors, scalar_vals, grid, pid_off, err_word
             args.append(ctypes.c_int32(launch_grid[name]))
         elif kind == "err":
             args.append(ctypes.c_uint64(err_word.data_ptr()))
+        elif kind in ("skws", "skflags"):
+            args.append(ctypes.c_uint64(extra[kind].data_ptr()))
         elif kind == "tensormap":
             args.append(_tensor_map(tensors[ct["buffer"]], ct))
         else:
@@ -399,12 +403,16 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
             launch_grid[ax] = hi - lo
             pid_off[ax] = lo
         err = _error_word(device)
-        args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err, launch_grid)
         stream = torch.cuda.current_stream(device).cuda_stream
         cuda_grid = list(launch_grid)
         for ax, f in entry.spec.fuse.items():        # CTAs that run blocks of programs
             cuda_grid[ax] = -(-cuda_grid[ax] // f)
-        record = LaunchRecord(entry, tuple(cuda_grid), args, device, tensors)
+        extra = None
+        if entry.spec.persistent:
+            cuda_grid, extra = _streamk_geometry(cuda_grid, device, stream)
+        args = pack_args(entry, tk, tensors, scalar_vals, g, pid_off, err, launch_grid, extra)
+        record = LaunchRecord(entry, tuple(cuda_grid), args, device,
+                              dict(tensors, **(extra or {})))
         jf._b200_last_launch = record
         try:
             record.launch(stream)
@@ -421,6 +429,55 @@ def execute(launcher, tensors, scalar_vals, stride_vals, consts, grid):
                 read_device_errors(device)
                 raise AssertionError(f"device_assert failed: ti.assume at line {word & 0xFFFFFF} "
                                      f"of {tk.name} (TILA_DEBUG=1)")
+
+
+# Stream-K contraction kernels (codegen/fused.py): the persistent CTAs' workspace
+# slots (one per CTA: 4 programs x 128 x 128 f32 partial accumulators) and the
+# flags that hand a tile's parked high-K part to the CTA that finishes it.  One
+# set per device and stream, so that launches on different streams never share
+# them; launches on one stream are ordered.  Every flag a launch sets is
+# cleared by the same launch.
+_SK_SLOT_BYTES = 4 * 128 * 128 * 4
+_SK_MAX_BYTES = 256 << 20
+_sk_buffers = {}
+
+
+def _streamk_geometry(cuda_grid, device, stream):
+    """Grid of a stream-K launch: as many CTAs as SMs when there are more
+    tiles than SMs (the K loops are then split evenly over them), one CTA per
+    tile otherwise; axis 2 stays on z.  Returns (grid, workspace args)."""
+    import torch
+    tiles = cuda_grid[0] * cuda_grid[1]
+    sms = _sm_count(device)
+    split = tiles > sms and cuda_grid[2] == 1 and cuda_grid[2] * sms * _SK_SLOT_BYTES <= _SK_MAX_BYTES
+    nct = sms if split else tiles
+    key = (device.index, int(stream))
+    bufs = _sk_buffers.get(key)
+    slots = cuda_grid[2] * nct if split else 1
+    if bufs is None or bufs["skflags"].numel() < slots:
+        bufs = {"skws": torch.empty(slots * _SK_SLOT_BYTES // 4, dtype=torch.float32, device=device),
+                "skflags": torch.zeros(slots, dtype=torch.int32, device=device)}
+        _sk_buffers[key] = bufs
+    return [nct, 1, cuda_grid[2]], bufs
+
+
+_sm_counts = {}
+
+
+def _sm_count(device):
+    import torch
+    n = _sm_counts.get(device.index)
+    if n is None:
+        n = _sm_counts[device.index] = torch.cuda.get_device_properties(device).multi_processor_count
+    return n
+
+
+def _reset_streamk_flags(device):
+    """After a device error a launch may have stopped between parking a tile
+    and clearing its flag: clear every flag of the device."""
+    for (dev, _), bufs in _sk_buffers.items():
+        if dev == device.index:
+            bufs["skflags"].zero_()
 
 
 def launch_flags() -> int:

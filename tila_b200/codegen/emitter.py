@@ -261,6 +261,7 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         # first generation found ({"q": name of the loop's one-shot operand})
         self._ws = dict(ws) if ws else None
         self._ws_found = None
+        self.persistent = False     # the stream-K contraction (fused.py)
         self.source_map = source_map     # annotate the output with Tila source lines
         self.versioning = versioning     # loop bodies specialised for interior tiles
         self.consts = dict(consts)
@@ -2413,6 +2414,12 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         for ax in sorted(self.fuse or {}):
             sig.append(f"tila::i32 launch_{ax}")
             params.append(("launch", ax, "i32"))
+        if self.persistent:
+            # workspace and flags of the split tiles (one slot per CTA)
+            sig.append("float* __restrict__ tila_sk_ws")
+            params.append(("skws", None, "ptr"))
+            sig.append("tila::u32* __restrict__ tila_sk_flags")
+            params.append(("skflags", None, "ptr"))
         for tm in self.tensor_maps:
             sig.append(f"const __grid_constant__ tila::TensorMap {tm['param']}")
             params.append(("tensormap", tm["param"], tm))
@@ -2553,7 +2560,8 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         return KernelSpec(self.entry, src, threads, smem, params, fp_contract=self.uses_mma or self._contracted,
                           assume_lines=list(self._assume_lines),
                           tmem_cols=self.tmem_cols,
-                          tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}))
+                          tensor_maps=list(self.tensor_maps), fuse=dict(self.fuse or {}),
+                          persistent=self.persistent)
 
 
 def _ws_generate_impl(self, sig, params, per_prog, body, scratch_off, red_off, scratch_col, cta_cols):

@@ -480,6 +480,37 @@ __device__ __forceinline__ bool mbar_wait(u64 *bar, u32 parity, u32 *err, u32 wh
   return false;
 }
 
+// Hand-off flags between CTAs of one grid (global memory, GPU scope): a CTA
+// writes data, synchronises its threads, and one thread releases the flag; a
+// reader acquires it (bounded wait) and synchronises its threads before
+// reading the data.
+__device__ __forceinline__ void flag_release(u32 *flag, u32 v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+__device__ __forceinline__ u32 flag_acquire(const u32 *flag) {
+  u32 v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+  return v;
+}
+// Wait until *flag == v; on timeout record kErrMbarrierTimeout, mark the CTA
+// dead and return false (the writer is a CTA of the same grid that runs at
+// the same time or earlier, so the wait ends unless something failed).
+__device__ __forceinline__ bool flag_wait(const u32 *flag, u32 v, u32 *err, u32 where,
+                                          volatile int *dead) {
+  if (flag_acquire(flag) == v) return true;
+  const u64 start = globaltimer_ns();
+  for (u32 i = 1;; ++i) {
+    if (flag_acquire(flag) == v) return true;
+    if ((i & 63u) == 0u) {
+      if (dead != nullptr && *dead) return false;
+      if (globaltimer_ns() - start > TILA_WAIT_NS) break;
+    }
+  }
+  report_error(err, kErrMbarrierTimeout, where);
+  if (dead != nullptr) *dead = 1;
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tensor memory accelerator) tile loads - single CTA, no multicast
 // ---------------------------------------------------------------------------
