@@ -171,18 +171,18 @@ def test_heavy_first_cta_order_is_a_bijection():
 
 
 def test_warp_specialised_budgets_fit_the_launch_pool():
-    """Every warpgroup's setmaxnreg share adds up to at most the registers the
-    CTA is launched with (threads x launch registers), for 4- and 8-warp
-    programs; 8-warp programs run 2 x 256 consumers and a producer warpgroup."""
+    """The warpgroups' setmaxnreg shares add up to at most the registers the
+    CTA is launched with (threads x launch registers).  Programs requested
+    with 8 warps get the same 4-warp warp-specialised kernel (384 threads)."""
     from tila_b200.codegen.wspec import ws_budget
-    for T in (128, 256):
-        threads, launch, producer, consumer = ws_budget(T)
-        assert threads == 2 * T + 128 and launch == (65536 // threads) // 8 * 8
-        assert 128 * producer + 2 * T * consumer <= threads * launch
+    threads, launch, producer, consumer = ws_budget(128)
+    assert threads == 2 * 128 + 128 and launch == (65536 // threads) // 8 * 8
+    assert 128 * producer + 2 * 128 * consumer <= threads * launch
     q = torch.zeros(2, 512, 128, dtype=f16)
-    spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
-               8, CAUSAL=0, BM=128, BN=128, BD=128)
-    assert spec.threads == 640 and spec.launch_regs == 96 and spec.fuse == {0: 2}
+    for causal in (0, 1):
+        spec = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+                   8, CAUSAL=causal, BM=128, BN=128, BD=128)
+        assert spec.threads == 384 and spec.launch_regs == 168 and spec.fuse == {0: 2}
 
 
 def test_warp_specialised_kernel_register_budget(tmp_path):
@@ -205,14 +205,17 @@ def test_warp_specialised_kernel_register_budget(tmp_path):
     assert out.returncode == 0, out.stderr[-2000:]
     regs = re.findall(r"Used (\d+) registers", out.stderr)
     assert regs and int(regs[-1]) == spec.launch_regs == 168
-    spec8 = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
-                8, CAUSAL=0, BM=128, BN=128, BD=128)
-    cu.write_text(spec8.source)
+    assert not re.search(r"[1-9]\d* bytes spill stores", out.stderr), out.stderr[-2000:]
+    # the causal chain (per-program trip counts, CTA renumbering) too
+    spec1 = gen(W.fused_attention_kernel, dict(q=q, k=q.clone(), v=q.clone(), o=torch.zeros(2, 512, 128)),
+                CAUSAL=1, BM=128, BN=128, BD=128)
+    cu.write_text(spec1.source)
     out = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-Xptxas", "-v",
                           f"-I{build.PKG / 'csrc' / 'tile'}", "-c", str(cu), "-o", str(tmp_path / "ws.o")],
                          capture_output=True, text=True)
     assert out.returncode == 0, out.stderr[-2000:]
-    assert int(re.findall(r"Used (\d+) registers", out.stderr)[-1]) == spec8.launch_regs == 96
+    assert int(re.findall(r"Used (\d+) registers", out.stderr)[-1]) == spec1.launch_regs == 168
+    assert not re.search(r"[1-9]\d* bytes spill stores", out.stderr), out.stderr[-2000:]
 
 
 def test_static_if_resolution_leaves_kernel_untouched():

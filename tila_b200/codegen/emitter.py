@@ -2398,15 +2398,17 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         if ws_fit and os.environ.get("TILA_B200_WS", "1") != "0":
             # the loops have the flash-attention shape: generate the
             # warp-specialised kernel instead (this pass's plan is the fallback)
+            # (always 4-warp programs: the thread layout is the backend's
+            # choice and does not change results; see wspec.ws_budget)
             try:
-                return KernelEmitter(self.tk, self.consts, self.buffers, num_warps=self._num_warps,
+                return KernelEmitter(self.tk, self.consts, self.buffers, num_warps=4,
                                      entry_name=self.entry, debug=self.debug,
                                      versioning=self.versioning, source_map=self.source_map,
                                      ws=found).generate()
             except CodegenError:
                 pass
         if self._ws is not None:
-            if not (self.T in (128, 256) and self.uses_tmem and self.tmem_cols <= 256 and not self.fuse):
+            if not (self.T == 128 and self.uses_tmem and self.tmem_cols <= 256 and not self.fuse):
                 self.fail("warp-specialised loop: two programs per CTA do not fit")
             wg = True
         if wg:

@@ -71,7 +71,7 @@ RING = 2                   # stages of the K and V rings
 
 def ws_budget(T):
     """(threads, registers per thread at launch, producer, consumer registers)
-    of the warp-specialised kernel whose programs have T threads.
+    of the warp-specialised kernel whose programs have T = 128 threads.
 
     The CTA is two programs of T threads plus the producer warpgroup.
     ``__launch_bounds__(threads, 1)`` gives every thread 65536 / threads
@@ -80,10 +80,13 @@ def ws_budget(T):
     producer gives back all but its share, the consumers take theirs, and the
     shares add up to at most the pool, so reg_alloc never waits for
     registers that do not exist.  The host refuses to launch the kernel
-    unless ptxas allocated exactly the launch count."""
+    unless ptxas allocated exactly the launch count.  (Programs requested
+    with 8 warps get this 4-warp form too: with two 256-thread softmax
+    warpgroups the registers left per thread made the kernel spill.)"""
+    assert T == 128
     threads = 2 * T + 128
     launch = (65536 // threads) // 8 * 8
-    producer, consumer = {128: (64, 216), 256: (24, 112)}[T]
+    producer, consumer = 64, 216
     assert 128 * producer + 2 * T * consumer <= threads * launch
     assert producer <= launch <= consumer and producer % 8 == 0 and consumer % 8 == 0
     return threads, launch, producer, consumer
@@ -270,11 +273,6 @@ class WarpSpecMixin:
         if f is None or getattr(self, "_ws_bad", False):
             return None
         if len(self.uses.get(f["q"], [])) != len(f["loops"]):
-            return None
-        # 8-warp programs keep the one-loop, equal-trip form: with uneven
-        # trip counts their producer spills and the one-program-per-CTA plan
-        # is faster (742 against 688 TFLOP/s for causal attention)
-        if self.T == 256 and (len(f["loops"]) > 1 or not f["loops"][0]["even"]):
             return None
         # programs whose trip counts grow or shrink with program_id(0): the
         # CTAs are renumbered heaviest-first (see cta_order_prelude)
