@@ -195,6 +195,24 @@ def test_program_range_shards_reproduce_the_full_launch(world):
     assert torch.equal(c_part, c_full)
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_causal_attention_head_shards_reproduce_the_full_launch(world):
+    """The warp-specialised causal kernel launched per shard of the head axis
+    (as bench.py --gpus N shards it; CTA renumbering within each shard's
+    grid): the shards together write exactly the full launch's output."""
+    from tila_b200.multigpu import shard
+    q, k, v = W.attention_inputs(11, 640, 128, seed=31)
+    qg, kg, vg = _cuda(q), _cuda(k), _cuda(v)
+    full = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    W.fused_attention_kernel[(5, 11)](qg, kg, vg, full, 128 ** -0.5, CAUSAL=1, BM=128, BN=128, BD=128)
+    parts = torch.full_like(full, float("nan"))
+    for rank in range(world):
+        with shard(1, 11, world, rank):
+            W.fused_attention_kernel[(5, 11)](qg, kg, vg, parts, 128 ** -0.5, CAUSAL=1, BM=128, BN=128, BD=128)
+    _no_device_errors()
+    assert torch.equal(parts, full)
+
+
 def test_program_shards_write_the_rows_shard_rows_names():
     """3 matmul tile rows of 128 on 2 ranks (programs [0, 2) and [2, 3)): each
     rank's launch writes exactly the rows multigpu.shard_rows gives it (0-255
