@@ -298,8 +298,8 @@ def test_matmul_persistent_split_matches_f64(monkeypatch, k):
     evenly, tiles parked by one CTA and finished by the previous one (with
     K = 320 nearly every CTA does both).  Every element within the K*eps_f32
     bound of the f64 product."""
-    monkeypatch.setenv("TILA_B200_STREAMK", "1")
-    kernel = ti.jit(W.matmul_kernel.fn)
+    monkeypatch.setenv("TILA_B200_STREAMK", "1")     # part of the kernel cache key
+    kernel = W.matmul_kernel
     a, b = W.matmul_inputs(4096, 4096, k, seed=29)
     c = torch.zeros((4096, 4096), dtype=torch.float32, device="cuda")
     kernel[(32, 32)](_cuda(a), _cuda(b), c, BM=128, BN=128, BK=64)

@@ -82,7 +82,13 @@ fast_hits = 0        # launches that took the repeated-signature path (for tests
 def _tila_env():
     """Every TILA_* environment switch (the checks and the code generation
     read several of them: TILA_SAFETY, TILA_RACE*, TILA_PROOF_*, TILA_DEBUG,
-    TILA_INTERP, TILA_EFFECTS, TILA_BACKEND_ARTIFACTS, ...)."""
+    TILA_INTERP, TILA_EFFECTS, TILA_BACKEND_ARTIFACTS, ...).  Read from the
+    environment's encoded table when the interpreter keeps one (CPython's
+    ``os.environ._data``), which spares decoding every variable per launch."""
+    data = getattr(os.environ, "_data", None)
+    if isinstance(data, dict):
+        return tuple(sorted((k, v) for k, v in data.items()
+                            if (k[:5] == b"TILA_" if isinstance(k, bytes) else k.startswith("TILA_"))))
     return tuple(sorted((k, v) for k, v in os.environ.items() if k.startswith("TILA_")))
 
 
@@ -179,7 +185,9 @@ def _remember(launcher, key, args, kwargs):
     tir = tuple(_statements(jf.tk.body, []))
     evidence = (getattr(jf, "last_alignment_facts", ()), getattr(jf, "last_race_report", None),
                 getattr(jf, "last_race_details", None))
-    cache[key] = (names, scalar_vals, stride_vals, consts, grid, jf.tk, tir, evidence)
+    last = getattr(jf, "_b200_last_launch", None)
+    cache[key] = (names, scalar_vals, stride_vals, consts, grid, jf.tk, tir, evidence,
+                  last.entry if last is not None else None)
 
 
 def _restore_evidence(jf, evidence):
@@ -241,7 +249,7 @@ def install():
                 vals = list(args) + [kwargs[k] for k in sorted(kwargs)]
                 from . import backend
                 backend.execute(self, {n: vals[i] for n, i in names.items()}, scalar_vals,
-                                stride_vals, consts, grid)
+                                stride_vals, consts, grid, entry=hit[8])
                 return None
         self._b200_last_exec = None
         out = full_call(self, *args, **kwargs)
