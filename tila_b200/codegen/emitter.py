@@ -83,10 +83,6 @@ class Val:
     smem: object = None       # smem: the shared-memory operand (TMA-loaded tile)
     const: object = None      # compile-time known python value (scalars)
 
-    @property
-    def is_tile(self):
-        return bool(self.shape)
-
 
 @dataclass
 class BufferInfo:
@@ -1227,9 +1223,6 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
         return res
 
     # -- memory ----------------------------------------------------------------
-
-    def _buffer_base(self, name):
-        return f"p_{name}"
 
     def address_terms(self, buffer, coords, layout, r, smaps):
         """Element offset (i64 C++ expr) of a buffer access at slot r."""

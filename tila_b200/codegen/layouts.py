@@ -24,10 +24,6 @@ from functools import cached_property
 import numpy as np
 
 
-def _subst(expr: str, r) -> str:
-    return expr.replace("{r}", str(r))
-
-
 class Layout:
     rank: int
     shape: tuple
@@ -58,9 +54,6 @@ class Layout:
 
     def __hash__(self):
         return hash(self.key())
-
-    def describe(self) -> str:
-        return repr(self.key())
 
     @cached_property
     def _tables(self):
