@@ -18,8 +18,9 @@ Per workload:
   proof checks included, as for every Tila launch).
 * ``roofline``  achieved / measured peak (MEASURED_PEAKS.json) of the
   dominant kernel.
-* ``cpu_baseline``  Tila's NumPy reference interpreter on the host cores on a
-  bounded sample of the workload (rank 0, N = 1).
+* ``cpu_baseline``  Tila's NumPy reference interpreter on a bounded sample of
+  the workload, spread over every host core by worker processes (rank 0,
+  N = 1).
 
 Multi-GPU (torchrun, one process per GPU): weak scaling.  The job is N copies
 of the configuration along its program axis (rows, output tiles or
@@ -35,6 +36,7 @@ with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import atexit
 import json
 import os
 import statistics
@@ -513,7 +515,7 @@ def run_ours(args, world, rank, device, keys):
         if case.e2e_call is not None and not args.no_e2e:
             entry["e2e"] = _e2e(case, args, world, rank, device)
         if rank == 0 and world == 1 and not args.no_cpu:
-            entry["cpu_baseline"] = cpu_baseline(key, repeats=1)
+            entry["cpu_baseline"] = cpu_reference(key, steps=1)
         if gather_ms is not None:
             # the same steps followed by the gather (weak scaling, the gather
             # measured above; device times added)
@@ -679,75 +681,164 @@ def _e2e(case, args, world, rank, device):
 
 
 # ---------------------------------------------------------------------------
-# CPU: Tila's NumPy reference interpreter on a bounded sample
+# CPU: Tila's NumPy reference interpreter on every host core
 # ---------------------------------------------------------------------------
+#
+# The interpreter runs one program after another in one Python thread, so it
+# uses the host's cores through processes: a spawned pool of one worker per
+# core (one BLAS thread each), every worker holding the seeded inputs of each
+# workload's per-step sample and running a contiguous share of the sample's
+# program axis through ``kernel[grid](numpy arrays)`` - the reference's own
+# launch path, contract checks included.  A step is one pass over the whole
+# sample; its rate is the sample's work over the step's wall time.
 
-def _blas_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        return 1
+# per workload: (length of the sample's program axis, what the sample is)
+_REF_SAMPLE = {
+    "add": (1024, "full workload (N=1048576, 1024 programs of 1024)"),
+    "softmax": (8192, "full workload (8192 rows of 1000, BN=1024)"),
+    "matmul": (16, "16 of the 32 rows of 128x128 output tiles (C 2048x4096, full K=4096)"),
+    "unfused_attention": (16, "16 of the 128 batch*heads (L=1024, D=64)"),
+    "fused_attention": (16, "16 of the 128 batch*heads (L=4096, D=128)"),
+    "fused_attention_causal": (16, "16 of the 128 batch*heads (L=4096, D=128, causal)"),
+}
+_REF_DATA = {}
+_REF_POOL = []
 
 
-def cpu_baseline(key, repeats=1):
-    """Time the reference interpreter on a bounded sample; rate in the
-    workload's unit.  The sample keeps one step to a few seconds."""
-    import tila_b200
+def _ref_units(key):
     from tila_b200 import workloads as W
-    ti = tila_b200.tila
-    os.environ.setdefault("TILA_RACE", "off")
-    if key == "add":
-        n = 1 << 20
-        x, y = W.add_inputs(n)
-        out = np.zeros_like(x)
-        fn = lambda: W.add_kernel[(n // 1024,)](x, y, out, BLOCK=1024)
-        units, unit, scale, sample, cores = W.add_bytes(n), "GB/s", 1e9, "full workload (N=1048576)", 1
-    elif key == "softmax":
-        m = 1024
-        x = W.softmax_inputs(m, 1000)
-        o = np.zeros_like(x)
-        fn = lambda: W.softmax_kernel[(m,)](x, o, BN=1024)
-        units, unit, scale, sample, cores = W.softmax_bytes(m, 1000), "GB/s", 1e9, \
-            "1024 of the 8192 rows (1000 columns, BN=1024)", 1
-    elif key == "matmul":
-        a, b = W.matmul_inputs(128, 512, 4096)
-        c = np.zeros((128, 512), np.float32)
-        fn = lambda: W.matmul_kernel[(1, 4)](a, b, c, BM=128, BN=128, BK=64)
-        units, unit, scale = W.matmul_flops(128, 512, 4096), "TFLOP/s", 1e12
-        sample, cores = "4 of the 1024 output tiles (128x512 of C, full K=4096)", _blas_threads()
-    elif key == "unfused_attention":
-        q, k, v = W.attention_inputs(1, 1024, 64)
-        s = np.zeros((1, 1024, 1024), np.float32)
-        p = np.zeros_like(s)
-        o = np.zeros((1, 1024, 64), np.float32)
+    n = _REF_SAMPLE[key][0]
+    return {"add": (W.add_bytes(n * 1024), "GB/s", 1e9),
+            "softmax": (W.softmax_bytes(n, 1000), "GB/s", 1e9),
+            "matmul": (W.matmul_flops(n * 128, 4096, 4096), "TFLOP/s", 1e12),
+            "unfused_attention": (W.unfused_flops(n, 1024, 64), "TFLOP/s", 1e12),
+            "fused_attention": (W.fused_flops(n, 4096, 128), "TFLOP/s", 1e12),
+            "fused_attention_causal": (W.causal_flops(n, 4096, 128), "TFLOP/s", 1e12)}[key]
 
-        def fn():
-            W.attention_scores[(8, 8, 1)](q, k, s, 0.125, BM=128, BN=128, BD=64)
-            W.softmax_kernel[(1024,)](s.reshape(1024, 1024), p.reshape(1024, 1024), BN=1024)
-            W.attention_pv[(8, 1)](p, v, o, BM=128, BN=128, BD=64)
-        units, unit, scale = W.unfused_flops(1, 1024, 64), "TFLOP/s", 1e12
-        sample, cores = "1 of the 128 batch*heads (L=1024, D=64)", _blas_threads()
-    elif key == "fused_attention_causal":
-        q, k, v = W.attention_inputs(1, 4096, 128)
-        o = np.zeros((1, 4096, 128), np.float32)
-        fn = lambda: W.fused_attention_kernel[(32, 1)](q, k, v, o, 128 ** -0.5, CAUSAL=1, BM=128, BN=128, BD=128)
-        units, unit, scale = W.causal_flops(1, 4096, 128), "TFLOP/s", 1e12
-        sample, cores = "1 of the 128 batch*heads (L=4096, D=128, causal)", _blas_threads()
-    else:
-        q, k, v = W.attention_inputs(1, 4096, 128)
-        o = np.zeros((1, 4096, 128), np.float32)
-        fn = lambda: W.fused_attention_kernel[(32, 1)](q, k, v, o, 128 ** -0.5, CAUSAL=0, BM=128, BN=128, BD=128)
-        units, unit, scale = W.fused_flops(1, 4096, 128), "TFLOP/s", 1e12
-        sample, cores = "1 of the 128 batch*heads (L=4096, D=128)", _blas_threads()
-    fn()                      # warm (decoration caches, first-call imports)
+
+def _ref_init():
+    """Pool worker start: the seeded inputs of every sample (the same
+    generators and seeds as the GPU arm), then one launch of each kernel on
+    one entry of the program axis, so that Tila's per-process first-call
+    work (decoration, TIR) stays out of the timed steps.  A failure is kept
+    and raised by every task (a raising initializer would make the pool
+    restart the worker for ever)."""
+    try:
+        from tila_b200 import workloads as W
+        x, y = W.add_inputs(1024 * 1024)
+        _REF_DATA["add"] = (x, y, np.zeros_like(x))
+        x = W.softmax_inputs(8192, 1000)
+        _REF_DATA["softmax"] = (x, np.zeros_like(x))
+        a, b = W.matmul_inputs(16 * 128, 4096, 4096)
+        _REF_DATA["matmul"] = (a, b, np.zeros((16 * 128, 4096), np.float32))
+        q, k, v = W.attention_inputs(16, 1024, 64)
+        s = np.zeros((16, 1024, 1024), np.float32)
+        _REF_DATA["unfused_attention"] = (q, k, v, s, np.zeros_like(s), np.zeros((16, 1024, 64), np.float32))
+        q, k, v = W.attention_inputs(16, 4096, 128)
+        _REF_DATA["fused_attention"] = _REF_DATA["fused_attention_causal"] = \
+            (q, k, v, np.zeros((16, 4096, 128), np.float32))
+        for key in _REF_SAMPLE:
+            _ref_run(key, 0, 1)
+    except Exception as exc:        # noqa: BLE001 - reported by _ref_run
+        _REF_DATA["error"] = f"{type(exc).__name__}: {exc}"
+
+
+def _ref_run(key, lo, hi):
+    """Pool worker: run the interpreter on entries [lo, hi) of the sample's
+    program axis (each a contiguous slice of the inputs, launched with the
+    grid that slice calls for).  Returns the seconds taken."""
+    from tila_b200 import workloads as W
+    if "error" in _REF_DATA:
+        raise RuntimeError("reference worker setup failed: " + _REF_DATA["error"])
+    d = _REF_DATA[key]
+    h = hi - lo
     t0 = time.perf_counter()
-    for _ in range(repeats):
-        fn()
-    dt = (time.perf_counter() - t0) / repeats
-    return {"value": units / dt / scale, "unit": unit, "cores": cores, "kind": "reference",
-            "sample": f"Tila NumPy interpreter, {sample}; {repeats} run(s) of "
-                      f"{dt:.3f} s, {cores} thread(s) of {os.cpu_count()} host cores"}
+    if key == "add":
+        x, y, o = (t[lo * 1024:hi * 1024] for t in d)
+        W.add_kernel[(h,)](x, y, o, BLOCK=1024)
+    elif key == "softmax":
+        x, o = (t[lo:hi] for t in d)
+        W.softmax_kernel[(h,)](x, o, BN=1024)
+    elif key == "matmul":
+        a, b, c = d
+        W.matmul_kernel[(h, 32)](a[lo * 128:hi * 128], b, c[lo * 128:hi * 128], BM=128, BN=128, BK=64)
+    elif key == "unfused_attention":
+        q, k, v, s, p, o = (t[lo:hi] for t in d)
+        W.attention_scores[(8, 8, h)](q, k, s, 0.125, BM=128, BN=128, BD=64)
+        W.softmax_kernel[(h * 1024,)](s.reshape(h * 1024, 1024), p.reshape(h * 1024, 1024), BN=1024)
+        W.attention_pv[(8, h)](p, v, o, BM=128, BN=128, BD=64)
+    else:
+        q, k, v, o = (t[lo:hi] for t in d)
+        W.fused_attention_kernel[(32, h)](q, k, v, o, 128 ** -0.5,
+                                          CAUSAL=int(key == "fused_attention_causal"), BM=128, BN=128, BD=128)
+    return time.perf_counter() - t0
+
+
+def _ref_workers():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _ref_pool():
+    """The worker pool (spawned, never forked: the parent may hold a CUDA
+    context), started once; the workers inherit one BLAS thread each and
+    Tila's race analysis switched off, which the parent's own environment
+    does not keep."""
+    if not _REF_POOL:
+        import multiprocessing as mp
+        env = {"OMP_NUM_THREADS": "1", "OPENBLAS_NUM_THREADS": "1", "MKL_NUM_THREADS": "1",
+               "TILA_RACE": "off"}
+        saved = {k: os.environ.get(k) for k in env}
+        os.environ.update(env)
+        try:
+            n = _ref_workers()
+            _REF_POOL.append((mp.get_context("spawn").Pool(n, initializer=_ref_init), n))
+            atexit.register(_ref_close)
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+    return _REF_POOL[0]
+
+
+def _ref_shards(length, parts):
+    """Contiguous, nearly equal ranges [lo, hi) covering range(length)."""
+    cuts = [length * i // parts for i in range(parts + 1)]
+    return [(lo, hi) for lo, hi in zip(cuts, cuts[1:]) if hi > lo]
+
+
+def _ref_close():
+    """Stop the workers before the interpreter shuts down (a pool collected
+    during shutdown fails in its finaliser)."""
+    while _REF_POOL:
+        pool, _ = _REF_POOL.pop()
+        pool.terminate()
+        pool.join()
+
+
+def cpu_reference(key, steps=1):
+    """Tila's interpreter on all host cores: one untimed pass over the
+    sample, then ``steps`` timed passes; the median rate in the workload's
+    unit."""
+    pool, n = _ref_pool()
+    length, desc = _REF_SAMPLE[key]
+    shards = [(key, lo, hi) for lo, hi in _ref_shards(length, n)]
+    pool.starmap(_ref_run, shards, chunksize=1)
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        pool.starmap(_ref_run, shards, chunksize=1)
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
+    units, unit, scale = _ref_units(key)
+    return {"value": units / dt / scale, "unit": unit, "cores": len(shards), "kind": "reference",
+            "sample": f"Tila NumPy interpreter, {desc}, split over {len(shards)} worker processes "
+                      f"(one BLAS thread each) on {_ref_workers()} of {os.cpu_count()} host cores; "
+                      f"median of {len(times)} pass(es) of {dt:.3f} s"}
 
 
 # ---------------------------------------------------------------------------
@@ -782,9 +873,8 @@ def main():
             return
         out = {}
         for key in keys:
-            runs = [cpu_baseline(key) for _ in range(max(1, min(args.steps, 3)))]
-            v = statistics.median(r["value"] for r in runs)
-            base = dict(runs[0], value=v)
+            base = cpu_reference(key, steps=min(args.steps, 3))
+            v = base["value"]
             out[key] = {"value": v, "unit": base["unit"], "cpu_baseline": base,
                         "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
                                 "d2h_bytes_per_step": 0}}
