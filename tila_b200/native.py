@@ -276,7 +276,7 @@ class Kernel:
         cfg.stream = stream
         cfg.flags = flags
         ptrs = (ctypes.c_void_p * max(1, len(args)))(
-            *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
+            *[ctypes.addressof(a) for a in args])
         log = ctypes.create_string_buffer(1024)
         _check(library().tila_launch(self.handle, ctypes.byref(cfg), ptrs, log, len(log)),
                f"launch of {self.name}", log)
@@ -295,7 +295,7 @@ class Kernel:
         cfg.stream = stream
         cfg.flags = flags
         ptrs = (ctypes.c_void_p * max(1, len(args)))(
-            *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in args])
+            *[ctypes.addressof(a) for a in args])
         log = ctypes.create_string_buffer(1024)
         status = library().tila_launch_noalloc(self.handle, ctypes.byref(cfg), ptrs, scratch_arg,
                                                scratch_bytes, log, len(log))
