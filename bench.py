@@ -723,20 +723,25 @@ def _ref_init():
     work (decoration, TIR) stays out of the timed steps.  A failure is kept
     and raised by every task (a raising initializer would make the pool
     restart the worker for ever)."""
+    def zeros(shape):
+        z = np.empty(shape, np.float32)
+        z.fill(0.0)             # every page mapped now, not in a timed pass
+        return z
+
     try:
         from tila_b200 import workloads as W
         x, y = W.add_inputs(1024 * 1024)
-        _REF_DATA["add"] = (x, y, np.zeros_like(x))
+        _REF_DATA["add"] = (x, y, zeros(x.shape))
         x = W.softmax_inputs(8192, 1000)
-        _REF_DATA["softmax"] = (x, np.zeros_like(x))
+        _REF_DATA["softmax"] = (x, zeros(x.shape))
         a, b = W.matmul_inputs(16 * 128, 4096, 4096)
-        _REF_DATA["matmul"] = (a, b, np.zeros((16 * 128, 4096), np.float32))
+        _REF_DATA["matmul"] = (a, b, zeros((16 * 128, 4096)))
         q, k, v = W.attention_inputs(16, 1024, 64)
-        s = np.zeros((16, 1024, 1024), np.float32)
-        _REF_DATA["unfused_attention"] = (q, k, v, s, np.zeros_like(s), np.zeros((16, 1024, 64), np.float32))
+        _REF_DATA["unfused_attention"] = (q, k, v, zeros((16, 1024, 1024)), zeros((16, 1024, 1024)),
+                                          zeros((16, 1024, 64)))
         q, k, v = W.attention_inputs(16, 4096, 128)
         _REF_DATA["fused_attention"] = _REF_DATA["fused_attention_causal"] = \
-            (q, k, v, np.zeros((16, 4096, 128), np.float32))
+            (q, k, v, zeros((16, 4096, 128)))
         for key in _REF_SAMPLE:
             _ref_run(key, 0, 1)
     except Exception as exc:        # noqa: BLE001 - reported by _ref_run
@@ -820,16 +825,17 @@ def _ref_close():
         pool.join()
 
 
-def cpu_reference(key, steps=1):
+def cpu_reference(key, steps=1, min_seconds=1.0):
     """Tila's interpreter on all host cores: one untimed pass over the
-    sample, then ``steps`` timed passes; the median rate in the workload's
-    unit."""
+    sample, then timed passes, at least ``steps`` of them and at least
+    ``min_seconds`` in all (short samples get several passes); the median
+    pass gives the rate in the workload's unit."""
     pool, n = _ref_pool()
     length, desc = _REF_SAMPLE[key]
     shards = [(key, lo, hi) for lo, hi in _ref_shards(length, n)]
     pool.starmap(_ref_run, shards, chunksize=1)
     times = []
-    for _ in range(max(1, steps)):
+    while len(times) < max(1, steps) or (sum(times) < min_seconds and len(times) < 100):
         t0 = time.perf_counter()
         pool.starmap(_ref_run, shards, chunksize=1)
         times.append(time.perf_counter() - t0)
