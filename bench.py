@@ -779,11 +779,18 @@ def _ref_run(key, lo, hi):
     return time.perf_counter() - t0
 
 
+# A worker holds Tila, NumPy and torch (about 0.55 GB) plus the samples' inputs
+# (about 0.4 GB); past this many workers the host memory they take grows
+# faster than the interpreter's rate.
+_REF_MAX_WORKERS = 32
+
+
 def _ref_workers():
     try:
-        return len(os.sched_getaffinity(0))
+        cores = len(os.sched_getaffinity(0))
     except AttributeError:
-        return os.cpu_count() or 1
+        cores = os.cpu_count() or 1
+    return max(1, min(cores, _REF_MAX_WORKERS))
 
 
 def _ref_pool():
@@ -843,7 +850,7 @@ def cpu_reference(key, steps=1, min_seconds=1.0):
     units, unit, scale = _ref_units(key)
     return {"value": units / dt / scale, "unit": unit, "cores": len(shards), "kind": "reference",
             "sample": f"Tila NumPy interpreter, {desc}, split over {len(shards)} worker processes "
-                      f"(one BLAS thread each) on {_ref_workers()} of {os.cpu_count()} host cores; "
+                      f"(one BLAS thread each) on {len(shards)} of {os.cpu_count()} host cores; "
                       f"median of {len(times)} pass(es) of {dt:.3f} s"}
 
 
