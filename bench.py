@@ -222,6 +222,7 @@ class Case:
         m = m1 * self.mult
         a, b = W.matmul_inputs(m, 4096, 4096, seed=0)
         self.host_inputs = [a, b]
+        self.e2e_whole_inputs = {1}       # every rank's programs read all of B
         nset = self._sets(2 * 4096 * 4096 * 2 + 4 * 4096 * 4096)
         self.sets = [(self._dev(a), self._dev(b), torch.empty((m, 4096), device=self.device))
                      for _ in range(nset)]
@@ -620,6 +621,12 @@ def _e2e(case, args, world, rank, device):
     outs = [make_out(), make_out()]
     host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
     ax, lo, hi = case._ranges()[0]
+    # this rank's leading rows: the output rows its programs write, which are
+    # also the input rows they read (inputs every program reads whole, such
+    # as matmul's B, travel whole); each rank moves only its own share
+    r0, r1 = case.gather_rows(outs[0])[rank]
+    whole = getattr(case, "e2e_whole_inputs", set())
+    in_rows = [slice(None) if i in whole else slice(r0, r1) for i in range(len(pinned))]
     # enough steps that the pipeline's fill (the first copy-in) and drain (the
     # last copy-out), both inside the timed region, weigh little
     steps = max(8, min(4 * args.steps, 48))
@@ -637,8 +644,8 @@ def _e2e(case, args, world, rank, device):
         b = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(in_free[b])
-            for p, d in zip(pinned, dev_in[b]):
-                d.copy_(p, non_blocking=True)
+            for p, d, rows in zip(pinned, dev_in[b], in_rows):
+                d[rows].copy_(p[rows], non_blocking=True)
             in_ready[b].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_ready[b])
@@ -649,7 +656,7 @@ def _e2e(case, args, world, rank, device):
             out_ready[b].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(out_ready[b])
-            host_out[b].copy_(outs[b], non_blocking=True)
+            host_out[b][r0:r1].copy_(outs[b][r0:r1], non_blocking=True)
             out_free[b].record(s_out)
 
     for i in range(2):
@@ -672,12 +679,13 @@ def _e2e(case, args, world, rank, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
     name, unit, scale = case.metric_unit
-    h2d = sum(p.numel() * p.element_size() for p in pinned)
-    d2h = host_out[0].numel() * host_out[0].element_size()
+    h2d = sum(p[rows].numel() * p.element_size() for p, rows in zip(pinned, in_rows)) * world
+    d2h = host_out[0][r0:r1].numel() * host_out[0].element_size() * world
     return {"value": round(case.units_per_rank * world / dt / scale, 3), "unit": unit,
             "ms_per_step": round(dt * 1e3, 3), "steps": steps,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "pipelining": "two buffer sets, copy-in / compute / copy-out streams"}
+            "pipelining": "two buffer sets, copy-in / compute / copy-out streams"
+                          + ("; each rank copies its own rows, bytes summed over ranks" if world > 1 else "")}
 
 
 # ---------------------------------------------------------------------------
