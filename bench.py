@@ -1,4 +1,4 @@
-"""Benchmark of the B200 Tila backend on the five judged workloads.
+"""Benchmark of the B200 Tila backend on the five benchmarked workloads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--only]
                     [--impl reference]

@@ -3,7 +3,7 @@
 * ``libtila_b200.so``: the C-ABI launcher (csrc/launcher.cpp), linked
   against NVRTC; libcuda is opened at run time.
 * a compile check of the tile library for sm_100a with nvcc;
-* optionally, the cubins of the five judged workloads (NVRTC works without
+* optionally, the cubins of the five benchmarked workloads (NVRTC works without
   a GPU), so that a fresh GPU machine does not spend its first launches
   compiling.
 

@@ -1,9 +1,9 @@
-"""The five judged workloads: the kernels, their seeded inputs and their work.
+"""The five benchmarked workloads: the kernels, their seeded inputs and their work.
 
 Four of the five are Tila's own example kernels, imported unchanged from the
 installed Tila tree (``examples/add_kernel.py:12-27``, ``examples/softmax.py:14-29``,
 ``examples/matmul.py:10-40``, ``examples/fused_attention.py:34-128``; the latter
-with ``CAUSAL=0`` is the judged fused attention and with ``CAUSAL=1`` its
+with ``CAUSAL=0`` is the benchmarked fused attention and with ``CAUSAL=1`` its
 causal variant), plus ``examples/self_attention.py:18-73``.  The unfused
 attention has no example in Tila; it is written here as three ordinary Tila
 programs (scores, the row softmax of ``examples/softmax.py``, P@V).  Nothing in
@@ -91,7 +91,7 @@ def attention_pv(
 
 
 # ---------------------------------------------------------------------------
-# configurations (the judged sizes) and their synthetic inputs
+# configurations (the benchmarked sizes) and their synthetic inputs
 # ---------------------------------------------------------------------------
 
 @dataclass(frozen=True)
