@@ -516,7 +516,7 @@ def run_ours(args, world, rank, device, keys):
         if case.e2e_call is not None and not args.no_e2e:
             entry["e2e"] = _e2e(case, args, world, rank, device)
         if rank == 0 and world == 1 and not args.no_cpu:
-            entry["cpu_baseline"] = cpu_reference(key, steps=1)
+            entry["cpu_baseline"] = cpu_reference(key, keys, steps=1)
         if gather_ms is not None:
             # the same steps followed by the gather (weak scaling, the gather
             # measured above; device times added)
@@ -724,9 +724,9 @@ def _ref_units(key):
             "fused_attention_causal": (W.causal_flops(n, 4096, 128), "TFLOP/s", 1e12)}[key]
 
 
-def _ref_init():
-    """Pool worker start: the seeded inputs of every sample (the same
-    generators and seeds as the GPU arm), then one launch of each kernel on
+def _ref_init(keys):
+    """Pool worker start: the seeded inputs of the samples of ``keys`` (the
+    same generators and seeds as the GPU arm), then one launch of each kernel on
     one entry of the program axis, so that Tila's per-process first-call
     work (decoration, TIR) stays out of the timed steps.  A failure is kept
     and raised by every task (a raising initializer would make the pool
@@ -738,19 +738,24 @@ def _ref_init():
 
     try:
         from tila_b200 import workloads as W
-        x, y = W.add_inputs(1024 * 1024)
-        _REF_DATA["add"] = (x, y, zeros(x.shape))
-        x = W.softmax_inputs(8192, 1000)
-        _REF_DATA["softmax"] = (x, zeros(x.shape))
-        a, b = W.matmul_inputs(16 * 128, 4096, 4096)
-        _REF_DATA["matmul"] = (a, b, zeros((16 * 128, 4096)))
-        q, k, v = W.attention_inputs(16, 1024, 64)
-        _REF_DATA["unfused_attention"] = (q, k, v, zeros((16, 1024, 1024)), zeros((16, 1024, 1024)),
-                                          zeros((16, 1024, 64)))
-        q, k, v = W.attention_inputs(16, 4096, 128)
-        _REF_DATA["fused_attention"] = _REF_DATA["fused_attention_causal"] = \
-            (q, k, v, zeros((16, 4096, 128)))
-        for key in _REF_SAMPLE:
+        if "add" in keys:
+            x, y = W.add_inputs(1024 * 1024)
+            _REF_DATA["add"] = (x, y, zeros(x.shape))
+        if "softmax" in keys:
+            x = W.softmax_inputs(8192, 1000)
+            _REF_DATA["softmax"] = (x, zeros(x.shape))
+        if "matmul" in keys:
+            a, b = W.matmul_inputs(16 * 128, 4096, 4096)
+            _REF_DATA["matmul"] = (a, b, zeros((16 * 128, 4096)))
+        if "unfused_attention" in keys:
+            q, k, v = W.attention_inputs(16, 1024, 64)
+            _REF_DATA["unfused_attention"] = (q, k, v, zeros((16, 1024, 1024)), zeros((16, 1024, 1024)),
+                                              zeros((16, 1024, 64)))
+        if {"fused_attention", "fused_attention_causal"} & set(keys):
+            q, k, v = W.attention_inputs(16, 4096, 128)
+            _REF_DATA["fused_attention"] = _REF_DATA["fused_attention_causal"] = \
+                (q, k, v, zeros((16, 4096, 128)))
+        for key in keys:
             _ref_run(key, 0, 1)
     except Exception as exc:        # noqa: BLE001 - reported by _ref_run
         _REF_DATA["error"] = f"{type(exc).__name__}: {exc}"
@@ -801,11 +806,11 @@ def _ref_workers():
     return max(1, min(cores, _REF_MAX_WORKERS))
 
 
-def _ref_pool():
-    """The worker pool (spawned, never forked: the parent may hold a CUDA
-    context), started once; the workers inherit one BLAS thread each and
-    Tila's race analysis switched off, which the parent's own environment
-    does not keep."""
+def _ref_pool(keys):
+    """The worker pool for the workloads ``keys`` (spawned, never forked: the
+    parent may hold a CUDA context), started once; the workers inherit one
+    BLAS thread each and Tila's race analysis switched off, which the
+    parent's own environment does not keep."""
     if not _REF_POOL:
         import multiprocessing as mp
         env = {"OMP_NUM_THREADS": "1", "OPENBLAS_NUM_THREADS": "1", "MKL_NUM_THREADS": "1",
@@ -814,7 +819,8 @@ def _ref_pool():
         os.environ.update(env)
         try:
             n = _ref_workers()
-            _REF_POOL.append((mp.get_context("spawn").Pool(n, initializer=_ref_init), n))
+            _REF_POOL.append((mp.get_context("spawn").Pool(n, initializer=_ref_init,
+                                                            initargs=(tuple(keys),)), n))
             atexit.register(_ref_close)
         finally:
             for k, v in saved.items():
@@ -840,12 +846,13 @@ def _ref_close():
         pool.join()
 
 
-def cpu_reference(key, steps=1, min_seconds=1.0):
+def cpu_reference(key, keys, steps=1, min_seconds=1.0):
     """Tila's interpreter on all host cores: one untimed pass over the
     sample, then timed passes, at least ``steps`` of them and at least
     ``min_seconds`` in all (short samples get several passes); the median
-    pass gives the rate in the workload's unit."""
-    pool, n = _ref_pool()
+    pass gives the rate in the workload's unit.  ``keys``: every workload
+    of this run (the pool, started by the first call, prepares them all)."""
+    pool, n = _ref_pool(keys)
     length, desc = _REF_SAMPLE[key]
     shards = [(key, lo, hi) for lo, hi in _ref_shards(length, n)]
     pool.starmap(_ref_run, shards, chunksize=1)
@@ -894,7 +901,7 @@ def main():
             return
         out = {}
         for key in keys:
-            base = cpu_reference(key, steps=min(args.steps, 3))
+            base = cpu_reference(key, keys, steps=min(args.steps, 3))
             v = base["value"]
             out[key] = {"value": v, "unit": base["unit"], "cpu_baseline": base,
                         "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,

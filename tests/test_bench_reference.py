@@ -46,3 +46,25 @@ def test_reference_samples_cover_their_program_axis():
             assert all(a[1] == b[0] for a, b in zip(shards, shards[1:]))
         units, unit, scale = bench._ref_units(key)
         assert units > 0 and unit in ("GB/s", "TFLOP/s") and desc
+
+
+def test_reference_arm_prints_the_contract_line():
+    """``bench.py --impl reference`` (what the driver runs beside the GPU arm)
+    prints one JSON line with the reference keys: no GPU is needed for it."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(bench.__file__).resolve().parent
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--workload", "add",
+                          "--only", "--steps", "1", "--warmup", "3"],
+                         capture_output=True, text=True, timeout=600, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
+    assert line["higher_is_better"] is True and line["config"]["workload"] == "add"
+    base = line["cpu_baseline"]
+    assert base["kind"] == "reference" and base["cores"] >= 1 and base["value"] == line["value"]
+    assert "worker processes" in base["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
