@@ -331,16 +331,23 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
     SMALL_PROGRAM_TILE = 2048
 
     def _small_program(self):
-        """Programs without tensor-core work whose tiles have at most 2048
-        elements run with 64 threads: more programs resident per SM and
-        shorter CTA-wide reductions (measured best for row reductions)."""
+        """Programs without tensor-core work that reduce across threads and
+        whose tiles have at most 2048 elements run with 64 threads: more
+        programs resident per SM and shorter CTA-wide reductions (measured
+        best for row reductions: row softmax 8192x1000).  Element-wise
+        programs keep 32 * num_warps threads: the vector add over 2^20 f32
+        takes 2.48 us per launch with 128 threads per 1024-element program
+        against 2.57 us with 64 (more loads in flight per SM)."""
         if self.dot_rows or self.T != 128:
             return False
         ok = [True]
+        reduces = [False]
 
         def visit(node):
             if isinstance(node, (T_.TDot, T_.TAtomicAdd)):
                 ok[0] = False
+            if isinstance(node, T_.TReduce):
+                reduces[0] = True
             vt = getattr(node, "vt", None)
             if isinstance(vt, (TY.BlockT, TY.MaskT)):
                 try:
@@ -360,7 +367,7 @@ class KernelEmitter(FusedContractionMixin, WarpSpecMixin, AsyncLoopMixin, MmaMix
                             visit(x)
         for st in self.tk.body:
             visit(st)
-        return ok[0]
+        return ok[0] and reduces[0]
 
     def _scan_dots(self, stmts):
         """Row counts of dot results: 2-D tiles with that many rows default to
