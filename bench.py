@@ -640,12 +640,16 @@ def _e2e(case, args, world, rank, device):
         for e, st in ((in_free[b], s_comp), (out_free[b], s_out)):
             e.record(st)
 
+    # each set's copy views (destination, source), sliced once
+    in_copies = [[(d[rows], p[rows]) for p, d, rows in zip(pinned, dev_in[b], in_rows)] for b in range(2)]
+    out_copies = [(host_out[b][r0:r1], outs[b][r0:r1]) for b in range(2)]
+
     def step(i):
         b = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(in_free[b])
-            for p, d, rows in zip(pinned, dev_in[b], in_rows):
-                d[rows].copy_(p[rows], non_blocking=True)
+            for d, p in in_copies[b]:
+                d.copy_(p, non_blocking=True)
             in_ready[b].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_ready[b])
@@ -656,7 +660,7 @@ def _e2e(case, args, world, rank, device):
             out_ready[b].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(out_ready[b])
-            host_out[b][r0:r1].copy_(outs[b][r0:r1], non_blocking=True)
+            out_copies[b][0].copy_(out_copies[b][1], non_blocking=True)
             out_free[b].record(s_out)
 
     for i in range(2):
@@ -667,8 +671,10 @@ def _e2e(case, args, world, rank, device):
     # device time from the first copy-in to the last copy-out, max over ranks
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s_in)
+    t_host = time.perf_counter()
     for i in range(steps):
         step(i)
+    t_host = time.perf_counter() - t_host
     s_out.wait_stream(s_in)
     s_out.wait_stream(s_comp)
     e1.record(s_out)
@@ -683,6 +689,10 @@ def _e2e(case, args, world, rank, device):
     d2h = host_out[0][r0:r1].numel() * host_out[0].element_size() * world
     return {"value": round(case.units_per_rank * world / dt / scale, 3), "unit": unit,
             "ms_per_step": round(dt * 1e3, 3), "steps": steps,
+            # host time to issue one step (the kernel[grid] call, the copies
+            # and the stream events); a step cannot take less on the device
+            # once the host is the slower side
+            "host_ms_per_step": round(t_host * 1e3 / steps, 3),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "pipelining": "two buffer sets, copy-in / compute / copy-out streams"
                           + ("; each rank copies its own rows, bytes summed over ranks" if world > 1 else "")}
