@@ -103,6 +103,29 @@ def test_build_cli_emits_the_launch_time_tensor_core_plan(tmp_path):
     assert "tila::tma_load_2d(" in cu and "tila::mma_f16_ss(" in cu
 
 
+@pytest.mark.parametrize("example,consts", [
+    ("add_kernel.py", ["BLOCK=1024"]),
+    ("softmax.py", ["BN=1024"]),
+    ("matmul.py", ["BM=128", "BN=128", "BK=64"]),
+    ("fused_attention.py", ["CAUSAL=0", "BM=128", "BN=128", "BD=128"]),
+    ("fused_attention.py", ["CAUSAL=1", "BM=128", "BN=128", "BD=128"]),
+    ("self_attention.py", ["BM=128", "BN=128", "BD=64"]),
+])
+def test_every_reference_example_builds_to_an_sm100a_cubin(tmp_path, example, consts):
+    """Each Tila kernel the reference ships in examples/ (the benchmarked
+    configurations) generates CUDA that NVRTC compiles for sm_100a, with no
+    GPU present: a code-generation regression fails here before any launch."""
+    from tila_b200._reference import reference_tree
+    from tila_b200.__main__ import main
+    src = reference_tree() / "examples" / example
+    args = ["build", str(src), "-o", str(tmp_path), "--cubin"]
+    for c in consts:
+        args += ["--const", c]
+    assert main(args) == 0
+    cubins = list(tmp_path.glob("*.cubin"))
+    assert cubins and all(c.stat().st_size > 0 for c in cubins)
+
+
 def test_repeated_signature_key_follows_every_tila_switch(monkeypatch):
     """The repeated-signature path keys on every TILA_* variable (TILA_SAFETY,
     TILA_RACE_MAX_PAIRS and TILA_PROOF_* included): flipping one makes the
